@@ -1,0 +1,403 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 chunk-causal cached attention (BASELINE config 2 at N = 1).
+
+One step = one ``causal_attention_with_cache_mp`` call of a 4-frame chunk (4 x 1560
+image tokens + 1 text token, 24 heads x 128) against a 16-frame E4M3 KV cache
+(24,960 tokens) with frame-level block-causal masking, including the quantise-on-write
+append of the chunk into the cache.  Metric: attention TFLOP/s, FLOPs = 4*H*D*(visible
+query-key pairs) = 2.213 TFLOP per step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 (launched with torchrun, one rank per GPU): Ulysses sequence parallelism over the
+same global chunk (strong scaling): every rank holds 6240/N image tokens and 24/N heads
+of the head-sharded cache; Q/K/V and O cross NVLink through NCCL all_to_all_single.
+
+``--impl reference`` times the reference's CPU path (restated in oracle/: decode the
+INT8-style history, append the chunk, torch.cat, one SDPA call with the mask) on the
+host cores, on a sample of the heads; it prints the same metric and config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+H_TOTAL, D, T = 24, 128, 1560
+HIST_FRAMES, CHUNK_FRAMES, TXT = 16, 4, 1
+METRIC = "chunk-causal attn TFLOP/s (config 2: 4-frame chunk vs 16-frame FP8 KV cache, frame-causal)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def load_traffic():
+    p = REPO / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for name, val in zip(names, r[5:9]):
+                    if val.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    import torch.distributed as dist
+    if n_gpus <= 1:
+        return 0, 1, 0
+    import datetime
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def build_problem(rank, world, device):
+    """Global chunk of config 2 split for Ulysses SP over `world` ranks."""
+    from hy_nomas_b200 import kv_cache as kvc
+    from hy_nomas_b200.synthetic import make_generator, seeded_kv
+    Lh = HIST_FRAMES * T
+    Li = CHUNK_FRAMES * T
+    Hl = H_TOTAL // world
+    gen = make_generator(1236 + rank, device=device)
+    # head-sharded cache: this rank's heads for the whole history (+ room for the chunk)
+    cap = Lh + Li + TXT
+    cache = kvc.make_fp8_kv_block(1, cap, Hl, D, device=device)
+    with torch.no_grad():
+        hk = seeded_kv((1, Lh, Hl, D), gen, device=device)
+        hv = seeded_kv((1, Lh, Hl, D), gen, device=device)
+        kvc.quantize_kv_pair_into(cache, hk, hv, 0)
+        del hk, hv
+    Ls = Li // world
+    img = [seeded_kv((1, Ls, H_TOTAL, D), gen, device=device) for _ in range(3)]
+    txt = [seeded_kv((1, TXT, H_TOTAL, D), gen, device=device) for _ in range(3)]
+    cache_mask = torch.zeros(1, cap, dtype=torch.bool, device=device)
+    cache_mask[:, :Lh] = True
+    return dict(cache=cache, img=img, txt=txt, cache_mask=cache_mask, Lh=Lh, Li=Li, Ls=Ls, Hl=Hl)
+
+
+def run_b200(args):
+    from hy_nomas_b200 import _lib
+    from hy_nomas_b200 import attention as hatt
+    from hy_nomas_b200 import parallel_states as ps
+    from hy_nomas_b200.flops import attention_flops
+    import torch.distributed as dist
+
+    rank, world, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        ps.initialize_sequence_parallel_group()
+    os.environ["HYB_ASSUME_FINITE_KV"] = "1"   # validation stays on the device (status word)
+    prob = build_problem(rank, world, device)
+    Lh, Li, Ls, Hl = prob["Lh"], prob["Li"], prob["Ls"], prob["Hl"]
+    cache, cmask = prob["cache"], prob["cache_mask"]
+    img, txt = prob["img"], prob["txt"]
+    flops_total = attention_flops(Lh, Li, TXT, H_TOTAL, D, True, T)
+    stream = torch.cuda.current_stream(device)
+
+    def step(q_img, k_img, v_img, q_txt, k_txt, v_txt):
+        with torch.no_grad():
+            return hatt.causal_attention_with_cache_mp(
+                (q_img, q_txt), (k_img, k_txt), (v_img, v_txt), cache, cache_valid_len=Lh,
+                attn_mode="flash3", update_cache=True, cache_txt=True, cache_mask=cmask,
+                tokens_per_frame=T, seg_ar_attention_backend="b200", chunk_causal_frames=1)
+
+    for _ in range(args.warmup):
+        step(*img, *txt)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(*img, *txt)
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = tt.item()
+    _lib.check_device_status(device)
+    value = flops_total / (ms * 1e-3) / 1e12
+
+    # ---- end-to-end through the public API with pinned host buffers
+    host_in = [t.cpu().pin_memory() for t in (*img, *txt)]
+    host_out_img = torch.empty((1, Ls, H_TOTAL * D), dtype=torch.bfloat16).pin_memory()
+    host_out_txt = torch.empty((1, TXT, H_TOTAL * D), dtype=torch.bfloat16).pin_memory()
+    dev_in = [torch.empty_like(t, device=device) for t in host_in]
+
+    def e2e_step():
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+        o_img, o_txt = step(*dev_in)
+        host_out_img.copy_(o_img, non_blocking=True)
+        host_out_txt.copy_(o_txt, non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    ems = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ems], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ems = tt.item()
+    h2d = sum(t.numel() * t.element_size() for t in host_in) * world
+    d2h = (host_out_img.numel() + host_out_txt.numel()) * 2 * world
+
+    # ---- dominant kernel alone: the tcgen05 attention launch over the staged buffers
+    kern = time_attention_kernel(prob, device, args.steps)
+    peak_bf16, peak_hbm, peak_src = load_peaks()
+    local_flops = attention_flops(Lh, Li, TXT, Hl, D, True, T)
+    achieved = local_flops / (kern["ms"] * 1e-3) / 1e12
+    traffic = load_traffic().get("attn_fwd_config2_bytes_per_launch")
+    if traffic is not None and world > 1:
+        traffic = traffic * Hl / H_TOTAL
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_heads, reps=2)
+
+    if world > 1:
+        from hy_nomas_b200 import parallel_states as ps2
+        ps2.destroy_sequence_parallel_group()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "bf16 MMA / fp32 softmax; e4m3 KV cache", "data": "synthetic (seeded N(0,1), 4 outlier channels/head x8)",
+        "config": {"workload": "config 2: 1x B200 single block (N>1: Ulysses SP over the same chunk)",
+                   "heads": H_TOTAL, "head_dim": D, "history_tokens": Lh, "chunk_image_tokens": Li,
+                   "text_tokens": TXT, "tokens_per_frame": T, "mask": "frame-level block-causal (G=1)",
+                   "kv_cache": "fp8_e4m3 per-token-per-head scale", "append": "quantise-on-write of the chunk each step",
+                   "parallelism": f"ulysses_sp{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (153 MB FP8 history + 115 MB bf16 chunk per step)",
+                   "tflop_per_step": round(flops_total / 1e12, 4)},
+        "gpu_launches": 5 * args.steps * (1 if world == 1 else 1),
+        "e2e": {"value": round(flops_total / (ems * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "ms_per_step": round(ems, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_bf16, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak_bf16, 4), "traffic": traffic,
+                     "kernel": "attn_fwd_kernel (tcgen05 kind::f16, bf16 operands)",
+                     "kernel_ms": round(kern["ms"], 4), "peak_source": f"{peak_src} bf16 dense (cuBLAS)",
+                     "algorithmic_unit": "4*H*D FLOP per visible (query, key) pair"},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def time_attention_kernel(prob, device, iters):
+    """CUDA-event time of the attention kernel launch alone on the staged workspace."""
+    from hy_nomas_b200 import _lib
+    from hy_nomas_b200 import attention as hatt
+    Lh, Li, Ls, Hl = prob["Lh"], prob["Li"], prob["Ls"], prob["Hl"]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99)
+    from hy_nomas_b200.synthetic import seeded_kv
+    img = [seeded_kv((1, Li, Hl, D), gen, device=device) for _ in range(3)]
+    txt = [seeded_kv((1, TXT, Hl, D), gen, device=device) for _ in range(3)]
+    ws = hatt.Workspace()
+    hatt.cached_attention_local(*img, *txt, prob["cache"], Lh, group_tokens=T, workspace=ws)
+    args = ws.attn_args
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(device)
+    for _ in range(3):
+        _lib.check(lib.hyb_attn_fwd(args, stream.cuda_stream), "attention")
+    torch.cuda.synchronize(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        _lib.check(lib.hyb_attn_fwd(args, stream.cuda_stream), "attention")
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    return {"ms": e0.elapsed_time(e1) / iters}
+
+
+def cpu_problem(heads, seed=1236):
+    from hy_nomas_b200.synthetic import make_generator, seeded_kv
+    from oracle import quant as oq
+    gen = make_generator(seed)
+    Lh, Li = HIST_FRAMES * T, CHUNK_FRAMES * T
+    hk = seeded_kv((1, Lh, heads, D), gen)
+    hv = seeded_kv((1, Lh, heads, D), gen)
+    ck, sk = oq.quantize_e4m3(hk)
+    cv, sv = oq.quantize_e4m3(hv)
+    cur = [seeded_kv((1, L, heads, D), gen) for L in (Li, TXT) for _ in range(3)]
+    return dict(ck=ck, sk=sk, cv=cv, sv=sv, cur=cur, Lh=Lh, Li=Li)
+
+
+def cpu_step(p):
+    """The reference CPU path for one chunk: decode history, quantise-on-write the chunk,
+    compose and run SDPA with the frame-causal mask (oracle restatement)."""
+    from oracle import attention as oatt
+    from oracle import quant as oq
+    hk = oq.dequantize(p["ck"], p["sk"])
+    hv = oq.dequantize(p["cv"], p["sv"])
+    cur = p["cur"]
+    oq.quantize_e4m3(torch.cat([cur[1], cur[4]], 1))
+    oq.quantize_e4m3(torch.cat([cur[2], cur[5]], 1))
+    return oatt.reference_sdpa_path(*cur, hk, hv, group_tokens=T)
+
+
+def cpu_baseline(heads, reps=2):
+    from hy_nomas_b200.flops import attention_flops
+    torch.set_num_threads(os.cpu_count() or 1)
+    p = cpu_problem(heads)
+    cpu_step(p)
+    t = time.perf_counter()
+    for _ in range(reps):
+        cpu_step(p)
+    dt = (time.perf_counter() - t) / reps
+    fl = attention_flops(p["Lh"], p["Li"], TXT, heads, D, True, T)
+    return {"value": round(fl / dt / 1e12, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"config 2 with {heads} of {H_TOTAL} heads per step (decode + append + SDPA), "
+                      f"{reps} reps, {dt:.2f} s per step"}
+
+
+def run_reference(args):
+    if args.gpus > 1:
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+    from hy_nomas_b200.flops import attention_flops
+    torch.set_num_threads(os.cpu_count() or 1)
+    heads = args.cpu_heads
+    p = cpu_problem(heads)
+    for _ in range(args.warmup):
+        cpu_step(p)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(p)
+    dt = (time.perf_counter() - t) / args.steps
+    fl = attention_flops(p["Lh"], p["Li"], TXT, heads, D, True, T)
+    value = fl / dt / 1e12
+    sample = f"config 2 with {heads} of {H_TOTAL} heads per step (decode + append + SDPA)"
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (CPU SDPA)",
+        "data": "synthetic (seeded N(0,1), 4 outlier channels/head x8)", "impl": "reference",
+        "config": {"workload": "config 2: 1x B200 single block", "heads_sampled": heads,
+                   "history_tokens": p["Lh"], "chunk_image_tokens": p["Li"], "tokens_per_frame": T},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

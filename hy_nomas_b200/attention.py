@@ -1,0 +1,365 @@
+"""Drop-in ``causal_attention_with_cache_mp`` on the sm_100a library.
+
+Same signature, argument meaning, mutation contract and exceptions as the reference
+(``hymm/models/dit/nomas_cpt.py:335-884``), including the reactor's older positional
+order (``reactor/hy_nomas_cache.py:192-209``, which lacks ``sp_metadata`` and
+``attention_metadata``).  One call on one rank:
+
+1. SP in (Ulysses): packed Q|K|V all-to-all seq->head, text heads sliced
+   (nomas_cpt.py:410-429).
+2. Cache write when ``update_cache``: quantise-on-write (INT8 / E4M3) or bf16 copy at
+   token offset ``cache_valid_len``; ``cache_mask`` updated in place (:592-606).
+3. Attention over [visible history | current image | current text] (:608-685) by
+   ``hyb_cached_attention``: history decoded from its codes inside the staging pass,
+   masked keys excluded, masked text queries produce zero rows (flash3 semantics,
+   :786-829).  ``chunk_causal_frames`` (keyword-only extension) restricts image queries
+   to image keys of the same or earlier G-frame blocks, the chunk-causal ranges of
+   ``attention/magi_attn.py:290-309``; 0 keeps the reference's bidirectional chunk.
+4. SP out: O head->seq all-to-all, text all-gather over heads (:864-872); cast to the
+   input dtypes and reshape to [B, L, H*D] (:874-884).
+
+Modes the reference routes elsewhere and this build does not implement raise:
+``qvg`` storage, ``sparse_context``, intra-segment action masks and SWA commits.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import torch
+
+from . import _lib
+from . import kv_cache as kvc
+from . import parallel_states as _ps
+
+_BACKENDS = ("magi", "flex", "b200")
+
+# Parallel-state provider: (get_sequence_parallel_state, nccl_info).  install.install()
+# points this at the reference's hymm.distributed.parallel_states.
+_STATE = {"get_state": _ps.get_sequence_parallel_state, "info": _ps.nccl_info}
+
+stats = {"calls": 0, "writes": 0}
+
+
+def set_parallel_state_provider(get_state, info) -> None:
+    _STATE["get_state"] = get_state
+    _STATE["info"] = info
+
+
+def _assume_finite() -> bool:
+    return os.environ.get("HYB_ASSUME_FINITE_KV", "0") == "1"
+
+
+def _new_out(B, L, H, D, device):
+    return torch.empty((B, L, H, D), dtype=torch.bfloat16, device=device)
+
+
+def _align256(x: int) -> int:
+    return (x + 255) & ~255
+
+
+def workspace_layout(B, H, Lh, Li, Lt, attend_txt, D=128):
+    """Byte offsets of the staging workspace (mirrors layout_for in csrc/hyb_attn.cu):
+    q [B, H, Lq, D] bf16 | k [B, H, Lk, D] | v | key bitmap [B, kwords] | query bitmap."""
+    Lq = Li + Lt
+    Lk = Lh + Li + (Lt if attend_txt else 0)
+    kwords = -(-Lk // 128) * 4
+    qwords = -(-Lq // 32)
+    off = 0
+    lay = {"Lq": Lq, "Lk": Lk, "kwords": kwords, "qwords": qwords, "q": off}
+    off = _align256(off + B * H * Lq * D * 2)
+    lay["k"] = off
+    off = _align256(off + B * H * Lk * D * 2)
+    lay["v"] = off
+    off = _align256(off + B * H * Lk * D * 2)
+    lay["kbits"] = off
+    off = _align256(off + B * kwords * 4)
+    lay["qbits"] = off
+    off = _align256(off + B * max(qwords, 1) * 4)
+    lay["total"] = off
+    return lay
+
+
+class Workspace:
+    """Reusable staging buffer.  After a call, ``attn_args`` re-launches the attention
+    kernel alone on the staged tensors (``hyb_attn_fwd``), e.g. to time it."""
+
+    def __init__(self):
+        self.buf = None
+        self.attn_args = None
+        self.keep = ()
+
+    def get(self, nbytes, device):
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+            self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        return self.buf
+
+
+def cached_attention_local(
+    img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, cache_valid_len, *,
+    history_mask=None, text_mask=None, attend_txt=True, group_tokens=0,
+    softmax_scale=None, out_img=None, out_img_strides=None, out_txt=None, lse=None,
+    hist_rows=None, workspace=None,
+):
+    """Single-rank attention of the current chunk over [history | image | text].
+
+    Inputs are bf16 [B, L, H, D] (any strides with unit stride on D).  History is
+    ``kv_cache`` rows [0, cache_valid_len) in its storage format; ``history_mask`` is
+    bool [B or 1, >= cache_valid_len], indexed by cache row.  ``hist_rows`` (int32
+    [cache_valid_len] on the device) maps composed history position -> cache row (a
+    sink + sliding-window ring); None means rows [0, cache_valid_len).  Returns ``(out_img, out_txt)`` bf16
+    [B, L, H, D]; ``out_img`` may be supplied pre-allocated with custom element
+    strides ``(sb, st, sh)`` or ``(sb, st, sh, seg, sseg)`` where image row t lands at
+    ``(t // seg) * sseg + (t % seg) * st`` (e.g. the Ulysses O send buffer).
+    """
+    lib = _lib.load()
+    B, Li, H, D = img_q.shape
+    Lt = txt_q.shape[1]
+    dev = img_q.device
+    fmt_name = kvc.cache_format(kv_cache)
+    if fmt_name == "none":
+        hk, hv = kv_cache["k"], kv_cache["v"]
+        if hk.dtype != torch.bfloat16:
+            raise RuntimeError(f"b200 cached attention requires a bf16 or quantised cache, got {hk.dtype}")
+        hist_k, hist_v = _lib.bf16_view(hk), _lib.bf16_view(hv)
+    elif fmt_name in ("int8", kvc.FP8_FORMAT):
+        code = _lib.HYB_FMT_INT8 if fmt_name == "int8" else _lib.HYB_FMT_E4M3
+        hist_k = _lib.coded_view(kv_cache["k"], kv_cache["k_scale"], code)
+        hist_v = _lib.coded_view(kv_cache["v"], kv_cache["v_scale"], code)
+    else:
+        raise ValueError(f"b200 cached attention does not support {fmt_name!r} storage")
+    cache_batch = kv_cache["k"].shape[0]
+    if out_img is None:
+        out_img = _new_out(B, Li, H, D, dev)
+    if out_txt is None:
+        out_txt = _new_out(B, Lt, H, D, dev)
+    oi = tuple(out_img_strides) if out_img_strides is not None else tuple(out_img.stride()[:3])
+    if len(oi) == 3:
+        oi = oi + (0, 0)
+    ws_bytes = lib.hyb_cached_attention_workspace_bytes(B, H, D, cache_valid_len, Li, Lt, int(attend_txt))
+    if ws_bytes < 0:
+        raise RuntimeError("hyb200: unsupported sizes for cached attention (head_dim must be 128)")
+    ws_obj = workspace if isinstance(workspace, Workspace) else None
+    workspace = ws_obj.get(int(ws_bytes), dev) if ws_obj is not None else \
+        torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=dev)
+    if history_mask is not None:
+        history_mask = history_mask.to(torch.bool)
+        if history_mask.stride(-1) != 1:
+            history_mask = history_mask.contiguous()
+    if text_mask is not None:
+        text_mask = text_mask.to(torch.bool).contiguous()
+    empty = _lib.Tensor4()
+    args = _lib.CachedAttnArgs()
+    args.abi_version = _lib.HYB_ABI_VERSION
+    args.B, args.H, args.D = B, H, D
+    args.cache_batch = cache_batch
+    args.valid_len = cache_valid_len
+    args.img_len, args.txt_len = Li, Lt
+    args.attend_txt = int(bool(attend_txt))
+    args.group_tokens = int(group_tokens)
+    args.softmax_scale = float(softmax_scale) if softmax_scale else 0.0
+    args.hist_k, args.hist_v = hist_k, hist_v
+    args.img_q = _lib.bf16_view(img_q) if Li else empty
+    args.img_k = _lib.bf16_view(img_k) if Li else empty
+    args.img_v = _lib.bf16_view(img_v) if Li else empty
+    args.txt_q = _lib.bf16_view(txt_q) if Lt else empty
+    args.txt_k = _lib.bf16_view(txt_k) if Lt else empty
+    args.txt_v = _lib.bf16_view(txt_v) if Lt else empty
+    if hist_rows is not None:
+        if hist_rows.dtype != torch.int32 or hist_rows.numel() < cache_valid_len or not hist_rows.is_contiguous():
+            raise ValueError("hist_rows must be a contiguous int32 tensor with cache_valid_len entries")
+    args.hist_rows = _lib.ptr(hist_rows)
+    args.cache_mask = _lib.ptr(history_mask)
+    args.cache_mask_sb = history_mask.stride(0) if history_mask is not None else 0
+    args.text_mask = _lib.ptr(text_mask)
+    args.text_mask_sb = text_mask.stride(0) if text_mask is not None else 0
+    args.out_img = out_img.data_ptr()
+    args.oi_sb, args.oi_st, args.oi_sh, args.oi_seg, args.oi_sseg = oi
+    args.out_txt = out_txt.data_ptr()
+    args.ot_sb, args.ot_st, args.ot_sh = out_txt.stride()[:3]
+    args.lse = _lib.ptr(lse)
+    args.workspace = workspace.data_ptr()
+    args.workspace_bytes = workspace.numel()
+    args.dev_status = _lib.device_status(dev).data_ptr()
+    with torch.cuda.device(dev):
+        _lib.check(lib.hyb_cached_attention(args, _lib.stream_ptr(dev)), "cached attention")
+    if ws_obj is not None:
+        lay = workspace_layout(B, H, cache_valid_len, Li, Lt, attend_txt, D)
+        base = workspace.data_ptr()
+        at = _lib.AttnArgs()
+        at.abi_version = _lib.HYB_ABI_VERSION
+        at.B, at.H, at.D, at.Lq, at.Lk = B, H, D, lay["Lq"], lay["Lk"]
+        at.hist_len, at.img_len, at.group_tokens = cache_valid_len, Li, int(group_tokens)
+        at.softmax_scale = args.softmax_scale
+        at.q, at.k, at.v = base + lay["q"], base + lay["k"], base + lay["v"]
+        at.kbits, at.kwords = base + lay["kbits"], lay["kwords"]
+        at.qbits, at.qwords = base + lay["qbits"], lay["qwords"]
+        at.out_img = args.out_img
+        at.oi_sb, at.oi_st, at.oi_sh = oi[0], oi[1], oi[2]
+        at.oi_seg, at.oi_sseg = (oi[3], oi[4]) if oi[3] > 0 else (max(Li, 1), 0)
+        at.out_txt = args.out_txt
+        at.ot_sb, at.ot_st, at.ot_sh = args.ot_sb, args.ot_st, args.ot_sh
+        at.lse = args.lse
+        at.dev_status = args.dev_status
+        ws_obj.attn_args = at
+        ws_obj.keep = (out_img, out_txt, lse)
+    return out_img, out_txt
+
+
+def causal_attention_with_cache_mp(
+    q,
+    k,
+    v,
+    kv_cache,
+    cache_valid_len: int = 0,
+    attn_mode: Optional[str] = None,
+    text_mask: Optional[torch.Tensor] = None,
+    update_cache: bool = False,
+    cache_txt: bool = True,
+    cache_mask: Optional[torch.Tensor] = None,
+    intra_seg_txt_offsets=None,
+    intra_seg_vid_windows=None,
+    tokens_per_frame: int = 0,
+    seg_ar_attention_backend: str = "magi",
+    sparse_context=None,
+    sp_metadata=None,
+    attention_metadata=None,
+    *,
+    chunk_causal_frames: int = 0,
+):
+    """Multi-prompt causal attention with KV cache on B200 (see module docstring)."""
+    if seg_ar_attention_backend not in _BACKENDS:
+        raise ValueError("Invalid seg_ar_attention_backend")
+    if seg_ar_attention_backend == "flex" and torch.is_grad_enabled():
+        raise RuntimeError("Flex cached attention requires no-grad inference")
+    if sparse_context is not None:
+        raise NotImplementedError("b200 cached attention: sparse_context routing is not implemented")
+    if (cache_txt and intra_seg_vid_windows is not None and len(intra_seg_vid_windows) > 0
+            and intra_seg_txt_offsets is not None and any(o is not None for o in intra_seg_txt_offsets)):
+        raise NotImplementedError("b200 cached attention: intra-segment action masks are not implemented")
+    if "swa_capacity" in kv_cache and update_cache:
+        raise NotImplementedError("b200 cached attention: SWA commit is not implemented; use window.py")
+
+    get_state, info = _STATE["get_state"], _STATE["info"]
+    is_sp = bool(get_state())
+    sp_group = info.sp_group
+
+    img_q, txt_q = q
+    img_k, txt_k = k
+    img_v, txt_v = v
+    img_output_dtype = img_q.dtype
+    txt_output_dtype = txt_q.dtype
+
+    storage_format = kvc.cache_format(kv_cache)
+    if storage_format == "qvg":
+        raise ValueError("QVG requires single-slot dense Flex segment attention (not built for b200)")
+    compressed = storage_format in ("int8", kvc.FP8_FORMAT)
+    cache_shape, cache_device, cache_dtype = kvc.cache_geometry(kv_cache)
+    if kv_cache["k"].dtype != kv_cache["v"].dtype:
+        raise RuntimeError("KV cache K/V dtype mismatch")
+    if kv_cache["k"].device != kv_cache["v"].device:
+        raise RuntimeError("KV cache K/V device mismatch")
+    if (compressed or "swa_capacity" in kv_cache) and torch.is_grad_enabled():
+        raise ValueError("Compressed KV/SWA requires no-grad inference")
+    if img_q.device != cache_device or txt_q.device != cache_device:
+        raise RuntimeError(
+            "Current Q and KV cache must be on the same device: "
+            f"img_q={img_q.device}, txt_q={txt_q.device}, cache={cache_device}")
+    _lib.require_device(img_q)
+
+    from . import communications as comm
+
+    o_send = None
+    if is_sp:
+        if sp_metadata is None:
+            sp_metadata = comm.prepare_sp_communication(img_q.shape[1], img_q.shape[2], img_q.device, sp_group)
+        img_q, img_k, img_v = comm.all_to_all_qkv(
+            img_q, img_k, img_v, group=sp_group, sequence_lengths=sp_metadata.sequence_lengths)
+        if txt_q.shape[2] != img_q.shape[2]:
+            shard = img_q.shape[2]
+            start_h = info.rank_within_spgroup * shard
+            txt_q = txt_q[:, :, start_h:start_h + shard, :]
+            txt_k = txt_k[:, :, start_h:start_h + shard, :]
+            txt_v = txt_v[:, :, start_h:start_h + shard, :]
+
+    # Kernel dtype is bf16 for every storage format (cache dtype for a bf16 cache).
+    img_q, txt_q, img_k, txt_k, img_v, txt_v = (
+        x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+        for x in (img_q, txt_q, img_k, txt_k, img_v, txt_v))
+    if not compressed and cache_dtype != torch.bfloat16:
+        raise RuntimeError(f"b200 cached attention requires a bf16 cache, got {cache_dtype}")
+
+    B = img_q.shape[0]
+    img_len = img_k.shape[1]
+    txt_len = txt_k.shape[1]
+    H, D = img_q.shape[2], img_q.shape[3]
+    if text_mask is not None:
+        cur_txt_mask = text_mask.bool()
+    else:
+        cur_txt_mask = torch.ones(B, txt_len, device=img_k.device, dtype=torch.bool)
+
+    history_batch = kv_cache["k"].shape[0]
+    if history_batch != B:
+        if update_cache:
+            raise ValueError(
+                "KV-cache batch mismatch during update: "
+                f"current={B}, cache={history_batch}. "
+                "Read-only history broadcasting is supported, cache writes are not.")
+        if history_batch != 1:
+            raise ValueError(
+                "KV-cache batch mismatch: "
+                f"current={B}, cache={history_batch}; only a single canonical "
+                "history slot can be broadcast.")
+    if cache_valid_len < 0 or cache_valid_len > cache_shape[1]:
+        raise ValueError("Invalid KV valid length")
+
+    # ---- cache write (validated before either payload is touched)
+    if update_cache:
+        cache_k = torch.cat([img_k, txt_k], dim=1) if cache_txt else img_k
+        cache_v = torch.cat([img_v, txt_v], dim=1) if cache_txt else img_v
+        write_tokens = cache_k.shape[1]
+        new_end = cache_valid_len + write_tokens
+        if new_end > cache_shape[1]:
+            raise ValueError("KV pair shape, capacity, dtype, or device mismatch")
+        if compressed:
+            kvc.quantize_kv_pair_into(kv_cache, cache_k.detach(), cache_v.detach(), cache_valid_len,
+                                      assume_finite=_assume_finite())
+        else:
+            kv_cache["k"][:, cache_valid_len:new_end] = cache_k.detach()
+            kv_cache["v"][:, cache_valid_len:new_end] = cache_v.detach()
+        if cache_mask is not None:
+            if cache_txt:
+                cache_mask[:, cache_valid_len:cache_valid_len + img_len] = True
+                cache_mask[:, cache_valid_len + img_len:new_end] = cur_txt_mask
+            else:
+                cache_mask[:, cache_valid_len:new_end] = True
+        stats["writes"] += 1
+
+    history_mask = cache_mask[:, :cache_valid_len] if (cache_mask is not None and cache_valid_len > 0) else None
+    attend_txt = bool(cache_txt or update_cache)
+    group_tokens = int(chunk_causal_frames) * int(tokens_per_frame) if chunk_causal_frames else 0
+
+    out_img_strides = None
+    if is_sp:
+        o_send, out_img_strides = comm.o_send_buffer(
+            B, sp_metadata.sequence_lengths, H, D, img_q.device)
+    out_img, out_txt = cached_attention_local(
+        img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, cache_valid_len,
+        history_mask=history_mask, text_mask=cur_txt_mask, attend_txt=attend_txt,
+        group_tokens=group_tokens, out_img=o_send, out_img_strides=out_img_strides)
+    stats["calls"] += 1
+
+    if is_sp:
+        img_attn = comm.all_to_all_o(o_send, group=sp_group, batch=B,
+                                     sequence_lengths=sp_metadata.sequence_lengths, heads_local=H, dim=D)
+        txt_attn = comm.all_gather(out_txt, dim=2, group=sp_group, sizes=sp_metadata.head_sizes)
+    else:
+        img_attn, txt_attn = out_img, out_txt
+
+    if img_attn.dtype != img_output_dtype:
+        img_attn = img_attn.to(dtype=img_output_dtype)
+    if txt_attn.dtype != txt_output_dtype:
+        txt_attn = txt_attn.to(dtype=txt_output_dtype)
+    img_attn = img_attn.reshape(img_attn.size(0), img_attn.size(1), -1)
+    txt_attn = txt_attn.reshape(txt_attn.size(0), txt_attn.size(1), -1)
+    return img_attn, txt_attn

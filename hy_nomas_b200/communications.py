@@ -1,0 +1,218 @@
+"""Ulysses sequence-parallel exchange for the cached attention (B200 / NCCL).
+
+Mirrors ``hymm/distributed/communications.py`` (``prepare_sp_communication`` :24-43,
+``all_to_all_4D`` :260-267 / ``_all_to_all_4D`` :66-200, ``all_to_all_qkv`` :270-280,
+``all_gather`` :410-421) with the same names, layouts and errors.  The difference is
+the data movement around the collectives: the reference builds each send buffer with
+cat + reshape + transpose + contiguous and unpacks with more copies; here one pack
+kernel writes the send buffer directly from the (strided) inputs, the Q/K/V receive
+buffer is consumed in place through strided views, and the cached attention writes
+its image output straight into the O send buffer (``o_send_buffer``), so the head->
+sequence direction costs one all_to_all_single plus one unpack kernel.
+
+The exchange itself is ``torch.distributed.all_to_all_single`` (NCCL over NVLink on
+B200).  ``exchange`` is the bare collective step; the pack / unpack kernels are CUDA
+only, and the CPU process-group tests drive ``exchange`` with host-built buffers.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+
+@dataclass(frozen=True)
+class SPCommunicationMetadata:
+    """Host-side sizes shared by all attention layers in one model forward."""
+
+    sequence_lengths: Tuple[int, ...]
+    head_sizes: Tuple[int, ...]
+
+
+def prepare_sp_communication(local_sequence_length, heads, device, group):
+    """Exchange sequence/head sizes once, before the layer loop (one host sync)."""
+    world_size = dist.get_world_size(group)
+    local = torch.tensor([[local_sequence_length, heads]], dtype=torch.int64, device=device)
+    if world_size > 1:
+        sizes = torch.empty((world_size, 2), dtype=torch.int64, device=device)
+        dist.all_gather_into_tensor(sizes, local, group=group)
+    else:
+        sizes = local
+    rows = sizes.tolist()
+    sequence_lengths = tuple(row[0] for row in rows)
+    all_heads = tuple(row[1] for row in rows)
+    if any(length < 0 for length in sequence_lengths):
+        raise ValueError("SP sequence lengths must be nonnegative")
+    if len(set(all_heads)) != 1 or heads <= 0 or heads % world_size:
+        raise ValueError("SP ranks require identical head counts divisible by SP size")
+    return SPCommunicationMetadata(sequence_lengths, (heads // world_size,) * world_size)
+
+
+def _validate_sizes(sizes, world_size):
+    sizes = tuple(sizes)
+    if len(sizes) != world_size or any(type(size) is not int or size < 0 for size in sizes):
+        raise ValueError("Expected one nonnegative Python integer size per process-group rank")
+    return sizes
+
+
+def exchange(send: torch.Tensor, group) -> torch.Tensor:
+    """The collective step: equal-split all_to_all_single along dim 0 (P blocks)."""
+    world = dist.get_world_size(group)
+    if send.shape[0] != world:
+        raise ValueError("send buffer's leading dimension must equal the SP world size")
+    if world == 1:
+        return send
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    return recv
+
+
+def _legacy_lengths(length, world_size):
+    chunk = (length + world_size - 1) // world_size
+    return tuple(min(chunk, max(0, length - rank * chunk)) for rank in range(world_size))
+
+
+def all_to_all_qkv(q, k, v, group, sequence_lengths=None):
+    """Sequence-sharded [B, Ls, H, D] Q/K/V -> head-sharded [B, L, H/P, D], one collective.
+
+    Returns strided views into the receive buffer when every rank holds the same number
+    of tokens (the common case), compact tensors otherwise."""
+    if any(t.shape != q.shape or t.dtype != q.dtype or t.device != q.device for t in (k, v)):
+        raise ValueError("Fused QKV all-to-all requires identical shapes, dtypes and devices")
+    if q.ndim != 4 or q.shape[0] == 0:
+        raise ValueError("Fused QKV all-to-all requires nonempty-batch [B,S,H,D] tensors")
+    return _seq_to_heads((q, k, v), group, sequence_lengths)
+
+
+def _seq_to_heads(tensors, group, sequence_lengths):
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    x0 = tensors[0]
+    B, Ls, H, D = x0.shape
+    if sequence_lengths is None:
+        sizes = torch.empty(world, dtype=torch.int64, device=x0.device)
+        dist.all_gather_into_tensor(sizes, torch.tensor([Ls], dtype=torch.int64, device=x0.device), group=group)
+        sequence_lengths = tuple(sizes.tolist())
+    sequence_lengths = _validate_sizes(sequence_lengths, world)
+    if Ls != sequence_lengths[rank]:
+        raise ValueError("Local sequence length does not match SP metadata")
+    if H % world:
+        raise ValueError(f"Invalid Head size: {H}, which should be divisible by spsize {world}")
+    Hp = H // world
+    Ls_max = max(sequence_lengths)
+    total = sum(sequence_lengths)
+    n = len(tensors)
+    if total == 0:
+        return tuple(x0.new_empty((B, 0, Hp, D)) for _ in tensors)
+    tensors = tuple(t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16) for t in tensors)
+    send = torch.empty((world, Ls_max, n * B, Hp, D), dtype=torch.bfloat16, device=x0.device)
+    lib = _lib.load()
+    views = [_lib.bf16_view(t) for t in tensors]
+    with torch.cuda.device(x0.device):
+        _lib.check(lib.hyb_ulysses_pack_qkv(
+            world, B, Ls, Ls_max, H, D, views[0],
+            views[1] if n == 3 else None, views[2] if n == 3 else None,
+            send.data_ptr(), _lib.stream_ptr(x0.device)), "ulysses pack")
+    recv = exchange(send, group)                      # [P(src), Ls_max, nB, Hp, D]
+    if any(length != Ls_max for length in sequence_lengths):
+        recv = torch.cat([recv[src, :length] for src, length in enumerate(sequence_lengths)], dim=0)
+    else:
+        recv = recv.reshape(world * Ls_max, n * B, Hp, D)
+    full = recv.permute(1, 0, 2, 3)                   # [nB, L, Hp, D] strided view
+    out = tuple(full[i * B:(i + 1) * B] for i in range(n))
+    return tuple(t if t.dtype == x.dtype else t.to(x.dtype) for t, x in zip(out, tensors))
+
+
+def o_send_buffer(B, sequence_lengths, Hp, D, device):
+    """Allocate the head->sequence send buffer [P, Hp, Ls_max, B, D] and the element strides
+    (sb, st, sh, seg, sseg) with which the attention epilogue writes image row t of head h
+    straight into it.  Needs equal per-rank lengths (else returns a plain [B, L, Hp, D]
+    buffer that ``all_to_all_o`` packs with a kernel)."""
+    P = len(sequence_lengths)
+    Ls_max = max(sequence_lengths) if sequence_lengths else 0
+    if all(length == Ls_max for length in sequence_lengths) and Ls_max > 0:
+        buf = torch.empty((P, Hp, Ls_max, B, D), dtype=torch.bfloat16, device=device)
+        # offset(b, t, h) = ((t // Ls) * Hp + h) * Ls * B * D + (t % Ls) * B * D + b * D
+        strides = (D, B * D, Ls_max * B * D, Ls_max, Hp * Ls_max * B * D)
+        return buf, strides
+    total = sum(sequence_lengths)
+    buf = torch.empty((B, total, Hp, D), dtype=torch.bfloat16, device=device)
+    return buf, None
+
+
+def all_to_all_o(send, group, batch, sequence_lengths, heads_local, dim):
+    """Head-sharded attention output -> sequence-sharded [B, Ls, H, D]."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    sequence_lengths = _validate_sizes(sequence_lengths, world)
+    Ls_max = max(sequence_lengths)
+    lib = _lib.load()
+    dev = send.device
+    if send.ndim == 4:  # [B, L, Hp, D]: pack into the send layout first
+        packed = torch.empty((world, heads_local, Ls_max, batch, dim), dtype=torch.bfloat16, device=dev)
+        lens = (ctypes.c_int32 * world)(*sequence_lengths)
+        with torch.cuda.device(dev):
+            _lib.check(lib.hyb_ulysses_pack_o(world, batch, lens, Ls_max, heads_local, dim,
+                                              _lib.bf16_view(send), packed.data_ptr(),
+                                              _lib.stream_ptr(dev)), "ulysses pack o")
+        send = packed
+    recv = exchange(send, group)                      # [P(src), Hp, Ls_max, B, D]
+    Ls = sequence_lengths[rank]
+    H = heads_local * world
+    out = torch.empty((batch, Ls, H, dim), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(lib.hyb_ulysses_unpack_o(world, batch, Ls, Ls_max, H, dim, recv.data_ptr(), out.data_ptr(),
+                                            *out.stride()[:3], _lib.stream_ptr(dev)), "ulysses unpack")
+    return out
+
+
+def all_to_all_4D(input_: torch.Tensor, group, scatter_dim: int = 2, gather_dim: int = 1,
+                  sequence_lengths=None):
+    """Generic 4-D all-to-all (forward only), same layouts as the reference."""
+    if input_.dim() != 4:
+        raise ValueError(f"input must be 4D tensor, got {input_.dim()} and shape {input_.shape}")
+    world = dist.get_world_size(group)
+    if scatter_dim == 2 and gather_dim == 1:
+        return _seq_to_heads((input_,), group, sequence_lengths)[0]
+    if scatter_dim == 1 and gather_dim == 2:
+        B, L, Hp, D = input_.shape
+        if sequence_lengths is None:
+            sequence_lengths = _legacy_lengths(L, world)
+        sequence_lengths = _validate_sizes(sequence_lengths, world)
+        if L != sum(sequence_lengths):
+            raise ValueError("Full sequence length does not match SP metadata")
+        x = input_ if input_.dtype == torch.bfloat16 else input_.to(torch.bfloat16)
+        out = all_to_all_o(x, group, B, sequence_lengths, Hp, D)
+        return out if out.dtype == input_.dtype else out.to(input_.dtype)
+    raise RuntimeError("scatter_idx must be 1 or 2 and gather_idx must be 1 or 2")
+
+
+def all_gather(input_: torch.Tensor, dim: int = 1, group=None, sizes=None):
+    """Concatenate every rank's tensor along ``dim`` (uneven sizes padded, as the reference)."""
+    dim = dim % input_.dim()
+    world = dist.get_world_size(group)
+    if sizes is None:
+        local = torch.tensor([input_.shape[dim]], dtype=torch.int64, device=input_.device)
+        all_sizes = torch.empty(world, dtype=torch.int64, device=input_.device)
+        dist.all_gather_into_tensor(all_sizes, local, group=group)
+        sizes = all_sizes.tolist()
+    sizes = _validate_sizes(sizes, world)
+    if input_.shape[dim] != sizes[dist.get_rank(group)]:
+        raise ValueError("Local gather size does not match supplied metadata")
+    if world == 1:
+        return input_.contiguous()
+    max_size = max(sizes)
+    x = input_.movedim(dim, 0)
+    if x.shape[0] < max_size:
+        pad = torch.zeros((max_size - x.shape[0], *x.shape[1:]), dtype=x.dtype, device=x.device)
+        x = torch.cat([x, pad], dim=0)
+    x = x.contiguous()
+    gathered = torch.empty((world, *x.shape), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(gathered, x, group=group)
+    parts = [gathered[r, :sizes[r]] for r in range(world)]
+    return torch.cat(parts, dim=0).movedim(0, dim).contiguous()

@@ -1,0 +1,871 @@
+// Chunk-causal cached attention for sm_100a.
+//
+//  * stage kernels: compose the key sequence [visible history | current image | current
+//    text] head-major in bf16 (history decoded from E4M3 / INT8 codes with its per-token
+//    per-head scale), the query sequence [image | text], and the key / query visibility
+//    bitmaps.  This replaces dequantize_kv + torch.cat + unpad of
+//    causal_attention_with_cache_mp (hymm/models/dit/nomas_cpt.py:520-531, :608-685,
+//    :807-817) and the compact_kv gather of reactor/hy_nomas_cache.py:48-73.
+//  * attention kernel: one CTA per (128-query tile, head, batch); a TMA producer warp,
+//    a single-thread tcgen05 MMA issuer, and one softmax/epilogue warpgroup.
+//    S = Q K^T and O += P V run on the tensor cores with fp32 accumulators in tensor
+//    memory (S double-buffered, 2 x 128 columns; O 128 columns); K/V tiles stream
+//    through a 2-stage shared-memory ring.  Online softmax with lazy rescaling (O is
+//    only rescaled when the running max grows by more than 2^8), frame-level
+//    block-causal masking with fully masked key tiles skipped, and key/query validity
+//    bitmaps for padded history and text.  The output is written at its final
+//    position (pad_tokens semantics: masked text queries produce zero rows).
+#include <limits.h>
+
+#include "hyb_common.cuh"
+
+namespace hyb {
+namespace {
+
+constexpr int kBM = 128;                    // query rows per tile
+constexpr int kBN = 128;                    // keys per tile
+constexpr int kHD = 128;                    // head dim
+constexpr int kStages = 2;                  // K/V shared-memory ring depth
+constexpr int kTileBytes = kBM * kHD * 2;   // one 128 x 128 bf16 tile
+constexpr int kHalfTile = kTileBytes / 2;   // one 64-column TMA box (128-byte rows)
+constexpr int kThreads = 192;               // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr uint32_t kTmemCols = 512;         // S0 [0,128) S1 [128,256) O [256,384)
+constexpr uint32_t kTmemO = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+struct AttnKParams {
+  int B, H, Lq, Lk, Lh, Li, gtok;
+  float scale_log2;
+  const uint32_t* kbits;
+  int kwords;
+  const uint32_t* qbits;
+  int qwords;
+  __nv_bfloat16* out_img;
+  long long oi_b, oi_t, oi_h, oi_seg, oi_sseg;
+  __nv_bfloat16* out_txt;
+  long long ot_b, ot_t, ot_h;
+  float* lse;
+  int* status;
+  int num_qtiles;
+};
+
+// Key tiles visited by one query tile: [0, a_end) then [b_begin, b_end).
+// Image keys past the block-causal limit of the tile's last row are never loaded.
+struct TileRange {
+  int a_end, b_begin, b_end;
+  __device__ int count() const { return a_end + (b_end - b_begin); }
+  __device__ int tile(int j) const { return j < a_end ? j : b_begin + (j - a_end); }
+};
+
+__device__ TileRange key_tiles(const AttnKParams& p, int q0) {
+  const int q_last = min(q0 + kBM, p.Lq) - 1;
+  const int ntk = (p.Lk + kBN - 1) / kBN;
+  int img_vis_end = p.Lh + p.Li;
+  if (p.gtok > 0 && q_last < p.Li) {
+    const long long lim = static_cast<long long>(q_last / p.gtok + 1) * p.gtok;
+    img_vis_end = p.Lh + static_cast<int>(lim < p.Li ? lim : p.Li);
+  }
+  TileRange r;
+  r.a_end = min((img_vis_end + kBN - 1) / kBN, ntk);
+  const int txt_begin = p.Lh + p.Li;
+  if (txt_begin < p.Lk) {
+    r.b_begin = max(txt_begin / kBN, r.a_end);
+    r.b_end = ntk;
+  } else {
+    r.b_begin = 0;
+    r.b_end = 0;
+  }
+  return r;
+}
+
+// Bounded wait that ignores the abort flag (used to drain in-flight async work on exit).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kSpinLimitCycles) break;
+  }
+}
+
+template <bool kPInTmem>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnKParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sV = sK + kStages * kTileBytes;
+  uint8_t* sP = sV + kStages * kTileBytes;  // used only when P goes through shared memory
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + (kPInTmem ? 0 : 2 * kTileBytes));
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + kStages;
+  uint64_t* v_full = k_empty + kStages;
+  uint64_t* v_empty = v_full + kStages;
+  uint64_t* s_full = v_empty + kStages;  // [2]
+  uint64_t* p_full = s_full + 2;         // [2]
+  uint64_t* o_full = p_full + 2;         // [1]
+  uint64_t* mma_done = o_full + 1;       // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qt = p.num_qtiles - 1 - static_cast<int>(blockIdx.x);  // heavy (late) tiles first
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int q0 = qt * kBM;
+  const int bh = b * p.H + h;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const TileRange tr = key_tiles(p, q0);
+  const int n = tr.count();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_expect_tx(q_full, kTileBytes);
+      tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
+      tma_load_3d(sQ + kHalfTile, &tmQ, q_full, 64, q0, bh);
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int k0 = tr.tile(j) * kBN;
+        const int st = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag)) break;
+        mbar_expect_tx(&k_full[st], kTileBytes);
+        tma_load_3d(sK + st * kTileBytes, &tmK, &k_full[st], 0, k0, bh);
+        tma_load_3d(sK + st * kTileBytes + kHalfTile, &tmK, &k_full[st], 64, k0, bh);
+        if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag)) {
+          issued = j;  // K of tile j is in flight
+          mbar_drain(&k_full[st], ph);
+          break;
+        }
+        mbar_expect_tx(&v_full[st], kTileBytes);
+        tma_load_3d(sV + st * kTileBytes, &tmV, &v_full[st], 0, k0, bh);
+        tma_load_3d(sV + st * kTileBytes + kHalfTile, &tmV, &v_full[st], 64, k0, bh);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        // Let every load already issued land before the CTA can exit.
+        mbar_drain(q_full, 0);
+        for (int j = max(0, issued - kStages); j < issued; ++j) {
+          mbar_drain(&k_full[j % kStages], (j / kStages) & 1);
+          mbar_drain(&v_full[j % kStages], (j / kStages) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescQK = idesc_bf16_f32(kBM, kBN, false, false);
+      constexpr uint32_t kIdescPV = idesc_bf16_f32(kBM, kHD, false, true);
+      const uint32_t sQa = smem_u32(sQ);
+      const uint32_t sKa = smem_u32(sK);
+      const uint32_t sVa = smem_u32(sV);
+      const uint32_t sPa = smem_u32(sP);
+      if (mbar_wait(q_full, 0, abort_flag)) {
+        for (int j = 0; j <= n; ++j) {
+          if (j < n) {
+            const int st = j % kStages;
+            if (!mbar_wait(&k_full[st], (j / kStages) & 1, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t d = tmem + static_cast<uint32_t>(j & 1) * 128u;
+#pragma unroll
+            for (int kk = 0; kk < kHD / 16; ++kk) {
+              const uint32_t koff = static_cast<uint32_t>((kk >> 2) * kHalfTile + (kk & 3) * 32);
+              const uint64_t ad = sdesc_sw128(sQa + koff, 16, 1024);
+              const uint64_t bd = sdesc_sw128(sKa + st * kTileBytes + koff, 16, 1024);
+              umma_ss(d, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
+            }
+            tc_commit(&k_empty[st]);
+            tc_commit(&s_full[j & 1]);
+          }
+          if (j >= 1) {
+            const int jj = j - 1;
+            const int sb = jj & 1;
+            const int st = jj % kStages;
+            if (!mbar_wait(&p_full[sb], (jj >> 1) & 1, abort_flag)) break;
+            if (!mbar_wait(&v_full[st], (jj / kStages) & 1, abort_flag)) break;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+              // V tile is [keys][d] with d contiguous: MN-major B operand.  A K-step of
+              // 16 keys is 16 rows of 128 B; the two 64-column boxes are 16 KB apart.
+              const uint64_t bd = sdesc_sw128(sVa + st * kTileBytes + kk * 2048, kHalfTile, 1024);
+              const uint32_t acc = (jj > 0 || kk > 0) ? 1u : 0u;
+              if (kPInTmem) {
+                umma_ts(tmem + kTmemO, tmem + static_cast<uint32_t>(sb) * 128u + kk * 8, bd,
+                        kIdescPV, acc);
+              } else {
+                const uint32_t koff = static_cast<uint32_t>((kk >> 2) * kHalfTile + (kk & 3) * 32);
+                const uint64_t ad = sdesc_sw128(sPa + sb * kTileBytes + koff, 16, 1024);
+                umma_ss(tmem + kTmemO, ad, bd, kIdescPV, acc);
+              }
+            }
+            tc_commit(&v_empty[st]);
+            tc_commit(o_full);
+          }
+        }
+      }
+      // Drain: every MMA issued by this thread completes before TMEM is released.
+      tc_commit(mma_done);
+      mbar_drain(mma_done, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const int qrow = q0 + row;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const bool img_row = qrow < p.Li;
+    // First invisible image key (relative to the image start) for this row.
+    const int row_lim = (p.gtok > 0 && img_row) ? (qrow / p.gtok + 1) * p.gtok : INT_MAX;
+    const int cta_lim = (p.gtok > 0 && q0 < p.Li) ? (q0 / p.gtok + 1) * p.gtok : INT_MAX;
+    const float sl2 = p.scale_log2;
+    float m_run = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    const uint32_t* kb_row = p.kbits + static_cast<size_t>(b) * p.kwords;
+    for (int j = 0; j < n; ++j) {
+      const int k0 = tr.tile(j) * kBN;
+      const int sb = j & 1;
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t r[32];
+        tmem_ld32_wait(t_lane + static_cast<uint32_t>(sb) * 128u + c4 * 32, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c4 * 32 + i] = __uint_as_float(r[i]);
+      }
+      // ---- masks: key visibility bits, then the block-causal interval of image keys
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = __ldg(kb_row + (k0 >> 5) + i);
+      const bool causal_tile = (cta_lim != INT_MAX) && (k0 + kBN > p.Lh + cta_lim) &&
+                               (k0 < p.Lh + p.Li);
+      if (causal_tile || (w[0] & w[1] & w[2] & w[3]) != 0xffffffffu) {
+        int ca = kBN, cb = 0;
+        if (row_lim != INT_MAX) {
+          ca = min(max(p.Lh + row_lim - k0, 0), kBN);
+          cb = min(max(p.Lh + p.Li - k0, 0), kBN);
+        }
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) {
+          const bool vis = ((w[c >> 5] >> (c & 31)) & 1u) && !(c >= ca && c < cb);
+          s[c] = vis ? s[c] : -INFINITY;
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, s[c]);
+      mx *= sl2;
+      const bool resc = mx > m_run + kRescaleThreshold;
+      const float m_new = resc ? mx : m_run;
+      const float alpha = resc ? ex2(m_run - m_new) : 1.f;
+      if (j > 0 && __any_sync(0xffffffffu, resc)) {
+        // O must hold PV_{j-1} before it is rescaled; PV_j waits for our P below.
+        if (!mbar_wait(o_full, (j - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t r[32];
+          tmem_ld32_wait(t_lane + kTmemO + c4 * 32, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(t_lane + kTmemO + c4 * 32, r);
+        }
+        tmem_st_wait();
+      }
+      l *= alpha;
+      m_run = m_new;
+      const float mref = (m_run == -INFINITY) ? 0.f : m_run;
+      uint32_t pk[kBN / 2];
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < kBN / 2; ++c) {
+        const float e0 = ex2(fmaf(s[2 * c], sl2, -mref));
+        const float e1 = ex2(fmaf(s[2 * c + 1], sl2, -mref));
+        l4[c & 3] += e0 + e1;
+        pk[c] = pack_bf16x2(e0, e1);
+      }
+      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      if (kPInTmem) {
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = pk[i];
+        tmem_st32(t_lane + static_cast<uint32_t>(sb) * 128u, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = pk[32 + i];
+        tmem_st32(t_lane + static_cast<uint32_t>(sb) * 128u + 32, r);
+        tmem_st_wait();
+      } else {
+        uint8_t* prow = sP + sb * kTileBytes + row * 128;
+#pragma unroll
+        for (int c16 = 0; c16 < 16; ++c16) {
+          const int atom = c16 >> 3;
+          const int cc = c16 & 7;
+          uint4 v = make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
+          *reinterpret_cast<uint4*>(prow + atom * kHalfTile + ((cc ^ (row & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[sb]);
+    }
+    // ---- epilogue: O / l at the row's final position
+    bool have_o = ok && n > 0;
+    if (have_o && n >= 2) have_o = mbar_wait(o_full, (n - 2) & 1, abort_flag);
+    if (have_o) have_o = mbar_wait(o_full, (n - 1) & 1, abort_flag);
+    have_o = __all_sync(0xffffffffu, have_o);
+    tc_fence_after();
+    const bool in_range = qrow < p.Lq;
+    bool valid = in_range;
+    if (in_range && p.qbits != nullptr)
+      valid = (__ldg(p.qbits + static_cast<size_t>(b) * p.qwords + (qrow >> 5)) >> (qrow & 31)) & 1u;
+    const float inv_l = (l > 0.f && valid) ? __frcp_rn(l) : 0.f;
+    __nv_bfloat16* dst = nullptr;
+    if (in_range) {
+      if (img_row) {
+        dst = p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg + (qrow % p.oi_seg) * p.oi_t +
+              h * p.oi_h;
+      } else {
+        dst = p.out_txt + b * p.ot_b + static_cast<long long>(qrow - p.Li) * p.ot_t + h * p.ot_h;
+      }
+    }
+#pragma unroll
+    for (int c4 = 0; c4 < 4; ++c4) {
+      uint32_t r[32];
+      if (have_o) {
+        tmem_ld32_wait(t_lane + kTmemO + c4 * 32, r);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = 0u;
+      }
+      uint32_t o[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        o[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
+      if (dst != nullptr) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      }
+    }
+    if (p.lse != nullptr && in_range) {
+      p.lse[static_cast<size_t>(bh) * p.Lq + qrow] =
+          (l > 0.f && valid) ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (threadIdx.x == 0 && *abort_flag && p.status != nullptr) atomicOr(p.status, HYB_DEV_TIMEOUT);
+}
+
+// ------------------------------------------------------------------ staging kernels
+struct StageSeg {
+  const int* rows;  // token -> source row map (history ring), or null
+  const void* data;
+  const float* scale;
+  long long s_b, s_t, s_h, c_b, c_t, c_h;
+  int fmt;
+  int len;
+  int bcast;  // 1: batch index 0 for every output batch
+};
+
+struct StageParams {
+  int B, H, L, nout, nseg;
+  StageSeg seg[2][3];
+  __nv_bfloat16* out[2];  // [B, H, L, 128]
+};
+
+__device__ __forceinline__ uint4 load_row8(const StageSeg& s, int b, int t, int h, int sub) {
+  const int bb = s.bcast ? 0 : b;
+  if (s.rows != nullptr) t = __ldg(s.rows + t);
+  if (s.fmt == HYB_FMT_BF16) {
+    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(s.data) + bb * s.s_b + t * s.s_t +
+                               h * s.s_h + sub * 8;
+    return *reinterpret_cast<const uint4*>(src);
+  }
+  const float sc = s.scale[bb * s.c_b + t * s.c_t + h * s.c_h];
+  const uint8_t* src = static_cast<const uint8_t*>(s.data) + bb * s.s_b + t * s.s_t + h * s.s_h + sub * 8;
+  const uint2 raw = *reinterpret_cast<const uint2*>(src);
+  const uint8_t* by = reinterpret_cast<const uint8_t*>(&raw);
+  uint32_t out[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float a, c;
+    if (s.fmt == HYB_FMT_INT8) {
+      a = static_cast<float>(static_cast<int8_t>(by[2 * i]));
+      c = static_cast<float>(static_cast<int8_t>(by[2 * i + 1]));
+    } else {
+      const __nv_fp8x2_storage_t pair =
+          static_cast<__nv_fp8x2_storage_t>(by[2 * i] | (by[2 * i + 1] << 8));
+      const float2 f = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3)));
+      a = f.x;
+      c = f.y;
+    }
+    out[i] = pack_bf16x2(__fmul_rn(a, sc), __fmul_rn(c, sc));
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+__global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
+  const long long chunks = static_cast<long long>(p.B) * p.L * p.H * 16;
+  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < chunks;
+       c += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int sub = static_cast<int>(c & 15);
+    const long long r = c >> 4;
+    const int h = static_cast<int>(r % p.H);
+    const long long bt = r / p.H;
+    int t = static_cast<int>(bt % p.L);
+    const int b = static_cast<int>(bt / p.L);
+    const long long out_off = ((static_cast<long long>(b) * p.H + h) * p.L + t) * kHD + sub * 8;
+    int si = 0;
+    while (si < p.nseg - 1 && t >= p.seg[0][si].len) {
+      t -= p.seg[0][si].len;
+      ++si;
+    }
+#pragma unroll
+    for (int o = 0; o < 2; ++o) {
+      if (o < p.nout) {
+        *reinterpret_cast<uint4*>(p.out[o] + out_off) = load_row8(p.seg[o][si], b, t, h, sub);
+      }
+    }
+  }
+}
+
+struct MaskParams {
+  int B, Lh, Li, Lt, Lk, kwords, Lq, qwords, attend_txt;
+  const int* hist_rows;
+  const uint8_t* cache_mask;
+  long long cm_sb;
+  int cm_bcast;
+  const uint8_t* text_mask;
+  long long tm_sb;
+  uint32_t* kbits;
+  uint32_t* qbits;
+};
+
+__global__ void __launch_bounds__(256) mask_kernel(const MaskParams p) {
+  const long long kw_total = static_cast<long long>(p.B) * p.kwords;
+  const long long qw_total = static_cast<long long>(p.B) * p.qwords;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+       i < kw_total + qw_total; i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    uint32_t word = 0;
+    if (i < kw_total) {
+      const int b = static_cast<int>(i / p.kwords);
+      const int w = static_cast<int>(i % p.kwords);
+      for (int bit = 0; bit < 32; ++bit) {
+        const int k = w * 32 + bit;
+        bool vis;
+        if (k < p.Lh) {
+          const int row = p.hist_rows != nullptr ? p.hist_rows[k] : k;
+          vis = p.cache_mask == nullptr || p.cache_mask[(p.cm_bcast ? 0 : b) * p.cm_sb + row] != 0;
+        } else if (k < p.Lh + p.Li) {
+          vis = true;
+        } else if (k < p.Lk) {
+          vis = p.text_mask == nullptr || p.text_mask[b * p.tm_sb + (k - p.Lh - p.Li)] != 0;
+        } else {
+          vis = false;
+        }
+        word |= (vis ? 1u : 0u) << bit;
+      }
+      p.kbits[i] = word;
+    } else {
+      const long long j = i - kw_total;
+      const int b = static_cast<int>(j / p.qwords);
+      const int w = static_cast<int>(j % p.qwords);
+      for (int bit = 0; bit < 32; ++bit) {
+        const int q = w * 32 + bit;
+        bool vis;
+        if (q < p.Li) {
+          vis = true;
+        } else if (q < p.Lq) {
+          vis = p.text_mask == nullptr || p.text_mask[b * p.tm_sb + (q - p.Li)] != 0;
+        } else {
+          vis = false;
+        }
+        word |= (vis ? 1u : 0u) << bit;
+      }
+      p.qbits[j] = word;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host helpers
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [BH, L, 128] bf16 head-major tensor, 64 x 128 boxes with 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, int BH, int L) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(HYB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(L), static_cast<cuuint64_t>(BH)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHD) * 2, static_cast<cuuint64_t>(L) * kHD * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HYB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return HYB_OK;
+}
+
+int grid_for(long long items, int threads) {
+  long long blocks = (items + threads - 1) / threads;
+  const long long cap = 148LL * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_view(const hyb_tensor4& v, const char* name, bool allow_quant) {
+  if (v.data == nullptr) return fail(HYB_ERR_INVALID_ARG, "%s: null data", name);
+  if (v.fmt == HYB_FMT_BF16) {
+    if (!al16(v.data) || (v.s_b % 8) || (v.s_t % 8) || (v.s_h % 8))
+      return fail(HYB_ERR_INVALID_ARG, "%s: bf16 rows must be 16-byte aligned", name);
+    return HYB_OK;
+  }
+  if (!allow_quant || (v.fmt != HYB_FMT_E4M3 && v.fmt != HYB_FMT_INT8))
+    return fail(HYB_ERR_UNSUPPORTED, "%s: unsupported format %d", name, v.fmt);
+  if ((reinterpret_cast<uintptr_t>(v.data) & 7u) || (v.s_b % 8) || (v.s_t % 8) || (v.s_h % 8))
+    return fail(HYB_ERR_INVALID_ARG, "%s: code rows must be 8-byte aligned", name);
+  if (v.scale == nullptr) return fail(HYB_ERR_INVALID_ARG, "%s: quantised view without scale", name);
+  return HYB_OK;
+}
+
+StageSeg seg_of(const hyb_tensor4& v, int len, int bcast, const int* rows = nullptr) {
+  StageSeg s;
+  s.rows = rows;
+  s.data = v.data;
+  s.scale = v.scale;
+  s.s_b = v.s_b;
+  s.s_t = v.s_t;
+  s.s_h = v.s_h;
+  s.c_b = v.ss_b;
+  s.c_t = v.ss_t;
+  s.c_h = v.ss_h;
+  s.fmt = v.fmt;
+  s.len = len;
+  s.bcast = bcast;
+  return s;
+}
+
+long long align256(long long x) { return (x + 255) & ~255LL; }
+
+struct WorkspaceLayout {
+  long long q, k, v, kbits, qbits, total;
+  int Lq, Lk, kwords, qwords;
+};
+
+WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt) {
+  WorkspaceLayout w;
+  w.Lq = Li + Lt;
+  w.Lk = Lh + Li + (attend_txt ? Lt : 0);
+  w.kwords = ((w.Lk + kBN - 1) / kBN) * (kBN / 32);
+  w.qwords = (w.Lq + 31) / 32;
+  long long off = 0;
+  w.q = off;
+  off = align256(off + static_cast<long long>(B) * H * w.Lq * kHD * 2);
+  w.k = off;
+  off = align256(off + static_cast<long long>(B) * H * w.Lk * kHD * 2);
+  w.v = off;
+  off = align256(off + static_cast<long long>(B) * H * w.Lk * kHD * 2);
+  w.kbits = off;
+  off = align256(off + static_cast<long long>(B) * w.kwords * 4);
+  w.qbits = off;
+  off = align256(off + static_cast<long long>(B) * (w.qwords > 0 ? w.qwords : 1) * 4);
+  w.total = off;
+  return w;
+}
+
+template <bool kPInTmem>
+int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnKParams& kp,
+                cudaStream_t stream) {
+  const int smem = 1024 + kTileBytes * (1 + 2 * kStages) + (kPInTmem ? 0 : 2 * kTileBytes) + 256;
+  static bool attr_set = false;
+  if (!attr_set) {
+    HYB_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_kernel<kPInTmem>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set = true;
+  }
+  dim3 grid(kp.num_qtiles, kp.H, kp.B);
+  attn_fwd_kernel<kPInTmem><<<grid, kThreads, smem, stream>>>(mq, mk, mv, kp);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
+
+// P (softmax probabilities) goes through tensor memory unless HYB_P_SMEM=1 selects the
+// shared-memory operand path (same math; kept to cross-check the tensor-memory A layout).
+bool p_in_tmem() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("HYB_P_SMEM");
+    mode = (e != nullptr && e[0] == '1') ? 0 : 1;
+  }
+  return mode == 1;
+}
+
+int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
+  if (a->D != kHD) return fail(HYB_ERR_UNSUPPORTED, "attention: head_dim %d != 128", a->D);
+  if (a->B <= 0 || a->H <= 0 || a->Lq < 0 || a->Lk < 0 || a->hist_len < 0 || a->img_len < 0 ||
+      a->hist_len + a->img_len > a->Lk || a->img_len > a->Lq || a->group_tokens < 0)
+    return fail(HYB_ERR_INVALID_ARG, "attention: inconsistent sizes");
+  if (a->Lq == 0) return HYB_OK;
+  if (!al16(a->q) || !al16(a->k) || !al16(a->v)) return fail(HYB_ERR_INVALID_ARG, "attention: q/k/v misaligned");
+  if (a->kwords < ((a->Lk + kBN - 1) / kBN) * (kBN / 32))
+    return fail(HYB_ERR_INVALID_ARG, "attention: kbits too short");
+  if (a->img_len > 0) {
+    if (a->out_img == nullptr || !al16(a->out_img) || (a->oi_sb % 8) || (a->oi_st % 8) || (a->oi_sh % 8) ||
+        (a->oi_sseg % 8) || a->oi_seg <= 0)
+      return fail(HYB_ERR_INVALID_ARG, "attention: image output misaligned");
+  }
+  if (a->Lq > a->img_len) {
+    if (a->out_txt == nullptr || !al16(a->out_txt) || (a->ot_sb % 8) || (a->ot_st % 8) || (a->ot_sh % 8))
+      return fail(HYB_ERR_INVALID_ARG, "attention: text output misaligned");
+  }
+  if (device_cc_major() != 10) return fail(HYB_ERR_UNSUPPORTED, "attention: requires an sm_100 GPU");
+  const int BH = a->B * a->H;
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_map(&mq, a->q, BH, a->Lq)) != HYB_OK) return rc;
+  if ((rc = make_map(&mk, a->k, BH, a->Lk > 0 ? a->Lk : 1)) != HYB_OK) return rc;
+  if ((rc = make_map(&mv, a->v, BH, a->Lk > 0 ? a->Lk : 1)) != HYB_OK) return rc;
+  AttnKParams kp;
+  kp.B = a->B;
+  kp.H = a->H;
+  kp.Lq = a->Lq;
+  kp.Lk = a->Lk;
+  kp.Lh = a->hist_len;
+  kp.Li = a->img_len;
+  kp.gtok = a->group_tokens;
+  const float scale = a->softmax_scale > 0.f ? a->softmax_scale : 1.0f / sqrtf(static_cast<float>(kHD));
+  kp.scale_log2 = scale * kLog2e;
+  kp.kbits = a->kbits;
+  kp.kwords = a->kwords;
+  kp.qbits = a->qbits;
+  kp.qwords = a->qwords;
+  kp.out_img = static_cast<__nv_bfloat16*>(a->out_img);
+  kp.oi_b = a->oi_sb;
+  kp.oi_t = a->oi_st;
+  kp.oi_h = a->oi_sh;
+  kp.oi_seg = a->oi_seg > 0 ? a->oi_seg : 1;
+  kp.oi_sseg = a->oi_sseg;
+  kp.out_txt = static_cast<__nv_bfloat16*>(a->out_txt);
+  kp.ot_b = a->ot_sb;
+  kp.ot_t = a->ot_st;
+  kp.ot_h = a->ot_sh;
+  kp.lse = a->lse;
+  kp.status = a->dev_status;
+  kp.num_qtiles = (a->Lq + kBM - 1) / kBM;
+  return p_in_tmem() ? launch_attn<true>(mq, mk, mv, kp, stream) : launch_attn<false>(mq, mk, mv, kp, stream);
+}
+
+}  // namespace
+}  // namespace hyb
+
+using namespace hyb;
+
+extern "C" int hyb_attn_fwd(const hyb_attn_args* a, void* stream) {
+  if (a == nullptr || a->abi_version != HYB_ABI_VERSION)
+    return fail(HYB_ERR_INVALID_ARG, "attention: null args or ABI version mismatch");
+  return attn_core(a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t hyb_cached_attention_workspace_bytes(int32_t B, int32_t H, int32_t D, int32_t valid_len,
+                                                        int32_t img_len, int32_t txt_len, int32_t attend_txt) {
+  if (D != kHD || B < 0 || H < 0 || valid_len < 0 || img_len < 0 || txt_len < 0) return -1;
+  return layout_for(B, H, valid_len, img_len, txt_len, attend_txt).total;
+}
+
+extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_ptr) {
+  if (a == nullptr || a->abi_version != HYB_ABI_VERSION)
+    return fail(HYB_ERR_INVALID_ARG, "cached attention: null args or ABI version mismatch");
+  if (a->D != kHD) return fail(HYB_ERR_UNSUPPORTED, "cached attention: head_dim %d != 128", a->D);
+  if (a->B <= 0 || a->H <= 0 || a->valid_len < 0 || a->img_len < 0 || a->txt_len < 0 || a->group_tokens < 0)
+    return fail(HYB_ERR_INVALID_ARG, "cached attention: negative sizes");
+  if (a->cache_batch != a->B && a->cache_batch != 1)
+    return fail(HYB_ERR_INVALID_ARG, "KV-cache batch mismatch: current=%d, cache=%d", a->B, a->cache_batch);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int Lh = a->valid_len, Li = a->img_len, Lt = a->txt_len;
+  const WorkspaceLayout w = layout_for(a->B, a->H, Lh, Li, Lt, a->attend_txt);
+  if (a->workspace == nullptr || a->workspace_bytes < w.total || !al16(a->workspace))
+    return fail(HYB_ERR_WORKSPACE, "cached attention: workspace %lld bytes < %lld needed",
+                (long long)a->workspace_bytes, (long long)w.total);
+  int rc;
+  if (Lh > 0) {
+    if ((rc = check_view(a->hist_k, "hist_k", true)) != HYB_OK) return rc;
+    if ((rc = check_view(a->hist_v, "hist_v", true)) != HYB_OK) return rc;
+    if (a->hist_k.fmt != a->hist_v.fmt) return fail(HYB_ERR_INVALID_ARG, "KV cache K/V dtype mismatch");
+  }
+  if (Li > 0) {
+    if ((rc = check_view(a->img_q, "img_q", false)) != HYB_OK) return rc;
+    if ((rc = check_view(a->img_k, "img_k", false)) != HYB_OK) return rc;
+    if ((rc = check_view(a->img_v, "img_v", false)) != HYB_OK) return rc;
+  }
+  if (Lt > 0) {
+    if ((rc = check_view(a->txt_q, "txt_q", false)) != HYB_OK) return rc;
+    if (a->attend_txt) {
+      if ((rc = check_view(a->txt_k, "txt_k", false)) != HYB_OK) return rc;
+      if ((rc = check_view(a->txt_v, "txt_v", false)) != HYB_OK) return rc;
+    }
+  }
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  __nv_bfloat16* q_all = reinterpret_cast<__nv_bfloat16*>(ws + w.q);
+  __nv_bfloat16* k_all = reinterpret_cast<__nv_bfloat16*>(ws + w.k);
+  __nv_bfloat16* v_all = reinterpret_cast<__nv_bfloat16*>(ws + w.v);
+  uint32_t* kbits = reinterpret_cast<uint32_t*>(ws + w.kbits);
+  uint32_t* qbits = reinterpret_cast<uint32_t*>(ws + w.qbits);
+
+  // key / query visibility bitmaps
+  MaskParams mp;
+  mp.B = a->B;
+  mp.Lh = Lh;
+  mp.Li = Li;
+  mp.Lt = Lt;
+  mp.Lk = w.Lk;
+  mp.kwords = w.kwords;
+  mp.Lq = w.Lq;
+  mp.qwords = w.qwords;
+  mp.attend_txt = a->attend_txt;
+  mp.hist_rows = a->hist_rows;
+  mp.cache_mask = a->cache_mask;
+  mp.cm_sb = a->cache_mask_sb;
+  mp.cm_bcast = a->cache_batch == 1 ? 1 : 0;
+  mp.text_mask = a->text_mask;
+  mp.tm_sb = a->text_mask_sb;
+  mp.kbits = kbits;
+  mp.qbits = qbits;
+  mask_kernel<<<grid_for(static_cast<long long>(a->B) * (w.kwords + w.qwords), 256), 256, 0, stream>>>(mp);
+  HYB_CHECK_LAUNCH();
+
+  // K / V composition (history decoded in the same pass)
+  if (w.Lk > 0) {
+    StageParams sp;
+    sp.B = a->B;
+    sp.H = a->H;
+    sp.L = w.Lk;
+    sp.nout = 2;
+    sp.nseg = 0;
+    const hyb_tensor4* srcs[2][3] = {{&a->hist_k, &a->img_k, &a->txt_k}, {&a->hist_v, &a->img_v, &a->txt_v}};
+    const int lens[3] = {Lh, Li, a->attend_txt ? Lt : 0};
+    for (int si = 0; si < 3; ++si) {
+      if (lens[si] == 0) continue;
+      for (int o = 0; o < 2; ++o)
+        sp.seg[o][sp.nseg] = seg_of(*srcs[o][si], lens[si], (si == 0 && a->cache_batch == 1) ? 1 : 0,
+                                    si == 0 ? a->hist_rows : nullptr);
+      ++sp.nseg;
+    }
+    sp.out[0] = k_all;
+    sp.out[1] = v_all;
+    stage_kernel<<<grid_for(static_cast<long long>(a->B) * a->H * w.Lk * 16, 256), 256, 0, stream>>>(sp);
+    HYB_CHECK_LAUNCH();
+  }
+  if (w.Lq > 0) {
+    StageParams sp;
+    sp.B = a->B;
+    sp.H = a->H;
+    sp.L = w.Lq;
+    sp.nout = 1;
+    sp.nseg = 0;
+    if (Li > 0) sp.seg[0][sp.nseg++] = seg_of(a->img_q, Li, 0);
+    if (Lt > 0) sp.seg[0][sp.nseg++] = seg_of(a->txt_q, Lt, 0);
+    sp.out[0] = q_all;
+    sp.out[1] = nullptr;
+    stage_kernel<<<grid_for(static_cast<long long>(a->B) * a->H * w.Lq * 16, 256), 256, 0, stream>>>(sp);
+    HYB_CHECK_LAUNCH();
+  } else {
+    return HYB_OK;
+  }
+
+  hyb_attn_args at;
+  at.abi_version = HYB_ABI_VERSION;
+  at.B = a->B;
+  at.H = a->H;
+  at.D = a->D;
+  at.Lq = w.Lq;
+  at.Lk = w.Lk;
+  at.hist_len = Lh;
+  at.img_len = Li;
+  at.group_tokens = a->group_tokens;
+  at.softmax_scale = a->softmax_scale;
+  at.q = q_all;
+  at.k = k_all;
+  at.v = v_all;
+  at.kbits = kbits;
+  at.kwords = w.kwords;
+  at.qbits = qbits;
+  at.qwords = w.qwords;
+  at.out_img = a->out_img;
+  at.oi_sb = a->oi_sb;
+  at.oi_st = a->oi_st;
+  at.oi_sh = a->oi_sh;
+  at.oi_seg = a->oi_seg > 0 ? a->oi_seg : (Li > 0 ? Li : 1);
+  at.oi_sseg = a->oi_seg > 0 ? a->oi_sseg : 0;
+  at.out_txt = a->out_txt;
+  at.ot_sb = a->ot_sb;
+  at.ot_st = a->ot_st;
+  at.ot_sh = a->ot_sh;
+  at.lse = a->lse;
+  at.dev_status = a->dev_status;
+  return attn_core(&at, stream);
+}

@@ -1,0 +1,49 @@
+// Library identity, per-thread error messages and device checks for the C ABI.
+#include <stdarg.h>
+#include <string.h>
+
+#include "hyb_common.cuh"
+
+namespace hyb {
+
+static thread_local char g_last_error[1024] = {0};
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int device_cc_major() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return -1;
+  return major;
+}
+
+}  // namespace hyb
+
+extern "C" int hyb_version(void) { return HYB_ABI_VERSION; }
+
+extern "C" int hyb_last_error(char* buf, size_t len) {
+  size_t n = strlen(hyb::g_last_error);
+  if (buf != nullptr && len > 0) {
+    size_t c = n < len - 1 ? n : len - 1;
+    memcpy(buf, hyb::g_last_error, c);
+    buf[c] = 0;
+  }
+  return static_cast<int>(n);
+}
+
+extern "C" int hyb_device_supported(void) { return hyb::device_cc_major() == 10 ? 1 : 0; }

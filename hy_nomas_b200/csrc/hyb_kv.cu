@@ -1,0 +1,292 @@
+// Quantised KV cache kernels: quantise-on-write append (E4M3 / INT8), finite check,
+// and decode of the valid prefix.  HBM-bound byte work: one 16-lane group owns one
+// (batch, token, head) row of D = 128 bf16 values (16-byte loads, 8-byte stores).
+//
+// Arithmetic follows the CPU branch of quantize_kv_into
+// (hymm/models/dit/modules/int8_kv_cache.py:149-158):
+//   peak  = max |x|                       (fp32)
+//   s     = peak > 0 ? peak / R : 1       (IEEE fp32 division, R = 127 or 448)
+//   y     = x / s                         (IEEE fp32 division)
+//   INT8: code = clamp(y >= 0 ? floor(y + 0.5) : ceil(y - 0.5), -127, 127)
+//   E4M3: code = e4m3_rn(clamp(y, -448, 448))
+#include "hyb_common.cuh"
+
+namespace hyb {
+namespace {
+
+constexpr int kRowLanes = 16;  // lanes per row: 16 x 8 bf16 = 128 values
+
+struct AppendParams {
+  int fmt;
+  int B, L, H;
+  long long start;
+  const __nv_bfloat16* src[2];
+  long long s_b[2], s_t[2], s_h[2];
+  void* dst[2];
+  long long d_b, d_t, d_h;
+  float* scale[2];
+  long long c_b, c_t, c_h;
+  int* status;
+};
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(p[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+__global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams p) {
+  const int which = blockIdx.y;  // 0 = K, 1 = V
+  const long long rows = static_cast<long long>(p.B) * p.L * p.H;
+  const int sub = threadIdx.x & (kRowLanes - 1);
+  const long long row0 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / kRowLanes;
+  const long long row_step = static_cast<long long>(gridDim.x) * blockDim.x / kRowLanes;
+  bool nonfinite = false;
+  for (long long row = row0; row < rows; row += row_step) {
+    const int h = static_cast<int>(row % p.H);
+    const long long bt = row / p.H;
+    const int t = static_cast<int>(bt % p.L);
+    const int b = static_cast<int>(bt / p.L);
+    const __nv_bfloat16* src = p.src[which] + b * p.s_b[which] + t * p.s_t[which] +
+                               h * p.s_h[which] + sub * 8;
+    uint4 raw = *reinterpret_cast<const uint4*>(src);
+    float x[8];
+    unpack8(raw, x);
+    float peak = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      peak = fmaxf(peak, fabsf(x[i]));
+      nonfinite |= !isfinite(x[i]);
+    }
+#pragma unroll
+    for (int off = kRowLanes / 2; off >= 1; off >>= 1)
+      peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, off, kRowLanes));
+    const float denom = (p.fmt == HYB_FMT_INT8) ? 127.0f : 448.0f;
+    const float s = peak > 0.f ? __fdiv_rn(peak, denom) : 1.0f;
+    const long long dst_off =
+        b * p.d_b + (t + p.start) * p.d_t + h * p.d_h + sub * 8;
+    if (p.fmt == HYB_FMT_INT8) {
+      uint32_t w[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float y = __fdiv_rn(x[half * 4 + i], s);
+          float r = (y >= 0.f) ? floorf(__fadd_rn(y, 0.5f)) : ceilf(__fsub_rn(y, 0.5f));
+          r = fminf(fmaxf(r, -127.f), 127.f);
+          const int8_t c = static_cast<int8_t>(static_cast<int>(r));
+          acc |= static_cast<uint32_t>(static_cast<uint8_t>(c)) << (8 * i);
+        }
+        w[half] = acc;
+      }
+      *reinterpret_cast<uint2*>(static_cast<int8_t*>(p.dst[which]) + dst_off) =
+          make_uint2(w[0], w[1]);
+    } else {
+      uint32_t w[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i += 2) {
+          float2 y;
+          y.x = fminf(fmaxf(__fdiv_rn(x[half * 4 + i], s), -448.f), 448.f);
+          y.y = fminf(fmaxf(__fdiv_rn(x[half * 4 + i + 1], s), -448.f), 448.f);
+          const __nv_fp8x2_storage_t c2 = __nv_cvt_float2_to_fp8x2(y, __NV_SATFINITE, __NV_E4M3);
+          acc |= static_cast<uint32_t>(c2) << (8 * i);
+        }
+        w[half] = acc;
+      }
+      *reinterpret_cast<uint2*>(static_cast<uint8_t*>(p.dst[which]) + dst_off) =
+          make_uint2(w[0], w[1]);
+    }
+    if (sub == 0) p.scale[which][b * p.c_b + (t + p.start) * p.c_t + h * p.c_h] = s;
+  }
+  if (p.status != nullptr && __any_sync(0xffffffffu, nonfinite) && (threadIdx.x & 31) == 0)
+    atomicOr(p.status, HYB_DEV_NONFINITE);
+}
+
+struct FiniteParams {
+  const __nv_bfloat16* src;
+  long long s_b, s_t, s_h;
+  int B, L, H;
+  int* status;
+};
+
+__global__ void __launch_bounds__(256) check_finite_kernel(const FiniteParams p) {
+  const long long chunks = static_cast<long long>(p.B) * p.L * p.H * 16;
+  bool bad = false;
+  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < chunks;
+       c += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int sub = static_cast<int>(c & 15);
+    const long long row = c >> 4;
+    const int h = static_cast<int>(row % p.H);
+    const long long bt = row / p.H;
+    const int t = static_cast<int>(bt % p.L);
+    const int b = static_cast<int>(bt / p.L);
+    uint4 raw = *reinterpret_cast<const uint4*>(p.src + b * p.s_b + t * p.s_t + h * p.s_h + sub * 8);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      // bf16 exponent field all ones <=> inf or nan
+      bad |= ((w[i] & 0x7F80u) == 0x7F80u) || ((w[i] & 0x7F800000u) == 0x7F800000u);
+    }
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(p.status, HYB_DEV_NONFINITE);
+}
+
+struct DequantParams {
+  int fmt;
+  const void* src;
+  long long s_b, s_t, s_h;
+  const float* scale;
+  long long c_b, c_t, c_h;
+  int B, L, H;
+  __nv_bfloat16* dst;  // contiguous [B, L, H, 128]
+};
+
+// bf16(code * scale) with one fp32 multiply and one RNE rounding, as in dequantize_kv's
+// CPU branch (int8_kv_cache.py:202-204).
+__global__ void __launch_bounds__(256) kv_dequant_kernel(const DequantParams p) {
+  const long long chunks = static_cast<long long>(p.B) * p.L * p.H * 16;
+  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < chunks;
+       c += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int sub = static_cast<int>(c & 15);
+    const long long row = c >> 4;
+    const int h = static_cast<int>(row % p.H);
+    const long long bt = row / p.H;
+    const int t = static_cast<int>(bt % p.L);
+    const int b = static_cast<int>(bt / p.L);
+    const float s = p.scale[b * p.c_b + t * p.c_t + h * p.c_h];
+    const uint8_t* src = static_cast<const uint8_t*>(p.src) + b * p.s_b + t * p.s_t + h * p.s_h + sub * 8;
+    const uint2 raw = *reinterpret_cast<const uint2*>(src);
+    const uint8_t* bytes = reinterpret_cast<const uint8_t*>(&raw);
+    uint32_t out[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float a, bb;
+      if (p.fmt == HYB_FMT_INT8) {
+        a = static_cast<float>(static_cast<int8_t>(bytes[2 * i]));
+        bb = static_cast<float>(static_cast<int8_t>(bytes[2 * i + 1]));
+      } else {
+        const __nv_fp8x2_storage_t pair =
+            static_cast<__nv_fp8x2_storage_t>(bytes[2 * i] | (bytes[2 * i + 1] << 8));
+        const __half2 hh = __half2(__nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3));
+        const float2 f = __half22float2(hh);
+        a = f.x;
+        bb = f.y;
+      }
+      out[i] = pack_bf16x2(__fmul_rn(a, s), __fmul_rn(bb, s));
+    }
+    *reinterpret_cast<uint4*>(p.dst + row * 128 + sub * 8) = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
+int grid_for(long long work_items, int threads) {
+  long long blocks = (work_items + threads - 1) / threads;
+  const long long cap = 148LL * 16;  // plenty of resident warps on 148 SMs
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace hyb
+
+using namespace hyb;
+
+extern "C" int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, int32_t D,
+                                  int64_t cap, int64_t start, const hyb_tensor4* src_k,
+                                  const hyb_tensor4* src_v, void* dst_k, void* dst_v,
+                                  int64_t d_sb, int64_t d_st, int64_t d_sh, float* scale_k,
+                                  float* scale_v, int64_t s_sb, int64_t s_st, int64_t s_sh,
+                                  int32_t* dev_status, void* stream) {
+  if (fmt != HYB_FMT_E4M3 && fmt != HYB_FMT_INT8)
+    return fail(HYB_ERR_UNSUPPORTED, "kv append: format %d is not E4M3 or INT8", fmt);
+  if (D != 128) return fail(HYB_ERR_UNSUPPORTED, "kv append: head_dim %d != 128", D);
+  if (B < 0 || L < 0 || H <= 0 || src_k == nullptr || src_v == nullptr)
+    return fail(HYB_ERR_INVALID_ARG, "kv append: bad sizes or null views");
+  if (start < 0 || start + L > cap)
+    return fail(HYB_ERR_CAPACITY, "kv append: tokens [%lld, %lld) exceed capacity %lld",
+                (long long)start, (long long)(start + L), (long long)cap);
+  if (L == 0 || B == 0) return HYB_OK;
+  if (src_k->fmt != HYB_FMT_BF16 || src_v->fmt != HYB_FMT_BF16)
+    return fail(HYB_ERR_INVALID_ARG, "kv append: sources must be bf16");
+  const hyb_tensor4* srcs[2] = {src_k, src_v};
+  for (int i = 0; i < 2; ++i) {
+    if (!aligned16(srcs[i]->data) || (srcs[i]->s_b % 8) || (srcs[i]->s_t % 8) || (srcs[i]->s_h % 8))
+      return fail(HYB_ERR_INVALID_ARG, "kv append: source rows must be 16-byte aligned");
+  }
+  if ((reinterpret_cast<uintptr_t>(dst_k) & 7u) || (reinterpret_cast<uintptr_t>(dst_v) & 7u) ||
+      (d_sb % 8) || (d_st % 8) || (d_sh % 8))
+    return fail(HYB_ERR_INVALID_ARG, "kv append: code rows must be 8-byte aligned");
+  AppendParams p;
+  p.fmt = fmt;
+  p.B = B;
+  p.L = L;
+  p.H = H;
+  p.start = start;
+  for (int i = 0; i < 2; ++i) {
+    p.src[i] = static_cast<const __nv_bfloat16*>(srcs[i]->data);
+    p.s_b[i] = srcs[i]->s_b;
+    p.s_t[i] = srcs[i]->s_t;
+    p.s_h[i] = srcs[i]->s_h;
+  }
+  p.dst[0] = dst_k;
+  p.dst[1] = dst_v;
+  p.d_b = d_sb;
+  p.d_t = d_st;
+  p.d_h = d_sh;
+  p.scale[0] = scale_k;
+  p.scale[1] = scale_v;
+  p.c_b = s_sb;
+  p.c_t = s_st;
+  p.c_h = s_sh;
+  p.status = dev_status;
+  const long long rows = static_cast<long long>(B) * L * H;
+  dim3 grid(grid_for(rows * kRowLanes, 256), 2);
+  kv_append_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
+
+extern "C" int hyb_check_finite(const hyb_tensor4* src, int32_t B, int32_t L, int32_t H, int32_t D,
+                                int32_t* dev_status, void* stream) {
+  if (D != 128) return fail(HYB_ERR_UNSUPPORTED, "finite check: head_dim %d != 128", D);
+  if (src == nullptr || dev_status == nullptr)
+    return fail(HYB_ERR_INVALID_ARG, "finite check: null argument");
+  if (src->fmt != HYB_FMT_BF16) return fail(HYB_ERR_INVALID_ARG, "finite check: bf16 only");
+  if (!aligned16(src->data) || (src->s_b % 8) || (src->s_t % 8) || (src->s_h % 8))
+    return fail(HYB_ERR_INVALID_ARG, "finite check: rows must be 16-byte aligned");
+  if (B == 0 || L == 0) return HYB_OK;
+  FiniteParams p{static_cast<const __nv_bfloat16*>(src->data), src->s_b, src->s_t, src->s_h, B, L, H,
+                 dev_status};
+  const long long chunks = static_cast<long long>(B) * L * H * 16;
+  check_finite_kernel<<<grid_for(chunks, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
+
+extern "C" int hyb_kv_dequant(const hyb_tensor4* src, int32_t B, int32_t valid, int32_t H,
+                              int32_t D, void* dst, void* stream) {
+  if (D != 128) return fail(HYB_ERR_UNSUPPORTED, "dequant: head_dim %d != 128", D);
+  if (src == nullptr || dst == nullptr) return fail(HYB_ERR_INVALID_ARG, "dequant: null argument");
+  if (src->fmt != HYB_FMT_E4M3 && src->fmt != HYB_FMT_INT8)
+    return fail(HYB_ERR_UNSUPPORTED, "dequant: format %d is not E4M3 or INT8", src->fmt);
+  if ((reinterpret_cast<uintptr_t>(src->data) & 7u) || (src->s_b % 8) || (src->s_t % 8) ||
+      (src->s_h % 8) || !aligned16(dst))
+    return fail(HYB_ERR_INVALID_ARG, "dequant: misaligned rows");
+  if (B == 0 || valid == 0) return HYB_OK;
+  DequantParams p{src->fmt, src->data, src->s_b, src->s_t, src->s_h, src->scale, src->ss_b,
+                  src->ss_t, src->ss_h, B, valid, H, static_cast<__nv_bfloat16*>(dst)};
+  const long long chunks = static_cast<long long>(B) * valid * H * 16;
+  kv_dequant_kernel<<<grid_for(chunks, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}

@@ -1,0 +1,188 @@
+/*
+ * hyb200.h — C ABI of the B200 (sm_100a) chunk-causal cached attention path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * launches on the caller's CUDA stream and returns an int status
+ * (HYB_OK == 0, negative on error; hyb_last_error() gives the message).
+ * Nothing here allocates device memory: per-call scratch comes from a
+ * caller-provided workspace whose size hyb_cached_attention_workspace_bytes()
+ * reports.  No torch types cross this boundary.
+ *
+ * Reference interfaces replaced (paths relative to the Hy-Nomas project):
+ *   hyb_kv_append_pair        <- quantize_kv_pair_into / quantize_kv_into / _quantize_rows
+ *                                hymm/models/dit/modules/int8_kv_cache.py:125-179, :22-58
+ *                                (HYB_FMT_INT8 exact; HYB_FMT_E4M3 is the same rule with a
+ *                                448 denominator and an e4m3 RNE cast)
+ *   hyb_kv_dequant            <- dequantize_kv / _dequantize_rows
+ *                                hymm/models/dit/modules/int8_kv_cache.py:182-205, :61-89
+ *   hyb_cached_attention      <- causal_attention_with_cache_mp, single rank part (history
+ *                                decode, K/V composition, masks, kernel, pad)
+ *                                hymm/models/dit/nomas_cpt.py:335-884 (steps 2-6 of the call),
+ *                                and the sm_100 incumbent CacheStaging.__call__ +
+ *                                compact_kv reactor/hy_nomas_cache.py:192-338, :48-73
+ *   hyb_attn_fwd              <- the kernel call inside it: flash_attn_varlen_func (FA3/FA4)
+ *                                nomas_cpt.py:786-829, magi flex_flash_attn_func with the
+ *                                chunk-causal ranges of attention/magi_attn.py:290-309
+ *   hyb_lse_merge             <- flash_attn_fwd_out_correction / _softmax_lse_correction
+ *                                hymm/models/dit/modules/attention/dynamic_ring_attention.py:86-105
+ *   hyb_ulysses_pack_qkv      <- pack_qkv + all_to_all_qkv send-side layout
+ *                                reactor/hy_nomas_fusions.py:56-78, hymm/distributed/communications.py:270-280
+ *   hyb_ulysses_unpack_o      <- _all_to_all_4D(scatter_idx=1, gather_idx=2) receive-side layout
+ *                                hymm/distributed/communications.py:158-200
+ */
+#ifndef HYB200_H_
+#define HYB200_H_
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HYB_ABI_VERSION 1
+
+/* status codes */
+#define HYB_OK 0
+#define HYB_ERR_INVALID_ARG (-1)   /* bad shape / stride / pointer / size (ValueError) */
+#define HYB_ERR_UNSUPPORTED (-2)   /* head_dim != 128, dtype, arch (RuntimeError) */
+#define HYB_ERR_CUDA (-3)          /* CUDA runtime error (RuntimeError) */
+#define HYB_ERR_TIMEOUT (-4)       /* a bounded device-side wait expired (RuntimeError) */
+#define HYB_ERR_NONFINITE (-5)     /* non-finite K/V handed to the quantiser (ValueError) */
+#define HYB_ERR_CAPACITY (-6)      /* write past cache capacity (ValueError) */
+#define HYB_ERR_WORKSPACE (-7)     /* workspace too small (RuntimeError) */
+
+/* element formats */
+#define HYB_FMT_BF16 0   /* plain bf16 values */
+#define HYB_FMT_E4M3 1   /* float8_e4m3fn codes + fp32 per-(token, head) scale */
+#define HYB_FMT_INT8 2   /* int8 codes + fp32 per-(token, head) scale (reference format) */
+
+/* device status bits written by kernels into a caller-provided int32 */
+#define HYB_DEV_TIMEOUT 0x1
+#define HYB_DEV_NONFINITE 0x2
+
+/* A [B, L, H, D] tensor view with unit stride on D (strides in elements).
+ * For HYB_FMT_E4M3 / HYB_FMT_INT8, `scale` is the fp32 [B, L, H(, 1)] scale tensor. */
+typedef struct hyb_tensor4 {
+  const void* data;
+  int32_t fmt;
+  int32_t pad_;
+  int64_t s_b, s_t, s_h;
+  const float* scale;
+  int64_t ss_b, ss_t, ss_h;
+} hyb_tensor4;
+
+/* One cached-attention call on one rank (after any Ulysses exchange).
+ * Keys attended by every query: [visible history | current image | current text].
+ * Image query i sees image key j iff j / group_tokens <= i / group_tokens
+ * (group_tokens == 0: the whole chunk is bidirectional, the reference's cached path).
+ * Text queries see every visible key.  History key t is visible iff cache_mask[b, t];
+ * text key t iff text_mask[b, t].  Output rows of masked text queries are zero
+ * (the flash3 path's pad_tokens semantics, nomas_cpt.py:823-829). */
+typedef struct hyb_cached_attn_args {
+  int32_t abi_version;     /* HYB_ABI_VERSION */
+  int32_t B, H, D;         /* batch, heads on this rank, head_dim (128) */
+  int32_t cache_batch;     /* batch of the history tensors: B, or 1 (read-only broadcast) */
+  int32_t valid_len;       /* history tokens [0, valid_len) read from hist_k/hist_v */
+  int32_t img_len, txt_len;
+  int32_t attend_txt;      /* 1: current text keys are attended (cache_txt or update_cache) */
+  int32_t group_tokens;    /* block-causal granularity in tokens (G frames x tokens/frame), 0 = off */
+  float softmax_scale;     /* <= 0 selects 1/sqrt(D) */
+  hyb_tensor4 hist_k, hist_v;                 /* cache: BF16 / E4M3 / INT8 */
+  hyb_tensor4 img_q, img_k, img_v;            /* BF16 [B, img_len, H, D] */
+  hyb_tensor4 txt_q, txt_k, txt_v;            /* BF16 [B, txt_len, H, D] */
+  const int32_t* hist_rows; /* [valid_len] cache row of composed history position t, or NULL
+                               (identity); sink + sliding-window rings use it */
+  const uint8_t* cache_mask; int64_t cache_mask_sb;  /* bool [cache_batch, cap] (cache rows) or NULL */
+  const uint8_t* text_mask;  int64_t text_mask_sb;   /* bool [B, txt_len] or NULL */
+  void* out_img; int64_t oi_sb, oi_st, oi_sh;        /* bf16 [B, img_len, H, D] */
+  int64_t oi_seg, oi_sseg; /* image row t at (t / oi_seg) * oi_sseg + (t % oi_seg) * oi_st;
+                              oi_seg <= 0 means img_len (no segmentation) */
+  void* out_txt; int64_t ot_sb, ot_st, ot_sh;        /* bf16 [B, txt_len, H, D] */
+  float* lse;              /* fp32 [B, H, img_len + txt_len] natural-log LSE, or NULL */
+  void* workspace; int64_t workspace_bytes;
+  int32_t* dev_status;     /* int32 on the device, OR-ed with HYB_DEV_* bits, or NULL */
+  int32_t pad_;
+} hyb_cached_attn_args;
+
+/* Library identity. */
+int hyb_version(void);
+/* Copies the calling thread's last error message (NUL-terminated). Returns its length. */
+int hyb_last_error(char* buf, size_t len);
+/* 1 if the current device is sm_100 (B200/GB200) and the kernels can run, else 0. */
+int hyb_device_supported(void);
+
+/* Quantise-on-write of a K/V pair into a per-token-per-head scaled cache.
+ * src: bf16 [B, L, H, D]; dst codes at token offset `start` of [B, cap, H, D];
+ * scales fp32 [B, cap, H, 1].  Scale = absmax/127 (INT8) or absmax/448 (E4M3),
+ * 1 for an all-zero row; codes use IEEE division.  dev_status (may be NULL)
+ * gets HYB_DEV_NONFINITE if any input was not finite. */
+int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, int32_t D, int64_t cap,
+                       int64_t start,
+                       const hyb_tensor4* src_k, const hyb_tensor4* src_v,
+                       void* dst_k, void* dst_v, int64_t d_sb, int64_t d_st, int64_t d_sh,
+                       float* scale_k, float* scale_v, int64_t s_sb, int64_t s_st, int64_t s_sh,
+                       int32_t* dev_status, void* stream);
+
+/* Finite check of a bf16 [B, L, H, D] tensor; ORs HYB_DEV_NONFINITE into dev_status. */
+int hyb_check_finite(const hyb_tensor4* src, int32_t B, int32_t L, int32_t H, int32_t D,
+                     int32_t* dev_status, void* stream);
+
+/* Decode the valid prefix of a quantised cache into bf16 [B, valid, H, D] (contiguous). */
+int hyb_kv_dequant(const hyb_tensor4* src, int32_t B, int32_t valid, int32_t H, int32_t D,
+                   void* dst, void* stream);
+
+/* Workspace bytes needed by hyb_cached_attention for these sizes. */
+int64_t hyb_cached_attention_workspace_bytes(int32_t B, int32_t H, int32_t D, int32_t valid_len,
+                                             int32_t img_len, int32_t txt_len, int32_t attend_txt);
+
+/* The whole single-rank cached attention (stage + tcgen05 attention kernel). */
+int hyb_cached_attention(const hyb_cached_attn_args* args, void* stream);
+
+/* Attention kernel alone over staged head-major bf16 tensors:
+ * q [B, H, Lq, D], k/v [B, H, Lk, D] (contiguous).  Key j < hist_len is history,
+ * [hist_len, hist_len + img_len) current image (block-causal), the rest text.
+ * kbits: [B, kwords] visibility bitmap of keys; qbits: [B, qwords] query validity. */
+typedef struct hyb_attn_args {
+  int32_t abi_version;
+  int32_t B, H, D, Lq, Lk, hist_len, img_len, group_tokens;
+  float softmax_scale;
+  const void* q; const void* k; const void* v;
+  const uint32_t* kbits; int32_t kwords;
+  const uint32_t* qbits; int32_t qwords;
+  void* out_img; int64_t oi_sb, oi_st, oi_sh;
+  int64_t oi_seg, oi_sseg;   /* image row t lands at (t / oi_seg) * oi_sseg + (t % oi_seg) * oi_st */
+  void* out_txt; int64_t ot_sb, ot_st, ot_sh;
+  float* lse;
+  int32_t* dev_status;
+} hyb_attn_args;
+int hyb_attn_fwd(const hyb_attn_args* args, void* stream);
+
+/* Ring merge of two partial attentions (fp32 LSE in natural log):
+ * lse = log(exp(lse_a) + exp(lse_b)); out = out_a * exp(lse_a - lse) + out_b * exp(lse_b - lse).
+ * out_acc/lse_acc [rows, H, D]/[H, rows] are updated in place with (out_b, lse_b). */
+int hyb_lse_merge(int32_t rows, int32_t H, int32_t D,
+                  float* out_acc, float* lse_acc, const void* out_b, int32_t out_b_fmt,
+                  const float* lse_b, void* stream);
+
+/* Ulysses send-side pack (sequence -> heads): q, k, v bf16 [B, Ls, H, D] -> send buffer
+ * [P, Ls_max, nsrc*B, H/P, D] (the all_to_all_qkv layout, padding rows zeroed).
+ * k == v == NULL packs q alone (nsrc = 1, the all_to_all_4D(scatter 2, gather 1) layout). */
+int hyb_ulysses_pack_qkv(int32_t P, int32_t B, int32_t Ls, int32_t Ls_max, int32_t H, int32_t D,
+                         const hyb_tensor4* q, const hyb_tensor4* k, const hyb_tensor4* v,
+                         void* send, void* stream);
+
+/* Ulysses send-side pack of O (heads -> sequence): x bf16 [B, L, H/P, D] with
+ * L = sum(lens[0..P)) -> send buffer [P, H/P, Ls_max, B, D], padding rows zeroed. */
+int hyb_ulysses_pack_o(int32_t P, int32_t B, const int32_t* lens, int32_t Ls_max, int32_t Hp, int32_t D,
+                       const hyb_tensor4* x, void* send, void* stream);
+
+/* Ulysses receive-side unpack of O: recv [P, H/P, Ls_max, B, D] -> out [B, Ls, H, D] strided. */
+int hyb_ulysses_unpack_o(int32_t P, int32_t B, int32_t Ls, int32_t Ls_max, int32_t H, int32_t D,
+                         const void* recv, void* out, int64_t o_sb, int64_t o_st, int64_t o_sh,
+                         void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HYB200_H_ */

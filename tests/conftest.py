@@ -1,0 +1,41 @@
+"""Shared test setup: the ``gpu`` marker, repo import path and golden-fixture loaders."""
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parent.parent
+GOLDEN = Path(__file__).resolve().parent / "golden"
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100) GPU and the built libhyb200.so")
+
+
+def load_golden(name: str) -> dict:
+    with np.load(GOLDEN / name, allow_pickle=False) as z:
+        return {k: z[k] for k in z.files}
+
+
+def bf16(a: np.ndarray) -> torch.Tensor:
+    """int16 bit patterns -> bf16 tensor."""
+    return torch.from_numpy(np.ascontiguousarray(a)).view(torch.bfloat16)
+
+
+def e4m3(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).view(torch.float8_e4m3fn)
+
+
+@pytest.fixture(scope="session")
+def cuda_lib():
+    """The built library on an sm_100 device (GPU tests only)."""
+    from hy_nomas_b200 import _lib
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test run without a CUDA device")
+    lib = _lib.load()
+    assert lib.hyb_device_supported() == 1, "libhyb200 needs an sm_100 device"
+    return lib

@@ -1,0 +1,298 @@
+#!/usr/bin/env python
+"""Generate the golden fixtures of tests/golden/ by running the Hy-Nomas reference.
+
+Run in a container that has the reference checkout (default ``/root/reference``,
+override with ``HY_NOMAS_REF``):
+
+    python tests/golden/make_golden.py
+
+The reference's DiT module imports ``diffusers`` only for two base classes; a 10-line
+stub package written to a temporary directory stands in for it.  Every fixture stores
+its inputs and the reference's outputs (bf16 as int16 bit patterns, e4m3 as uint8):
+
+  quant_int8.npz        quantize_kv_pair_into / dequantize_kv, CPU branch
+                        (hymm/models/dit/modules/int8_kv_cache.py:161-205)
+  attn_<case>.npz       causal_attention_with_cache_mp(attn_mode="torch")
+                        (hymm/models/dit/nomas_cpt.py:335-884): INT8 caches (O1), a bf16
+                        cache of decoded E4M3 values (O2), frame-causal via one reference
+                        call per query frame (O3), CFG history broadcast, cache writes
+  sp_<case>.npz         all_to_all_qkv / all_to_all_4D / all_gather over 2 gloo ranks
+                        (hymm/distributed/communications.py)
+  ring_merge.npz        flash_attn_fwd_out_correction / _softmax_lse_correction
+                        (attention/dynamic_ring_attention.py:86-105), eager bodies
+  window_slide.npz      SelfForcingTrainingPipeline._slide_kv_cache sink + window eviction
+                        (hymm/models/self_forcing/causal_training_pipeline.py:203-236)
+"""
+from __future__ import annotations
+
+import importlib
+import os
+import sys
+import tempfile
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+REF = Path(os.environ.get("HY_NOMAS_REF", "/root/reference"))
+
+
+def _install_stub() -> None:
+    stub = Path(tempfile.mkdtemp(prefix="hyb_stub_"))
+    (stub / "diffusers" / "models").mkdir(parents=True)
+    (stub / "diffusers" / "__init__.py").write_text("")
+    (stub / "diffusers" / "models" / "__init__.py").write_text(
+        "import torch.nn as nn\nclass ModelMixin(nn.Module):\n    pass\n")
+    (stub / "diffusers" / "configuration_utils.py").write_text(
+        "class ConfigMixin:\n    pass\ndef register_to_config(fn):\n    return fn\n")
+    sys.path.insert(0, str(stub))
+    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(REPO))
+
+
+def bf(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy()
+
+
+def seeded(shape, gen):
+    from hy_nomas_b200.synthetic import seeded_kv
+    return seeded_kv(shape, gen)
+
+
+def make_quant():
+    i8 = importlib.import_module("hymm.models.dit.modules.int8_kv_cache")
+    gen = torch.Generator().manual_seed(7)
+    k = seeded((1, 40, 3, 128), gen)
+    v = seeded((1, 40, 3, 128), gen)
+    k[0, 0] = 0                        # all-zero rows -> scale 1
+    v[0, 1, 1] = 0
+    k[0, 2] *= 1e-30                   # tiny values (subnormal codes)
+    v[0, 3] *= 4096.0                  # large values
+    k[0, 4, 0, :] = torch.linspace(-127.5, 127.5, 128).to(torch.bfloat16)  # exact .5 ties
+    cache = i8.make_int8_kv_block(1, 48, 3, 128, device="cpu")
+    start = 5
+    i8.quantize_kv_pair_into(cache, k, v, start)
+    dk = i8.dequantize_kv(cache, "k", start + 40)
+    dv = i8.dequantize_kv(cache, "v", start + 40)
+    np.savez_compressed(
+        HERE / "quant_int8.npz", k=bf(k), v=bf(v), start=start,
+        k_codes=cache["k"][:, start:start + 40].numpy(), v_codes=cache["v"][:, start:start + 40].numpy(),
+        k_scale=cache["k_scale"][:, start:start + 40].numpy(),
+        v_scale=cache["v_scale"][:, start:start + 40].numpy(),
+        k_deq=bf(dk[:, start:]), v_deq=bf(dv[:, start:]))
+
+
+def _call_ref(native, **kw):
+    with torch.no_grad():
+        return native.causal_attention_with_cache_mp(attn_mode="torch", **kw)
+
+
+def make_attention():
+    native = importlib.import_module("hymm.models.dit.nomas_cpt")
+    i8 = importlib.import_module("hymm.models.dit.modules.int8_kv_cache")
+    sys.path.insert(0, str(REPO))
+    from oracle.quant import quantize_e4m3, dequantize
+
+    H, D = 2, 128
+
+    def chunk(B, Li, Lt, gen):
+        return [seeded((B, L, H, D), gen) for L in (Li, Lt) for _ in range(3)]
+
+    def int8_cache(Bc, cap, Lh, gen):
+        cache = i8.make_int8_kv_block(Bc, cap, H, D, device="cpu")
+        hk, hv = seeded((Bc, Lh, H, D), gen), seeded((Bc, Lh, H, D), gen)
+        i8.quantize_kv_pair_into(cache, hk, hv, 0)
+        return cache
+
+    def save(name, cache, args, out, extra=None):
+        img_q, img_k, img_v, txt_q, txt_k, txt_v = args
+        d = dict(img_q=bf(img_q), img_k=bf(img_k), img_v=bf(img_v),
+                 txt_q=bf(txt_q), txt_k=bf(txt_k), txt_v=bf(txt_v),
+                 out_img=bf(out[0]), out_txt=bf(out[1]))
+        if cache["k"].dtype == torch.int8:
+            d.update(hist_k=cache["k"].numpy(), hist_v=cache["v"].numpy(),
+                     hist_k_scale=cache["k_scale"].numpy(), hist_v_scale=cache["v_scale"].numpy(),
+                     fmt="int8")
+        d.update(extra or {})
+        np.savez_compressed(HERE / f"attn_{name}.npz", **d)
+
+    def run_case(name, B, Bc, Lh, Li, Lt, text_mask, cache_mask_holes, update_cache, cache_txt, seed):
+        gen = torch.Generator().manual_seed(seed)
+        cap = Lh + Li + Lt + 16
+        cache = int8_cache(Bc, cap, Lh, gen)
+        args = chunk(B, Li, Lt, gen)
+        cmask = torch.zeros(Bc, cap, dtype=torch.bool)
+        cmask[:, :Lh] = True
+        for a, b in cache_mask_holes:
+            cmask[:, a:b] = False
+        tmask = torch.tensor(text_mask, dtype=torch.bool).reshape(B, Lt)
+        before = {k: v.clone() for k, v in cache.items()}
+        mask_before = cmask.clone()
+        out = _call_ref(native, q=(args[0], args[3]), k=(args[1], args[4]), v=(args[2], args[5]),
+                        kv_cache=cache, cache_valid_len=Lh, text_mask=tmask,
+                        update_cache=update_cache, cache_txt=cache_txt, cache_mask=cmask)
+        out = (out[0].reshape(B, Li, H, D), out[1].reshape(B, Lt, H, D))
+        extra = dict(Lh=Lh, cache_mask=mask_before.numpy(), text_mask=tmask.numpy(),
+                     update_cache=update_cache, cache_txt=cache_txt, cap=cap,
+                     cache_mask_after=cmask.numpy())
+        if update_cache:
+            extra.update(written_k=cache["k"].numpy(), written_v=cache["v"].numpy(),
+                         written_k_scale=cache["k_scale"].numpy(), written_v_scale=cache["v_scale"].numpy())
+        save(name, before, args, out, extra)
+
+    # O1: INT8 cache, reference-exact path (kv_mask honoured in torch mode for int8).
+    run_case("int8_basic", 1, 1, 96, 64, 4, [1, 1, 1, 0], [(10, 21)], False, True, 11)
+    run_case("int8_update", 1, 1, 96, 64, 4, [1, 1, 0, 1], [(40, 45)], True, True, 12)
+    run_case("int8_nocachetxt", 1, 1, 80, 48, 3, [1, 1, 1], [], False, False, 13)
+    run_case("int8_update_nocachetxt", 1, 1, 80, 48, 3, [1, 0, 1], [], True, False, 14)
+    run_case("int8_cfg", 2, 1, 64, 32, 2, [1, 1, 1, 0], [(0, 5)], False, True, 15)
+    run_case("int8_empty_history", 1, 1, 0, 48, 2, [1, 1], [], False, True, 16)
+
+    # O2: E4M3 codes (restated quantiser) decoded into a bf16 cache; torch mode ignores
+    # kv_mask for a bf16 cache, so every key is valid here.
+    gen = torch.Generator().manual_seed(21)
+    Lh, Li, Lt, B = 128, 64, 1, 1
+    hk, hv = seeded((1, Lh, H, D), gen), seeded((1, Lh, H, D), gen)
+    ck, sk = quantize_e4m3(hk)
+    cv, sv = quantize_e4m3(hv)
+    cache = {"k": torch.zeros(1, Lh + Li + Lt, H, D, dtype=torch.bfloat16),
+             "v": torch.zeros(1, Lh + Li + Lt, H, D, dtype=torch.bfloat16)}
+    cache["k"][:, :Lh] = dequantize(ck, sk)
+    cache["v"][:, :Lh] = dequantize(cv, sv)
+    args = chunk(B, Li, Lt, gen)
+    out = _call_ref(native, q=(args[0], args[3]), k=(args[1], args[4]), v=(args[2], args[5]),
+                    kv_cache=cache, cache_valid_len=Lh, text_mask=None, update_cache=False,
+                    cache_txt=True, cache_mask=None)
+    out = (out[0].reshape(B, Li, H, D), out[1].reshape(B, Lt, H, D))
+    np.savez_compressed(
+        HERE / "attn_fp8_o2.npz", fmt="fp8_e4m3", Lh=Lh, hist_k=ck.view(torch.uint8).numpy(),
+        hist_v=cv.view(torch.uint8).numpy(), hist_k_scale=sk.numpy(), hist_v_scale=sv.numpy(),
+        hist_k_raw=bf(hk), hist_v_raw=bf(hv),
+        img_q=bf(args[0]), img_k=bf(args[1]), img_v=bf(args[2]), txt_q=bf(args[3]),
+        txt_k=bf(args[4]), txt_v=bf(args[5]), out_img=bf(out[0]), out_txt=bf(out[1]))
+
+    # O3: frame-level block-causal = one reference call per query frame, history advanced
+    # by the chunk's earlier frames (bf16 cache of decoded INT8 history + raw frames).
+    gen = torch.Generator().manual_seed(31)
+    T, F, Lh, Lt, B = 16, 3, 64, 1, 1
+    Li = T * F
+    cache8 = int8_cache(1, Lh + Li + Lt + 8, Lh, gen)
+    args = chunk(B, Li, Lt, gen)
+    hist_k = i8.dequantize_kv(cache8, "k", Lh)
+    hist_v = i8.dequantize_kv(cache8, "v", Lh)
+    out_img = torch.zeros(B, Li, H, D, dtype=torch.bfloat16)
+    out_txt = None
+    for f in range(F):
+        prev = f * T
+        cap = Lh + prev + T + Lt
+        c = {"k": torch.zeros(1, cap, H, D, dtype=torch.bfloat16),
+             "v": torch.zeros(1, cap, H, D, dtype=torch.bfloat16)}
+        c["k"][:, :Lh] = hist_k
+        c["v"][:, :Lh] = hist_v
+        c["k"][:, Lh:Lh + prev] = args[1][:, :prev]
+        c["v"][:, Lh:Lh + prev] = args[2][:, :prev]
+        sl = slice(prev, prev + T)
+        o = _call_ref(native, q=(args[0][:, sl], args[3]), k=(args[1][:, sl], args[4]),
+                      v=(args[2][:, sl], args[5]), kv_cache=c, cache_valid_len=Lh + prev,
+                      text_mask=None, update_cache=False, cache_txt=True, cache_mask=None)
+        out_img[:, sl] = o[0].reshape(B, T, H, D)
+        if f == F - 1:
+            # text queries see every frame: take them from a call over the whole chunk
+            c2 = {"k": torch.zeros(1, Lh + Li + Lt, H, D, dtype=torch.bfloat16),
+                  "v": torch.zeros(1, Lh + Li + Lt, H, D, dtype=torch.bfloat16)}
+            c2["k"][:, :Lh] = hist_k
+            c2["v"][:, :Lh] = hist_v
+            o2 = _call_ref(native, q=(args[0], args[3]), k=(args[1], args[4]), v=(args[2], args[5]),
+                           kv_cache=c2, cache_valid_len=Lh, text_mask=None, update_cache=False,
+                           cache_txt=True, cache_mask=None)
+            out_txt = o2[1].reshape(B, Lt, H, D)
+    np.savez_compressed(
+        HERE / "attn_frame_causal_o3.npz", fmt="int8", Lh=Lh, tokens_per_frame=T, frames=F,
+        hist_k=cache8["k"].numpy(), hist_v=cache8["v"].numpy(), hist_k_scale=cache8["k_scale"].numpy(),
+        hist_v_scale=cache8["v_scale"].numpy(),
+        img_q=bf(args[0]), img_k=bf(args[1]), img_v=bf(args[2]), txt_q=bf(args[3]),
+        txt_k=bf(args[4]), txt_v=bf(args[5]), out_img=bf(out_img), out_txt=bf(out_txt))
+
+
+def _sp_worker(rank, world, init_file, out_dir):
+    import torch.distributed as dist
+    _install_stub()
+    comm = importlib.import_module("hymm.distributed.communications")
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+    H, D, B = 4, 128, 1
+    res = {}
+    for case, lens in (("even", (6, 6)), ("uneven", (5, 3))):
+        gen = torch.Generator().manual_seed(100 + rank)
+        q, k, v = (torch.randn(B, lens[rank], H, D, generator=gen).to(torch.bfloat16) for _ in range(3))
+        meta = comm.prepare_sp_communication(lens[rank], H, "cpu", None)
+        oq, ok, ov = comm.all_to_all_qkv(q, k, v, group=None, sequence_lengths=meta.sequence_lengths)
+        o_in = torch.randn(B, sum(lens), H // world, D, generator=gen).to(torch.bfloat16)
+        o_out = comm.all_to_all_4D(o_in, group=None, scatter_dim=1, gather_dim=2,
+                                   sequence_lengths=meta.sequence_lengths)
+        t_in = torch.randn(B, 3, H // world, D, generator=gen).to(torch.bfloat16)
+        t_out = comm.all_gather(t_in, dim=2, group=None, sizes=meta.head_sizes)
+        res.update({f"{case}_q": bf(q), f"{case}_k": bf(k), f"{case}_v": bf(v),
+                    f"{case}_oq": bf(oq), f"{case}_ok": bf(ok), f"{case}_ov": bf(ov),
+                    f"{case}_o_in": bf(o_in), f"{case}_o_out": bf(o_out),
+                    f"{case}_t_in": bf(t_in), f"{case}_t_out": bf(t_out),
+                    f"{case}_lens": np.array(lens)})
+    np.savez_compressed(Path(out_dir) / f"sp_rank{rank}.npz", **res)
+    dist.destroy_process_group()
+
+
+def make_sp():
+    import torch.multiprocessing as mp
+    init_file = tempfile.mktemp(prefix="hyb_gloo_")
+    mp.spawn(_sp_worker, args=(2, init_file, str(HERE)), nprocs=2, join=True)
+
+
+def make_ring_merge():
+    dra = importlib.import_module("hymm.models.dit.modules.attention.dynamic_ring_attention")
+    out_fn = dra.flash_attn_fwd_out_correction.__wrapped__
+    lse_fn = dra.flash_attn_fwd_softmax_lse_correction.__wrapped__
+    gen = torch.Generator().manual_seed(41)
+    S, H, D = 24, 3, 128
+    out_a = torch.randn(1, S, H, D, generator=gen, dtype=torch.float64)
+    lse_a = torch.randn(H, S, generator=gen, dtype=torch.float64) * 3
+    out_b = torch.randn(1, S, H, D, generator=gen, dtype=torch.float64)
+    lse_b = torch.randn(H, S, generator=gen, dtype=torch.float64) * 3
+    lse_b[0, :4] = float("-inf")       # rows a step could not see
+    lse = lse_a.clone()
+    lse_fn(lse, lse_b)
+    # The reference rescales every step's output by its own lse against the final lse.
+    out = torch.zeros_like(out_a)
+    out_fn(out, out_a, 1, lse, lse_a)   # bshd, seq_dim = 1 (dynamic_ring_attention.py:253-262)
+    out_fn(out, out_b, 1, lse, lse_b)
+    np.savez_compressed(HERE / "ring_merge.npz", out_a=out_a.numpy(), lse_a=lse_a.numpy(),
+                        out_b=out_b.numpy(), lse_b=lse_b.numpy(), lse=lse.numpy(), out=out.numpy())
+
+
+def make_window():
+    ctp = importlib.import_module("hymm.models.self_forcing.causal_training_pipeline")
+    T, frames, sink, keep = 4, 12, 1, 5
+    k = torch.arange(frames * T, dtype=torch.float32).reshape(1, frames * T, 1, 1).repeat(1, 1, 2, 1)
+    ns = types.SimpleNamespace(kv_cache1=[{"k": k.clone(), "v": (k + 1000).clone()}], sink_frames=sink,
+                               cache_keep_frames=keep, _tokens_per_frame=T, num_max_frames=frames)
+    new_count = ctp.SelfForcingTrainingPipeline._slide_kv_cache(ns, frames)
+    np.savez_compressed(HERE / "window_slide.npz", tokens_per_frame=T, frames=frames, sink=sink, keep=keep,
+                        new_count=new_count, k_after=ns.kv_cache1[0]["k"].numpy(),
+                        v_after=ns.kv_cache1[0]["v"].numpy())
+
+
+def main():
+    _install_stub()
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    if "--only-late" not in sys.argv:
+        make_quant()
+        make_attention()
+    make_ring_merge()
+    make_window()
+    make_sp()
+    print("fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

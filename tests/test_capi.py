@@ -1,0 +1,123 @@
+"""The C ABI without a GPU: the library loads, exports every symbol the header declares,
+the ctypes mirrors have the C struct layouts, and argument errors come back as status
+codes (no device work is attempted for rejected calls)."""
+import ctypes
+import re
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+import torch
+
+from hy_nomas_b200 import _lib
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "hyb200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(hyb_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 12
+    for name in names:
+        assert hasattr(lib, name), f"{name} missing from libhyb200.so"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert lib.hyb_version() == _lib.HYB_ABI_VERSION
+
+
+LAYOUT_C = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "hyb200.h"
+#define F(T, m) printf(#T "." #m " %zu\n", offsetof(T, m));
+int main(void) {
+  printf("hyb_tensor4 %zu\n", sizeof(hyb_tensor4));
+  printf("hyb_cached_attn_args %zu\n", sizeof(hyb_cached_attn_args));
+  printf("hyb_attn_args %zu\n", sizeof(hyb_attn_args));
+  F(hyb_tensor4, scale) F(hyb_tensor4, ss_h)
+  F(hyb_cached_attn_args, softmax_scale) F(hyb_cached_attn_args, hist_k) F(hyb_cached_attn_args, txt_v)
+  F(hyb_cached_attn_args, hist_rows) F(hyb_cached_attn_args, cache_mask) F(hyb_cached_attn_args, oi_seg)
+  F(hyb_cached_attn_args, out_txt) F(hyb_cached_attn_args, lse) F(hyb_cached_attn_args, workspace_bytes)
+  F(hyb_cached_attn_args, dev_status)
+  F(hyb_attn_args, q) F(hyb_attn_args, kwords) F(hyb_attn_args, qbits) F(hyb_attn_args, oi_sseg)
+  F(hyb_attn_args, lse) F(hyb_attn_args, dev_status)
+  return 0;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_ctypes_layouts_match_c(tmp_path):
+    src = tmp_path / "layout.c"
+    src.write_text(LAYOUT_C)
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    c = dict(line.rsplit(" ", 1) for line in out.strip().splitlines())
+    types = {"hyb_tensor4": _lib.Tensor4, "hyb_cached_attn_args": _lib.CachedAttnArgs,
+             "hyb_attn_args": _lib.AttnArgs}
+    for key, val in c.items():
+        if "." in key:
+            t, m = key.split(".")
+            assert getattr(types[t], m).offset == int(val), key
+        else:
+            assert ctypes.sizeof(types[key]) == int(val), key
+
+
+def test_status_codes_for_rejected_calls():
+    lib = _lib.load()
+    x = _lib.Tensor4(16, _lib.HYB_FMT_BF16, 0, 8, 8, 8, None, 0, 0, 0)
+    # head_dim other than 128 is unsupported
+    rc = lib.hyb_kv_append_pair(_lib.HYB_FMT_E4M3, 1, 4, 1, 64, 8, 0, x, x, 16, 16, 8, 8, 8,
+                                16, 16, 1, 1, 1, None, None)
+    assert rc == _lib.HYB_ERR_UNSUPPORTED and "head_dim" in _lib.last_error()
+    # writing past the capacity is a capacity error (ValueError in Python)
+    rc = lib.hyb_kv_append_pair(_lib.HYB_FMT_INT8, 1, 4, 1, 128, 8, 6, x, x, 16, 16, 8, 8, 8,
+                                16, 16, 1, 1, 1, None, None)
+    assert rc == _lib.HYB_ERR_CAPACITY
+    with pytest.raises(ValueError):
+        _lib.check(rc, "KV quantization")
+    # bf16 is not a quantised storage format
+    rc = lib.hyb_kv_append_pair(_lib.HYB_FMT_BF16, 1, 4, 1, 128, 8, 0, x, x, 16, 16, 8, 8, 8,
+                                16, 16, 1, 1, 1, None, None)
+    assert rc == _lib.HYB_ERR_UNSUPPORTED
+    # SP head counts must divide
+    rc = lib.hyb_ulysses_pack_qkv(3, 1, 4, 4, 8, 128, x, x, x, 16, None)
+    assert rc == _lib.HYB_ERR_INVALID_ARG
+    assert lib.hyb_cached_attention_workspace_bytes(1, 2, 64, 10, 10, 1, 1) == -1
+    assert lib.hyb_cached_attention_workspace_bytes(1, 2, 128, 10, 10, 1, 1) > 0
+    args = _lib.CachedAttnArgs()
+    args.abi_version = 99
+    assert lib.hyb_cached_attention(args, None) == _lib.HYB_ERR_INVALID_ARG
+
+
+def test_workspace_size_formula():
+    lib = _lib.load()
+    B, H, Lh, Li, Lt = 1, 24, 24960, 6240, 1
+    ws = lib.hyb_cached_attention_workspace_bytes(B, H, 128, Lh, Li, Lt, 1)
+    Lk, Lq = Lh + Li + Lt, Li + Lt
+    assert ws >= B * H * (Lq + 2 * Lk) * 128 * 2
+    assert ws < B * H * (Lq + 2 * Lk) * 128 * 2 + 1 << 20
+
+
+def test_no_device_is_reported_not_faked():
+    lib = _lib.load()
+    if torch.cuda.is_available():
+        pytest.skip("CPU-only check")
+    assert lib.hyb_device_supported() == 0
+
+
+def test_python_workspace_layout_mirrors_c():
+    from hy_nomas_b200.attention import workspace_layout
+    lib = _lib.load()
+    for args in [(1, 24, 24960, 6240, 1, 1), (2, 3, 0, 130, 2, 0), (1, 1, 7, 1, 0, 1), (3, 5, 1000, 384, 9, 1)]:
+        B, H, Lh, Li, Lt, att = args
+        assert workspace_layout(B, H, Lh, Li, Lt, att)["total"] == \
+            lib.hyb_cached_attention_workspace_bytes(B, H, 128, Lh, Li, Lt, att)

@@ -1,0 +1,252 @@
+"""The tcgen05 cached-attention kernel against the oracle and the reference's outputs.
+
+Tolerances.  The north star asks for max-abs-err 2e-2 and cosine >= 0.9995.  The
+attention output is bf16 (the reference returns the input dtype), and with the
+benchmark's x8 outlier channels outputs reach |o| ~ 15, where one bf16 ulp is 0.0625;
+no bf16 output can be within 2e-2 of the exact value there.  The bound used is therefore
+elementwise |out - ref| <= 2e-2 + 2^-7 * |ref| (2e-2 plus one bf16 output ulp) together
+with cosine >= 0.9995 over all valid rows, against the fp32 oracle on the same decoded
+inputs.  Against the reference's own bf16 outputs (golden fixtures), which carry their
+own bf16 rounding, the relative term is 1e-2.  Padded text query rows are exactly zero."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16, e4m3, load_golden
+from hy_nomas_b200 import attention as hatt
+from hy_nomas_b200 import kv_cache as kvc
+from hy_nomas_b200.synthetic import make_generator, seeded_kv
+from oracle import attention as oatt
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+RTOL = 2.0 ** -7       # one bf16 ulp of the reference value
+COS = 0.9995
+
+
+def errs(out: torch.Tensor, ref: torch.Tensor):
+    o = out.float().flatten().cpu()
+    r = ref.float().flatten().cpu()
+    mae = (o - r).abs().max().item() if o.numel() else 0.0
+    cos = torch.nn.functional.cosine_similarity(o[None], r[None]).item() if o.numel() else 1.0
+    return mae, cos
+
+
+def assert_close(out, ref, what=""):
+    mae, cos = errs(out, ref)
+    o = out.float().flatten().cpu()
+    r = ref.float().flatten().cpu()
+    excess = ((o - r).abs() - (ATOL + RTOL * r.abs())).max().item() if o.numel() else -1.0
+    assert excess <= 0 and cos >= COS, (
+        f"{what}: max_abs_err={mae:.3e} excess_over_bound={excess:.3e} cos={cos:.6f}")
+
+
+def make_case(B, Bc, Lh, Li, Lt, H, fmt, seed, cap_extra=8):
+    gen = make_generator(seed)
+    hk = seeded_kv((Bc, Lh, H, 128), gen)
+    hv = seeded_kv((Bc, Lh, H, 128), gen)
+    cur = [seeded_kv((B, L, H, 128), gen) for L in (Li, Lt) for _ in range(3)]
+    cap = Lh + Li + Lt + cap_extra
+    if fmt == "bf16":
+        cache = {"k": torch.zeros(Bc, cap, H, 128, dtype=torch.bfloat16),
+                 "v": torch.zeros(Bc, cap, H, 128, dtype=torch.bfloat16)}
+        cache["k"][:, :Lh] = hk
+        cache["v"][:, :Lh] = hv
+        dk, dv = hk, hv
+    else:
+        ck, sk = oq.quantize(hk, fmt)
+        cv, sv = oq.quantize(hv, fmt)
+        dt = torch.int8 if fmt == "int8" else torch.float8_e4m3fn
+        cache = {"k": torch.zeros(Bc, cap, H, 128, dtype=dt), "v": torch.zeros(Bc, cap, H, 128, dtype=dt),
+                 "k_scale": torch.ones(Bc, cap, H, 1), "v_scale": torch.ones(Bc, cap, H, 1)}
+        cache["k"][:, :Lh], cache["v"][:, :Lh] = ck, cv
+        cache["k_scale"][:, :Lh], cache["v_scale"][:, :Lh] = sk, sv
+        if fmt == "fp8_e4m3":
+            cache["storage_format"] = "fp8_e4m3"
+        dk, dv = oq.dequantize(ck, sk), oq.dequantize(cv, sv)
+    return cache, cur, dk, dv
+
+
+def to_dev(cache, dev):
+    return {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in cache.items()}
+
+
+CASES = [
+    # B, Bc, Lh,   Li,  Lt, H, fmt,        G,   text_mask,        hist holes
+    (1, 1, 256, 128, 1, 2, "fp8_e4m3", 0, None, []),
+    (1, 1, 300, 200, 3, 2, "fp8_e4m3", 50, [1, 0, 1], [(5, 9)]),
+    (1, 1, 0, 130, 2, 1, "int8", 0, [1, 1], []),
+    (1, 1, 1000, 384, 1, 3, "int8", 128, None, [(100, 356)]),
+    (2, 1, 513, 257, 4, 2, "fp8_e4m3", 64, [1, 1, 0, 0, 1, 0, 1, 1], [(0, 1)]),
+    (2, 2, 129, 64, 1, 2, "bf16", 16, None, []),
+    (1, 1, 64, 1, 1, 1, "fp8_e4m3", 0, None, []),
+    (1, 1, 4096, 1560, 1, 2, "fp8_e4m3", 390, None, []),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
+def test_cached_attention_vs_oracle(cuda_lib, case):
+    B, Bc, Lh, Li, Lt, H, fmt, G, tmask, holes = case
+    dev = torch.device("cuda")
+    cache, cur, dk, dv = make_case(B, Bc, Lh, Li, Lt, H, fmt, seed=100 + CASES.index(case))
+    hmask = torch.ones(Bc, Lh, dtype=torch.bool)
+    for a, b in holes:
+        hmask[:, a:b] = False
+    text_mask = torch.tensor(tmask, dtype=torch.bool).reshape(B, Lt) if tmask else None
+    lse = torch.empty(B, H, Li + Lt, dtype=torch.float32, device=dev)
+    out_img, out_txt = hatt.cached_attention_local(
+        *(t.to(dev) for t in cur), to_dev(cache, dev), Lh,
+        history_mask=hmask.to(dev), text_mask=text_mask.to(dev) if text_mask is not None else None,
+        attend_txt=True, group_tokens=G, lse=lse)
+    torch.cuda.synchronize()
+    from hy_nomas_b200 import _lib
+    _lib.check_device_status(dev)
+    ref_img, ref_txt, ref_lse = oatt.cached_attention(
+        *cur, dk, dv, history_mask=hmask, text_mask=text_mask, group_tokens=G, return_lse=True)
+    assert_close(out_img, ref_img, "image rows")
+    if Lt:
+        valid = text_mask if text_mask is not None else torch.ones(B, Lt, dtype=torch.bool)
+        assert_close(out_txt.cpu()[valid], ref_txt[valid], "text rows")
+        assert torch.all(out_txt.cpu()[~valid] == 0)
+    fin = torch.isfinite(ref_lse)
+    assert torch.equal(torch.isfinite(lse.cpu()), fin)
+    assert (lse.cpu()[fin] - ref_lse[fin]).abs().max() < 1e-3
+
+
+GOLDEN_CASES = ["int8_basic", "int8_update", "int8_nocachetxt", "int8_update_nocachetxt",
+                "int8_cfg", "int8_empty_history"]
+
+
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+def test_drop_in_matches_reference_outputs(cuda_lib, case):
+    g = load_golden(f"attn_{case}.npz")
+    dev = torch.device("cuda")
+    Lh = int(g["Lh"])
+    update, cache_txt = bool(g["update_cache"]), bool(g["cache_txt"])
+    cache = {"k": torch.from_numpy(g["hist_k"]).to(dev), "v": torch.from_numpy(g["hist_v"]).to(dev),
+             "k_scale": torch.from_numpy(g["hist_k_scale"]).to(dev),
+             "v_scale": torch.from_numpy(g["hist_v_scale"]).to(dev)}
+    cmask = torch.from_numpy(g["cache_mask"]).to(dev)
+    tmask = torch.from_numpy(g["text_mask"]).to(dev)
+    q = (bf16(g["img_q"]).to(dev), bf16(g["txt_q"]).to(dev))
+    k = (bf16(g["img_k"]).to(dev), bf16(g["txt_k"]).to(dev))
+    v = (bf16(g["img_v"]).to(dev), bf16(g["txt_v"]).to(dev))
+    with torch.no_grad():
+        out_img, out_txt = hatt.causal_attention_with_cache_mp(
+            q, k, v, cache, cache_valid_len=Lh, attn_mode="flash3", text_mask=tmask,
+            update_cache=update, cache_txt=cache_txt, cache_mask=cmask)
+    torch.cuda.synchronize()
+    B, Li, H, D = g["img_q"].shape
+    Lt = g["txt_q"].shape[1]
+    ref_img = bf16(g["out_img"]).float()
+    ref_txt = bf16(g["out_txt"]).float()
+    out_img = out_img.reshape(B, Li, H, D).float().cpu()
+    out_txt = out_txt.reshape(B, Lt, H, D).float().cpu()
+    assert ((out_img - ref_img).abs() <= ATOL + 1e-2 * ref_img.abs()).all()
+    valid = torch.from_numpy(g["text_mask"])
+    assert ((out_txt[valid] - ref_txt[valid]).abs() <= ATOL + 1e-2 * ref_txt[valid].abs()).all()
+    assert torch.all(out_txt[~valid] == 0)
+    if update:
+        n = Li + (Lt if cache_txt else 0)
+        for key in ("k", "v"):
+            assert np.array_equal(cache[key][:, Lh:Lh + n].cpu().numpy(), g[f"written_{key}"][:, Lh:Lh + n])
+            assert np.array_equal(cache[f"{key}_scale"][:, Lh:Lh + n].cpu().numpy().view(np.int32),
+                                  g[f"written_{key}_scale"][:, Lh:Lh + n].view(np.int32))
+        assert np.array_equal(cmask.cpu().numpy(), g["cache_mask_after"])
+
+
+def test_frame_causal_matches_per_frame_reference_calls(cuda_lib):
+    g = load_golden("attn_frame_causal_o3.npz")
+    dev = torch.device("cuda")
+    Lh, T, F = int(g["Lh"]), int(g["tokens_per_frame"]), int(g["frames"])
+    cache = {"k": torch.from_numpy(g["hist_k"]).to(dev), "v": torch.from_numpy(g["hist_v"]).to(dev),
+             "k_scale": torch.from_numpy(g["hist_k_scale"]).to(dev),
+             "v_scale": torch.from_numpy(g["hist_v_scale"]).to(dev)}
+    q = (bf16(g["img_q"]).to(dev), bf16(g["txt_q"]).to(dev))
+    k = (bf16(g["img_k"]).to(dev), bf16(g["txt_k"]).to(dev))
+    v = (bf16(g["img_v"]).to(dev), bf16(g["txt_v"]).to(dev))
+    with torch.no_grad():
+        out_img, out_txt = hatt.causal_attention_with_cache_mp(
+            q, k, v, cache, cache_valid_len=Lh, attn_mode="flash3", tokens_per_frame=T,
+            chunk_causal_frames=1)
+    B, Li, H, D = g["img_q"].shape
+    ref_img = bf16(g["out_img"]).float()
+    got = out_img.reshape(B, Li, H, D).float().cpu()
+    assert ((got - ref_img).abs() <= ATOL + 1e-2 * ref_img.abs()).all()
+    ref_txt = bf16(g["out_txt"]).float()
+    got_t = out_txt.reshape(ref_txt.shape).float().cpu()
+    assert ((got_t - ref_txt).abs() <= ATOL + 1e-2 * ref_txt.abs()).all()
+
+
+def test_fp8_drop_in_matches_o2_reference(cuda_lib):
+    g = load_golden("attn_fp8_o2.npz")
+    dev = torch.device("cuda")
+    Lh = int(g["Lh"])
+    cap = Lh + 80
+    cache = kvc.make_fp8_kv_block(1, cap, 2, 128, device=dev)
+    cache["k"][:, :Lh] = e4m3(g["hist_k"]).to(dev)
+    cache["v"][:, :Lh] = e4m3(g["hist_v"]).to(dev)
+    cache["k_scale"][:, :Lh] = torch.from_numpy(g["hist_k_scale"]).to(dev)
+    cache["v_scale"][:, :Lh] = torch.from_numpy(g["hist_v_scale"]).to(dev)
+    q = (bf16(g["img_q"]).to(dev), bf16(g["txt_q"]).to(dev))
+    k = (bf16(g["img_k"]).to(dev), bf16(g["txt_k"]).to(dev))
+    v = (bf16(g["img_v"]).to(dev), bf16(g["txt_v"]).to(dev))
+    with torch.no_grad():
+        out_img, out_txt = hatt.causal_attention_with_cache_mp(q, k, v, cache, cache_valid_len=Lh,
+                                                               attn_mode="flash3")
+    ref = bf16(g["out_img"]).float()
+    got = out_img.reshape(ref.shape).float().cpu()
+    assert ((got - ref).abs() <= ATOL + 1e-2 * ref.abs()).all()
+
+
+def test_config2_geometry_vs_torch_fp32(cuda_lib):
+    """BASELINE config 2 geometry (history 16 frames x 1560, 4-frame chunk, frame-causal)
+    with 2 of the 24 heads, against an fp32 torch computation on the GPU."""
+    dev = torch.device("cuda")
+    H, T = 2, 1560
+    Lh, Li, Lt = 16 * T, 4 * T, 1
+    cache, cur, dk, dv = make_case(1, 1, Lh, Li, Lt, H, "fp8_e4m3", seed=1236)
+    out_img, out_txt = hatt.cached_attention_local(
+        *(t.to(dev) for t in cur), to_dev(cache, dev), Lh, group_tokens=T)
+    torch.cuda.synchronize()
+    q = torch.cat([cur[0], cur[3]], 1).to(dev).float()
+    k = torch.cat([dk, cur[1], cur[4]], 1).to(dev).float()
+    v = torch.cat([dv, cur[2], cur[5]], 1).to(dev).float()
+    Lq, Lk = q.shape[1], k.shape[1]
+    kpos = torch.arange(Lk, device=dev)
+    qpos = torch.arange(Lq, device=dev)
+    qblk = torch.where(qpos < Li, qpos // T, torch.full_like(qpos, 10 ** 9))
+    kblk = torch.where((kpos >= Lh) & (kpos < Lh + Li), (kpos - Lh) // T, torch.full_like(kpos, -1))
+    mask = kblk[None, :] <= qblk[:, None]
+    ref = torch.empty(Lq, H, 128, device=dev)
+    for h in range(H):
+        s = (q[0, :, h] @ k[0, :, h].T) / (128 ** 0.5)
+        s.masked_fill_(~mask, float("-inf"))
+        ref[:, h] = torch.softmax(s, -1) @ v[0, :, h]
+    assert_close(out_img[0], ref[:Li], "config-2 image rows")
+    assert_close(out_txt[0], ref[Li:], "config-2 text row")
+
+
+def test_ring_history_rows(cuda_lib):
+    """A history given through a row map (sink + sliding window in a frame ring) equals the
+    same rows laid out contiguously."""
+    dev = torch.device("cuda")
+    T, H = 64, 2
+    cache, cur, dk, dv = make_case(1, 1, 10 * T, 2 * T, 1, H, "fp8_e4m3", seed=77)
+    rows = torch.cat([torch.arange(0, T), torch.arange(6 * T, 10 * T), torch.arange(2 * T, 3 * T)]).to(torch.int32)
+    cdev = to_dev(cache, dev)
+    out_a, _ = hatt.cached_attention_local(*(t.to(dev) for t in cur), cdev, rows.numel(),
+                                           hist_rows=rows.to(dev), group_tokens=T)
+    ref_img, _ = oatt.cached_attention(*cur, dk[:, rows.long()], dv[:, rows.long()], group_tokens=T)
+    assert_close(out_a, ref_img, "ring rows")
+
+
+def test_empty_text_and_single_query(cuda_lib):
+    dev = torch.device("cuda")
+    cache, cur, dk, dv = make_case(1, 1, 200, 1, 0, 2, "int8", seed=9)
+    out_img, out_txt = hatt.cached_attention_local(*(t.to(dev) for t in cur), to_dev(cache, dev), 200)
+    ref_img, _ = oatt.cached_attention(*cur, dk, dv)
+    assert out_txt.shape[1] == 0
+    assert_close(out_img, ref_img, "single query")
