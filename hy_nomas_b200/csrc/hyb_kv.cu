@@ -62,9 +62,12 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams p) {
       peak = fmaxf(peak, fabsf(x[i]));
       nonfinite |= !isfinite(x[i]);
     }
+    // The two 16-lane halves of a warp own different rows and may leave the loop on
+    // different iterations, so each half shuffles under its own lane mask.
+    const unsigned half_mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
 #pragma unroll
     for (int off = kRowLanes / 2; off >= 1; off >>= 1)
-      peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, off, kRowLanes));
+      peak = fmaxf(peak, __shfl_xor_sync(half_mask, peak, off, kRowLanes));
     const float denom = (p.fmt == HYB_FMT_INT8) ? 127.0f : 448.0f;
     const float s = peak > 0.f ? __fdiv_rn(peak, denom) : 1.0f;
     const long long dst_off =
