@@ -93,6 +93,7 @@ SIGNATURES = {
     "hyb_device_supported": (c_i32, []),
     "hyb_kv_append_pair": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64,
                                    ctypes.POINTER(Tensor4), ctypes.POINTER(Tensor4),
+                                   c_i32, ctypes.POINTER(Tensor4), ctypes.POINTER(Tensor4),
                                    c_ptr, c_ptr, c_i64, c_i64, c_i64,
                                    c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr]),
     "hyb_check_finite": (c_i32, [ctypes.POINTER(Tensor4), c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),

@@ -315,18 +315,21 @@ def causal_attention_with_cache_mp(
 
     # ---- cache write (validated before either payload is touched)
     if update_cache:
-        cache_k = torch.cat([img_k, txt_k], dim=1) if cache_txt else img_k
-        cache_v = torch.cat([img_v, txt_v], dim=1) if cache_txt else img_v
-        write_tokens = cache_k.shape[1]
+        seg_k = [img_k, txt_k] if cache_txt else [img_k]
+        seg_v = [img_v, txt_v] if cache_txt else [img_v]
+        write_tokens = sum(t.shape[1] for t in seg_k)
         new_end = cache_valid_len + write_tokens
         if new_end > cache_shape[1]:
             raise ValueError("KV pair shape, capacity, dtype, or device mismatch")
         if compressed:
-            kvc.quantize_kv_pair_into(kv_cache, cache_k.detach(), cache_v.detach(), cache_valid_len,
-                                      assume_finite=_assume_finite())
+            kvc.quantize_kv_segments_into(kv_cache, [t.detach() for t in seg_k], [t.detach() for t in seg_v],
+                                          cache_valid_len, assume_finite=_assume_finite())
         else:
-            kv_cache["k"][:, cache_valid_len:new_end] = cache_k.detach()
-            kv_cache["v"][:, cache_valid_len:new_end] = cache_v.detach()
+            off = cache_valid_len
+            for tk, tv in zip(seg_k, seg_v):
+                kv_cache["k"][:, off:off + tk.shape[1]] = tk.detach()
+                kv_cache["v"][:, off:off + tv.shape[1]] = tv.detach()
+                off += tk.shape[1]
         if cache_mask is not None:
             if cache_txt:
                 cache_mask[:, cache_valid_len:cache_valid_len + img_len] = True

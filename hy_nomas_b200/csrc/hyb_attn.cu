@@ -267,12 +267,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       float s[kBN];
+      {
+        uint32_t r[kBN];
+        tmem_ld128_wait(t_lane + static_cast<uint32_t>(sb) * 128u, r);
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t r[32];
-        tmem_ld32_wait(t_lane + static_cast<uint32_t>(sb) * 128u + c4 * 32, r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c4 * 32 + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < kBN; ++i) s[i] = __uint_as_float(r[i]);
       }
       // ---- masks: key visibility bits, then the block-causal interval of image keys
       uint32_t w[4];
@@ -292,9 +291,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           s[c] = vis ? s[c] : -INFINITY;
         }
       }
-      float mx = -INFINITY;
+      // Row max over 8 independent chains (a single chain is 128 dependent FMNMX).
+      float m8[8];
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, s[c]);
+      for (int i = 0; i < 8; ++i) m8[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < kBN; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= sl2;
       const bool resc = mx > m_run + kRescaleThreshold;
       const float m_new = resc ? mx : m_run;
@@ -319,34 +323,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       l *= alpha;
       m_run = m_new;
       const float mref = (m_run == -INFINITY) ? 0.f : m_run;
-      uint32_t pk[kBN / 2];
-      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+      float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // P = exp2(S * scale * log2e - m) as packed bf16 pairs, written in two 64-key halves
+      // so only 32 packed registers are live at a time.
 #pragma unroll
-      for (int c = 0; c < kBN / 2; ++c) {
-        const float e0 = ex2(fmaf(s[2 * c], sl2, -mref));
-        const float e1 = ex2(fmaf(s[2 * c + 1], sl2, -mref));
-        l4[c & 3] += e0 + e1;
-        pk[c] = pack_bf16x2(e0, e1);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float e0 = ex2(fmaf(s[64 * half + 2 * c], sl2, -mref));
+          const float e1 = ex2(fmaf(s[64 * half + 2 * c + 1], sl2, -mref));
+          l8[c & 7] += e0 + e1;
+          pk[c] = pack_bf16x2(e0, e1);
+        }
+        if (kPInTmem) {
+          tmem_st32(t_lane + static_cast<uint32_t>(sb) * 128u + 32 * half, pk);
+        } else {
+          uint8_t* prow = sP + sb * kTileBytes + row * 128 + half * kHalfTile;
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            uint4 v = make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+            *reinterpret_cast<uint4*>(prow + ((cc ^ (row & 7)) << 4)) = v;
+          }
+        }
       }
-      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
       if (kPInTmem) {
-        uint32_t r[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = pk[i];
-        tmem_st32(t_lane + static_cast<uint32_t>(sb) * 128u, r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = pk[32 + i];
-        tmem_st32(t_lane + static_cast<uint32_t>(sb) * 128u + 32, r);
         tmem_st_wait();
       } else {
-        uint8_t* prow = sP + sb * kTileBytes + row * 128;
-#pragma unroll
-        for (int c16 = 0; c16 < 16; ++c16) {
-          const int atom = c16 >> 3;
-          const int cc = c16 & 7;
-          uint4 v = make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
-          *reinterpret_cast<uint4*>(prow + atom * kHalfTile + ((cc ^ (row & 7)) << 4)) = v;
-        }
         fence_proxy_async_smem();
       }
       tc_fence_before();

@@ -18,10 +18,12 @@ constexpr int kRowLanes = 16;  // lanes per row: 16 x 8 bf16 = 128 values
 
 struct AppendParams {
   int fmt;
-  int B, L, H;
+  int B, L, L2, H;  // rows [0, L) from src, [L, L + L2) from src2
   long long start;
   const __nv_bfloat16* src[2];
   long long s_b[2], s_t[2], s_h[2];
+  const __nv_bfloat16* src2[2];
+  long long s2_b[2], s2_t[2], s2_h[2];
   void* dst[2];
   long long d_b, d_t, d_h;
   float* scale[2];
@@ -41,7 +43,8 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
 
 __global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams p) {
   const int which = blockIdx.y;  // 0 = K, 1 = V
-  const long long rows = static_cast<long long>(p.B) * p.L * p.H;
+  const int Lt = p.L + p.L2;
+  const long long rows = static_cast<long long>(p.B) * Lt * p.H;
   const int sub = threadIdx.x & (kRowLanes - 1);
   const long long row0 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / kRowLanes;
   const long long row_step = static_cast<long long>(gridDim.x) * blockDim.x / kRowLanes;
@@ -49,10 +52,12 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams p) {
   for (long long row = row0; row < rows; row += row_step) {
     const int h = static_cast<int>(row % p.H);
     const long long bt = row / p.H;
-    const int t = static_cast<int>(bt % p.L);
-    const int b = static_cast<int>(bt / p.L);
-    const __nv_bfloat16* src = p.src[which] + b * p.s_b[which] + t * p.s_t[which] +
-                               h * p.s_h[which] + sub * 8;
+    const int t = static_cast<int>(bt % Lt);
+    const int b = static_cast<int>(bt / Lt);
+    const __nv_bfloat16* src =
+        t < p.L ? p.src[which] + b * p.s_b[which] + t * p.s_t[which] + h * p.s_h[which] + sub * 8
+                : p.src2[which] + b * p.s2_b[which] + (t - p.L) * p.s2_t[which] + h * p.s2_h[which] +
+                      sub * 8;
     uint4 raw = *reinterpret_cast<const uint4*>(src);
     float x[8];
     unpack8(raw, x);
@@ -206,23 +211,26 @@ using namespace hyb;
 
 extern "C" int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, int32_t D,
                                   int64_t cap, int64_t start, const hyb_tensor4* src_k,
-                                  const hyb_tensor4* src_v, void* dst_k, void* dst_v,
+                                  const hyb_tensor4* src_v, int32_t L2, const hyb_tensor4* src_k2,
+                                  const hyb_tensor4* src_v2, void* dst_k, void* dst_v,
                                   int64_t d_sb, int64_t d_st, int64_t d_sh, float* scale_k,
                                   float* scale_v, int64_t s_sb, int64_t s_st, int64_t s_sh,
                                   int32_t* dev_status, void* stream) {
   if (fmt != HYB_FMT_E4M3 && fmt != HYB_FMT_INT8)
     return fail(HYB_ERR_UNSUPPORTED, "kv append: format %d is not E4M3 or INT8", fmt);
   if (D != 128) return fail(HYB_ERR_UNSUPPORTED, "kv append: head_dim %d != 128", D);
-  if (B < 0 || L < 0 || H <= 0 || src_k == nullptr || src_v == nullptr)
+  if (B < 0 || L < 0 || L2 < 0 || H <= 0 || src_k == nullptr || src_v == nullptr ||
+      (L2 > 0 && (src_k2 == nullptr || src_v2 == nullptr)))
     return fail(HYB_ERR_INVALID_ARG, "kv append: bad sizes or null views");
-  if (start < 0 || start + L > cap)
+  if (start < 0 || start + L + L2 > cap)
     return fail(HYB_ERR_CAPACITY, "kv append: tokens [%lld, %lld) exceed capacity %lld",
-                (long long)start, (long long)(start + L), (long long)cap);
-  if (L == 0 || B == 0) return HYB_OK;
-  if (src_k->fmt != HYB_FMT_BF16 || src_v->fmt != HYB_FMT_BF16)
-    return fail(HYB_ERR_INVALID_ARG, "kv append: sources must be bf16");
-  const hyb_tensor4* srcs[2] = {src_k, src_v};
-  for (int i = 0; i < 2; ++i) {
+                (long long)start, (long long)(start + L + L2), (long long)cap);
+  if (L + L2 == 0 || B == 0) return HYB_OK;
+  const hyb_tensor4* srcs[4] = {src_k, src_v, src_k2, src_v2};
+  for (int i = 0; i < (L2 > 0 ? 4 : 2); ++i) {
+    if (i < 2 && L == 0) continue;
+    if (srcs[i]->fmt != HYB_FMT_BF16)
+      return fail(HYB_ERR_INVALID_ARG, "kv append: sources must be bf16");
     if (!aligned16(srcs[i]->data) || (srcs[i]->s_b % 8) || (srcs[i]->s_t % 8) || (srcs[i]->s_h % 8))
       return fail(HYB_ERR_INVALID_ARG, "kv append: source rows must be 16-byte aligned");
   }
@@ -233,6 +241,7 @@ extern "C" int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, 
   p.fmt = fmt;
   p.B = B;
   p.L = L;
+  p.L2 = L2;
   p.H = H;
   p.start = start;
   for (int i = 0; i < 2; ++i) {
@@ -240,6 +249,11 @@ extern "C" int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, 
     p.s_b[i] = srcs[i]->s_b;
     p.s_t[i] = srcs[i]->s_t;
     p.s_h[i] = srcs[i]->s_h;
+    const hyb_tensor4* s2 = L2 > 0 ? srcs[2 + i] : srcs[i];
+    p.src2[i] = static_cast<const __nv_bfloat16*>(s2->data);
+    p.s2_b[i] = s2->s_b;
+    p.s2_t[i] = s2->s_t;
+    p.s2_h[i] = s2->s_h;
   }
   p.dst[0] = dst_k;
   p.dst[1] = dst_v;
@@ -252,7 +266,7 @@ extern "C" int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, 
   p.c_t = s_st;
   p.c_h = s_sh;
   p.status = dev_status;
-  const long long rows = static_cast<long long>(B) * L * H;
+  const long long rows = static_cast<long long>(B) * (L + L2) * H;
   dim3 grid(grid_for(rows * kRowLanes, 256), 2);
   kv_append_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   HYB_CHECK_LAUNCH();

@@ -128,7 +128,9 @@ def _any_nonfinite(*tensors: torch.Tensor) -> bool:
     return bool(status.item() & _lib.HYB_DEV_NONFINITE)
 
 
-def _append_pair(cache: dict, k: torch.Tensor, v: torch.Tensor, start: int) -> None:
+def _append_pair(cache: dict, k: torch.Tensor, v: torch.Tensor, start: int,
+                 k2: torch.Tensor | None = None, v2: torch.Tensor | None = None) -> None:
+    """Quantise-on-write of k/v (then k2/v2, appended right after) at token ``start``."""
     lib = _lib.load()
     fmt = _fmt_code(cache)
     codes_k, codes_v = cache["k"], cache["v"]
@@ -138,11 +140,13 @@ def _append_pair(cache: dict, k: torch.Tensor, v: torch.Tensor, start: int) -> N
     if codes_k.stride(3) != 1:
         raise ValueError("KV cache head_dim must be contiguous")
     B, L, H, D = k.shape
+    L2 = 0 if k2 is None else k2.shape[1]
     dev = k.device
     with torch.cuda.device(dev):
         _lib.check(lib.hyb_kv_append_pair(
             fmt, B, L, H, D, codes_k.shape[1], start,
-            _lib.bf16_view(k), _lib.bf16_view(v),
+            _lib.bf16_view(k), _lib.bf16_view(v), L2,
+            _lib.bf16_view(k2) if L2 else None, _lib.bf16_view(v2) if L2 else None,
             codes_k.data_ptr(), codes_v.data_ptr(), *codes_k.stride()[:3],
             sk.data_ptr(), sv.data_ptr(), *sk.stride()[:3],
             _lib.device_status(dev).data_ptr(), _lib.stream_ptr(dev)), "KV quantization")
@@ -184,6 +188,37 @@ def quantize_kv_pair_into(cache: dict, k: torch.Tensor, v: torch.Tensor, start: 
     if not assume_finite and _any_nonfinite(k, v):
         raise ValueError("Cannot quantize non-finite KV values")
     _append_pair(cache, k, v, start)
+
+
+def quantize_kv_segments_into(cache: dict, segments_k, segments_v, start: int, *,
+                              assume_finite: bool = False) -> None:
+    """Append [seg_0 | seg_1] (e.g. image then text tokens) at ``start`` in one pass, with
+    the validation of quantize_kv_pair_into; no concatenated copy is made."""
+    segments_k = [s for s in segments_k if s.shape[1] > 0]
+    segments_v = [s for s in segments_v if s.shape[1] > 0]
+    if not segments_k:
+        return
+    if len(segments_k) > 2 or len(segments_k) != len(segments_v):
+        raise ValueError("at most two K/V segments of matching shapes")
+    total = sum(s.shape[1] for s in segments_k)
+    for sk_, sv_ in zip(segments_k, segments_v):
+        if sk_.shape != sv_.shape or sk_.dtype != sv_.dtype or sk_.device != sv_.device:
+            raise ValueError("K/V shapes, dtypes, and devices must match")
+    for key in ("k", "v"):
+        _validate(cache, key)
+        q = cache[key]
+        for values in (segments_k if key == "k" else segments_v):
+            if (values.ndim != 4 or values.dtype != torch.bfloat16
+                    or values.shape[0] != q.shape[0] or values.shape[2:] != q.shape[2:]
+                    or start < 0 or start + total > q.shape[1] or values.device != q.device):
+                raise ValueError("KV pair shape, capacity, dtype, or device mismatch")
+    _lib.require_device(segments_k[0])
+    if not assume_finite and _any_nonfinite(*segments_k, *segments_v):
+        raise ValueError("Cannot quantize non-finite KV values")
+    if len(segments_k) == 1:
+        _append_pair(cache, segments_k[0], segments_v[0], start)
+    else:
+        _append_pair(cache, segments_k[0], segments_v[0], start, segments_k[1], segments_v[1])
 
 
 def dequantize_kv(cache: dict, key: str, valid_len: int) -> torch.Tensor:

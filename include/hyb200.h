@@ -113,13 +113,16 @@ int hyb_last_error(char* buf, size_t len);
 int hyb_device_supported(void);
 
 /* Quantise-on-write of a K/V pair into a per-token-per-head scaled cache.
- * src: bf16 [B, L, H, D]; dst codes at token offset `start` of [B, cap, H, D];
- * scales fp32 [B, cap, H, 1].  Scale = absmax/127 (INT8) or absmax/448 (E4M3),
- * 1 for an all-zero row; codes use IEEE division.  dev_status (may be NULL)
- * gets HYB_DEV_NONFINITE if any input was not finite. */
+ * Sources: bf16 [B, L, H, D] rows t < L from src_k/src_v, then (when L2 > 0) rows
+ * L <= t < L + L2 from src_k2/src_v2 (image tokens followed by text tokens, without
+ * concatenating them first).  Codes go to token offset `start` of [B, cap, H, D];
+ * scales fp32 [B, cap, H, 1].  Scale = absmax/127 (INT8) or absmax/448 (E4M3), 1 for an
+ * all-zero row; codes use IEEE division.  dev_status (may be NULL) gets
+ * HYB_DEV_NONFINITE if any input was not finite. */
 int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, int32_t D, int64_t cap,
                        int64_t start,
                        const hyb_tensor4* src_k, const hyb_tensor4* src_v,
+                       int32_t L2, const hyb_tensor4* src_k2, const hyb_tensor4* src_v2,
                        void* dst_k, void* dst_v, int64_t d_sb, int64_t d_st, int64_t d_sh,
                        float* scale_k, float* scale_v, int64_t s_sb, int64_t s_st, int64_t s_sh,
                        int32_t* dev_status, void* stream);

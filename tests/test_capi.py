@@ -75,17 +75,17 @@ def test_status_codes_for_rejected_calls():
     lib = _lib.load()
     x = _lib.Tensor4(16, _lib.HYB_FMT_BF16, 0, 8, 8, 8, None, 0, 0, 0)
     # head_dim other than 128 is unsupported
-    rc = lib.hyb_kv_append_pair(_lib.HYB_FMT_E4M3, 1, 4, 1, 64, 8, 0, x, x, 16, 16, 8, 8, 8,
+    rc = lib.hyb_kv_append_pair(_lib.HYB_FMT_E4M3, 1, 4, 1, 64, 8, 0, x, x, 0, None, None, 16, 16, 8, 8, 8,
                                 16, 16, 1, 1, 1, None, None)
     assert rc == _lib.HYB_ERR_UNSUPPORTED and "head_dim" in _lib.last_error()
     # writing past the capacity is a capacity error (ValueError in Python)
-    rc = lib.hyb_kv_append_pair(_lib.HYB_FMT_INT8, 1, 4, 1, 128, 8, 6, x, x, 16, 16, 8, 8, 8,
+    rc = lib.hyb_kv_append_pair(_lib.HYB_FMT_INT8, 1, 4, 1, 128, 8, 6, x, x, 0, None, None, 16, 16, 8, 8, 8,
                                 16, 16, 1, 1, 1, None, None)
     assert rc == _lib.HYB_ERR_CAPACITY
     with pytest.raises(ValueError):
         _lib.check(rc, "KV quantization")
     # bf16 is not a quantised storage format
-    rc = lib.hyb_kv_append_pair(_lib.HYB_FMT_BF16, 1, 4, 1, 128, 8, 0, x, x, 16, 16, 8, 8, 8,
+    rc = lib.hyb_kv_append_pair(_lib.HYB_FMT_BF16, 1, 4, 1, 128, 8, 0, x, x, 0, None, None, 16, 16, 8, 8, 8,
                                 16, 16, 1, 1, 1, None, None)
     assert rc == _lib.HYB_ERR_UNSUPPORTED
     # SP head counts must divide
