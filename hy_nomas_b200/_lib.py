@@ -109,6 +109,7 @@ SIGNATURES = {
                                    ctypes.POINTER(Tensor4), c_ptr, c_ptr]),
     "hyb_ulysses_unpack_o": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr,
                                      c_i64, c_i64, c_i64, c_ptr]),
+    "hyb_exp2_poly_eval": (c_i32, [c_ptr, c_ptr, c_i64, c_ptr]),
 }
 
 _LIB = None

@@ -28,7 +28,6 @@ constexpr int kHD = 128;                    // head dim
 constexpr int kStages = 2;                  // K/V shared-memory ring depth
 constexpr int kTileBytes = kBM * kHD * 2;   // one 128 x 128 bf16 tile
 constexpr int kHalfTile = kTileBytes / 2;   // one 64-column TMA box (128-byte rows)
-constexpr int kThreads = 192;               // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
 constexpr uint32_t kTmemCols = 512;         // S0 [0,128) S1 [128,256) O [256,384)
 constexpr uint32_t kTmemO = 256;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -59,8 +58,8 @@ struct TileRange {
   __device__ int tile(int j) const { return j < a_end ? j : b_begin + (j - a_end); }
 };
 
-__device__ TileRange key_tiles(const AttnKParams& p, int q0) {
-  const int q_last = min(q0 + kBM, p.Lq) - 1;
+__device__ TileRange key_tiles(const AttnKParams& p, int q0, int rows = kBM) {
+  const int q_last = min(q0 + rows, p.Lq) - 1;
   const int ntk = (p.Lk + kBN - 1) / kBN;
   int img_vis_end = p.Lh + p.Li;
   if (p.gtok > 0 && q_last < p.Li) {
@@ -88,36 +87,58 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   }
 }
 
-template <bool kPInTmem>
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const AttnKParams p) {
+// ======================================================================================
+// Two query tiles per CTA (256 rows of one head): the K/V tiles are loaded once for both,
+// and the single MMA thread alternates between the two softmax warpgroups so the tensor
+// pipe computes one tile's S = QK^T / O += PV while the other warpgroup exponentiates.
+// Warpgroup 0: warp 0 TMA producer, warp 1 MMA issuer (warps 2-3 idle); warpgroups 1 and
+// 2: softmax + epilogue of query tile 0 / 1 (a warp accesses the tensor-memory lane quarter
+// warp % 4).  A whole 128-column row of S is held in registers within the 168-register
+// budget of 384 threads (four max chains, O rescaled after P is written).
+// Tensor memory: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_i overwrites S_i.
+// ======================================================================================
+constexpr int kThreads2 = 384;  // warps 0-3: TMA / MMA / idle, warps 4-7 and 8-11 softmax
+constexpr int kPairRows = 2 * kBM;
+// The key-visibility bitmap of the CTA's batch row is staged in shared memory when it
+// fits (keys <= 32 * kMaxSmemBitWords); otherwise the softmax reads it through L1.
+constexpr int kMaxSmemBitWords = 4096;
+
+// kEmuPer8: of every 8 consecutive scores, that many take exp2 on the FMA pipe
+// (exp2_poly) and the rest on MUFU, to balance the two units against the tensor pipe.
+template <int kEmuPer8>
+__global__ void __launch_bounds__(kThreads2, 1)
+    attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const AttnKParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kTileBytes;
-  uint8_t* sV = sK + kStages * kTileBytes;
-  uint8_t* sP = sV + kStages * kTileBytes;  // used only when P goes through shared memory
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + (kPInTmem ? 0 : 2 * kTileBytes));
+  uint8_t* sQ = smem;                              // [2][kTileBytes]
+  uint8_t* sK = sQ + 2 * kTileBytes;               // [kStages][kTileBytes]
+  uint8_t* sV = sK + kStages * kTileBytes;         // [kStages][kTileBytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages * kTileBytes);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + kStages;
   uint64_t* v_full = k_empty + kStages;
   uint64_t* v_empty = v_full + kStages;
-  uint64_t* s_full = v_empty + kStages;  // [2]
+  uint64_t* s_full = v_empty + kStages;  // [2] one per query tile
   uint64_t* p_full = s_full + 2;         // [2]
   uint64_t* o_full = p_full + 2;         // [1]
   uint64_t* mma_done = o_full + 1;       // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* sBits = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qt = p.num_qtiles - 1 - static_cast<int>(blockIdx.x);  // heavy (late) tiles first
+  const int num_pairs = (p.num_qtiles + 1) / 2;
+  // Head-major grid (CTAs resident together share one head's K/V in L2), heaviest query
+  // pair of each head first.
+  const int qp = num_pairs - 1 - static_cast<int>(blockIdx.x);
   const int h = blockIdx.y;
   const int b = blockIdx.z;
-  const int q0 = qt * kBM;
+  const int q0 = qp * kPairRows;
+  const bool has1 = q0 + kBM < p.Lq;
   const int bh = b * p.H + h;
 
   if (threadIdx.x == 0) {
@@ -141,23 +162,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
+  const bool bits_in_smem = p.kwords <= kMaxSmemBitWords;
+  const uint32_t* kb_glob = p.kbits + static_cast<size_t>(b) * p.kwords;
+  if (bits_in_smem) {
+    for (int i = threadIdx.x; i < p.kwords / 4; i += blockDim.x)
+      reinterpret_cast<uint4*>(sBits)[i] = __ldg(reinterpret_cast<const uint4*>(kb_glob) + i);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const TileRange tr = key_tiles(p, q0);
+  const TileRange tr = key_tiles(p, q0, kPairRows);
   const int n = tr.count();
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+  if (warp < 4) {
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- TMA producer
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_expect_tx(q_full, kTileBytes);
+      mbar_expect_tx(q_full, has1 ? 2 * kTileBytes : kTileBytes);
       tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
       tma_load_3d(sQ + kHalfTile, &tmQ, q_full, 64, q0, bh);
+      if (has1) {
+        tma_load_3d(sQ + kTileBytes, &tmQ, q_full, 0, q0 + kBM, bh);
+        tma_load_3d(sQ + kTileBytes + kHalfTile, &tmQ, q_full, 64, q0 + kBM, bh);
+      }
       int issued = 0;
       for (int j = 0; j < n; ++j) {
         const int k0 = tr.tile(j) * kBN;
@@ -168,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(sK + st * kTileBytes, &tmK, &k_full[st], 0, k0, bh);
         tma_load_3d(sK + st * kTileBytes + kHalfTile, &tmK, &k_full[st], 64, k0, bh);
         if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag)) {
-          issued = j;  // K of tile j is in flight
+          issued = j;
           mbar_drain(&k_full[st], ph);
           break;
         }
@@ -178,90 +209,111 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = j + 1;
       }
       if (*abort_flag) {
-        // Let every load already issued land before the CTA can exit.
         mbar_drain(q_full, 0);
         for (int j = max(0, issued - kStages); j < issued; ++j) {
           mbar_drain(&k_full[j % kStages], (j / kStages) & 1);
           mbar_drain(&v_full[j % kStages], (j / kStages) & 1);
         }
       }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t kIdescQK = idesc_bf16_f32(kBM, kBN, false, false);
       constexpr uint32_t kIdescPV = idesc_bf16_f32(kBM, kHD, false, true);
       const uint32_t sQa = smem_u32(sQ);
       const uint32_t sKa = smem_u32(sK);
       const uint32_t sVa = smem_u32(sV);
-      const uint32_t sPa = smem_u32(sP);
-      if (mbar_wait(q_full, 0, abort_flag)) {
-        for (int j = 0; j <= n; ++j) {
-          if (j < n) {
-            const int st = j % kStages;
-            if (!mbar_wait(&k_full[st], (j / kStages) & 1, abort_flag)) break;
-            tc_fence_after();
-            const uint32_t d = tmem + static_cast<uint32_t>(j & 1) * 128u;
+      auto issue_qk = [&](int qi, int st) {
+        const uint32_t d = tmem + static_cast<uint32_t>(qi) * 128u;
 #pragma unroll
-            for (int kk = 0; kk < kHD / 16; ++kk) {
-              const uint32_t koff = static_cast<uint32_t>((kk >> 2) * kHalfTile + (kk & 3) * 32);
-              const uint64_t ad = sdesc_sw128(sQa + koff, 16, 1024);
-              const uint64_t bd = sdesc_sw128(sKa + st * kTileBytes + koff, 16, 1024);
-              umma_ss(d, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
-            }
-            tc_commit(&k_empty[st]);
-            tc_commit(&s_full[j & 1]);
-          }
-          if (j >= 1) {
-            const int jj = j - 1;
-            const int sb = jj & 1;
-            const int st = jj % kStages;
-            if (!mbar_wait(&p_full[sb], (jj >> 1) & 1, abort_flag)) break;
-            if (!mbar_wait(&v_full[st], (jj / kStages) & 1, abort_flag)) break;
-            tc_fence_after();
+        for (int kk = 0; kk < kHD / 16; ++kk) {
+          const uint32_t koff = static_cast<uint32_t>((kk >> 2) * kHalfTile + (kk & 3) * 32);
+          const uint64_t ad = sdesc_sw128(sQa + qi * kTileBytes + koff, 16, 1024);
+          const uint64_t bd = sdesc_sw128(sKa + st * kTileBytes + koff, 16, 1024);
+          umma_ss(d, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int qi, int st, bool first) {
 #pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk) {
-              // V tile is [keys][d] with d contiguous: MN-major B operand.  A K-step of
-              // 16 keys is 16 rows of 128 B; the two 64-column boxes are 16 KB apart.
-              const uint64_t bd = sdesc_sw128(sVa + st * kTileBytes + kk * 2048, kHalfTile, 1024);
-              const uint32_t acc = (jj > 0 || kk > 0) ? 1u : 0u;
-              if (kPInTmem) {
-                umma_ts(tmem + kTmemO, tmem + static_cast<uint32_t>(sb) * 128u + kk * 8, bd,
-                        kIdescPV, acc);
-              } else {
-                const uint32_t koff = static_cast<uint32_t>((kk >> 2) * kHalfTile + (kk & 3) * 32);
-                const uint64_t ad = sdesc_sw128(sPa + sb * kTileBytes + koff, 16, 1024);
-                umma_ss(tmem + kTmemO, ad, bd, kIdescPV, acc);
-              }
-            }
-            tc_commit(&v_empty[st]);
-            tc_commit(o_full);
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = sdesc_sw128(sVa + st * kTileBytes + kk * 2048, kHalfTile, 1024);
+          umma_ts(tmem + kTmemO + static_cast<uint32_t>(qi) * 128u,
+                  tmem + static_cast<uint32_t>(qi) * 128u + kk * 8, bd, kIdescPV,
+                  (!first || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      if (ok && n > 0) {
+        ok = mbar_wait(&k_full[0], 0, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(0, 0);
+          tc_commit(&s_full[0]);
+          if (has1) {
+            issue_qk(1, 0);
+            tc_commit(&s_full[1]);
           }
+          tc_commit(&k_empty[0]);
         }
       }
-      // Drain: every MMA issued by this thread completes before TMEM is released.
+      // Fixed issue order per key tile j: P.V of query tile 0, Q.K^T of tile 0 for j+1,
+      // P.V of query tile 1, Q.K^T of tile 1 for j+1.  Blocking waits (try_wait suspends
+      // the thread) keep this warp off the issue slots the softmax warps share.
+      for (int j = 0; ok && j < n; ++j) {
+        const int st = j % kStages;
+        const bool more = j + 1 < n;
+        const int st1 = (j + 1) % kStages;
+        if (!mbar_wait(&v_full[st], (j / kStages) & 1, abort_flag)) break;
+        if (!mbar_wait(&p_full[0], j & 1, abort_flag)) break;
+        tc_fence_after();
+        issue_pv(0, st, j == 0);
+        if (more) {
+          if (!mbar_wait(&k_full[st1], ((j + 1) / kStages) & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_qk(0, st1);
+          tc_commit(&s_full[0]);
+        }
+        if (has1) {
+          if (!mbar_wait(&p_full[1], j & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_pv(1, st, j == 0);
+        }
+        tc_commit(&v_empty[st]);
+        if (more) {
+          if (has1) {
+            issue_qk(1, st1);
+            tc_commit(&s_full[1]);
+          }
+          tc_commit(&k_empty[st1]);
+        }
+      }
+      tc_commit(o_full);
       tc_commit(mma_done);
       mbar_drain(mma_done, 0);
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int qi = (warp >> 2) - 1;  // query tile of this warpgroup
+    const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int qrow = q0 + row;
+    const int qt0 = q0 + qi * kBM;   // first row of this query tile
+    const int qrow = qt0 + row;
+    const bool active = qi == 0 || has1;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t t_s = t_lane + static_cast<uint32_t>(qi) * 128u;
+    const uint32_t t_o = t_lane + kTmemO + static_cast<uint32_t>(qi) * 128u;
     const bool img_row = qrow < p.Li;
-    // First invisible image key (relative to the image start) for this row.
     const int row_lim = (p.gtok > 0 && img_row) ? (qrow / p.gtok + 1) * p.gtok : INT_MAX;
-    const int cta_lim = (p.gtok > 0 && q0 < p.Li) ? (q0 / p.gtok + 1) * p.gtok : INT_MAX;
+    const int cta_lim = (p.gtok > 0 && qt0 < p.Li) ? (qt0 / p.gtok + 1) * p.gtok : INT_MAX;
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    const uint32_t* kb_row = p.kbits + static_cast<size_t>(b) * p.kwords;
-    for (int j = 0; j < n; ++j) {
+    for (int j = 0; active && j < n; ++j) {
       const int k0 = tr.tile(j) * kBN;
-      const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag)) {
+      uint4 w4 = bits_in_smem ? reinterpret_cast<const uint4*>(sBits)[k0 >> 7]
+                              : __ldg(reinterpret_cast<const uint4*>(kb_glob) + (k0 >> 7));
+      const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+      if (!mbar_wait(&s_full[qi], j & 1, abort_flag)) {
         ok = false;
         break;
       }
@@ -269,14 +321,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       float s[kBN];
       {
         uint32_t r[kBN];
-        tmem_ld128_wait(t_lane + static_cast<uint32_t>(sb) * 128u, r);
+        tmem_ld128_wait(t_s, r);
 #pragma unroll
         for (int i = 0; i < kBN; ++i) s[i] = __uint_as_float(r[i]);
       }
-      // ---- masks: key visibility bits, then the block-causal interval of image keys
-      uint32_t w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) w[i] = __ldg(kb_row + (k0 >> 5) + i);
+      // Mask: visibility bits of the tile's keys, then this row's block-causal interval
+      // [ca, cb) of invisible image keys.
       const bool causal_tile = (cta_lim != INT_MAX) && (k0 + kBN > p.Lh + cta_lim) &&
                                (k0 < p.Lh + p.Li);
       if (causal_tile || (w[0] & w[1] & w[2] & w[3]) != 0xffffffffu) {
@@ -291,114 +341,112 @@ __global__ void __launch_bounds__(kThreads, 1)
           s[c] = vis ? s[c] : -INFINITY;
         }
       }
-      // Row max over 8 independent chains (a single chain is 128 dependent FMNMX).
-      float m8[8];
+      // Row max: 4 chains of 3-input max.
+      float m4[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = s[i];
+      for (int c = 4; c + 8 <= kBN; c += 8) {
 #pragma unroll
-      for (int c = 8; c < kBN; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
-      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], s[c + 2 * i], s[c + 2 * i + 1]);
+      }
+      m4[0] = fmax3(m4[0], s[kBN - 4], s[kBN - 3]);
+      m4[1] = fmax3(m4[1], s[kBN - 2], s[kBN - 1]);
+      float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       mx *= sl2;
       const bool resc = mx > m_run + kRescaleThreshold;
       const float m_new = resc ? mx : m_run;
       const float alpha = resc ? ex2(m_run - m_new) : 1.f;
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {
-        // O must hold PV_{j-1} before it is rescaled; PV_j waits for our P below.
-        if (!mbar_wait(o_full, (j - 1) & 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t r[32];
-          tmem_ld32_wait(t_lane + kTmemO + c4 * 32, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(t_lane + kTmemO + c4 * 32, r);
-        }
-        tmem_st_wait();
-      }
       l *= alpha;
       m_run = m_new;
       const float mref = (m_run == -INFINITY) ? 0.f : m_run;
-      float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      // P = exp2(S * scale * log2e - m) as packed bf16 pairs, written in two 64-key halves
-      // so only 32 packed registers are live at a time.
+      // P = exp2(S * scale * log2e - m) in packed-pair arithmetic: one fma.f32x2 for the
+      // scaled, shifted scores of two keys, two MUFU exponentials, one bf16x2 pack and one
+      // add.f32x2 into the row sum.
+      float2 l2a = make_float2(0.f, 0.f), l2b = make_float2(0.f, 0.f);
+      const float2 sl2x2 = make_float2(sl2, sl2);
+      const float2 negm = make_float2(-mref, -mref);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float e0 = ex2(fmaf(s[64 * half + 2 * c], sl2, -mref));
-          const float e1 = ex2(fmaf(s[64 * half + 2 * c + 1], sl2, -mref));
-          l8[c & 7] += e0 + e1;
-          pk[c] = pack_bf16x2(e0, e1);
-        }
-        if (kPInTmem) {
-          tmem_st32(t_lane + static_cast<uint32_t>(sb) * 128u + 32 * half, pk);
-        } else {
-          uint8_t* prow = sP + sb * kTileBytes + row * 128 + half * kHalfTile;
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            uint4 v = make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-            *reinterpret_cast<uint4*>(prow + ((cc ^ (row & 7)) << 4)) = v;
+        for (int c = 0; c < 16; ++c) {
+          const int c0 = 2 * c;
+          const float2 x = ffma2(make_float2(s[32 * q4 + c0], s[32 * q4 + c0 + 1]), sl2x2, negm);
+          float2 e;
+          if ((c0 & 7) >= 8 - kEmuPer8) {
+            e = make_float2(exp2_poly(x.x), exp2_poly(x.y));
+          } else {
+            e = make_float2(ex2(x.x), ex2(x.y));
           }
+          if (c & 1) {
+            l2b = fadd2(l2b, e);
+          } else {
+            l2a = fadd2(l2a, e);
+          }
+          pk[c] = pack_bf16x2(e.x, e.y);
+        }
+        tmem_st16(t_s + 16 * q4, pk);
+      }
+      l += (l2a.x + l2a.y) + (l2b.x + l2b.y);
+      if (j > 0 && __any_sync(0xffffffffu, resc)) {
+        // O_i already holds every P·V of earlier tiles (the S commit this softmax waited
+        // on was issued after the previous P·V of this query tile), and the next P·V
+        // waits for the P-ready barrier below; rescaling after the P write keeps the S
+        // registers dead here.
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t r[32];
+          tmem_ld32_wait(t_o + c4 * 32, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(t_o + c4 * 32, r);
         }
       }
-      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
-      if (kPInTmem) {
-        tmem_st_wait();
-      } else {
-        fence_proxy_async_smem();
-      }
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
+      if (lane == 0) mbar_arrive(&p_full[qi]);
     }
-    // ---- epilogue: O / l at the row's final position
-    bool have_o = ok && n > 0;
-    if (have_o && n >= 2) have_o = mbar_wait(o_full, (n - 2) & 1, abort_flag);
-    if (have_o) have_o = mbar_wait(o_full, (n - 1) & 1, abort_flag);
-    have_o = __all_sync(0xffffffffu, have_o);
-    tc_fence_after();
-    const bool in_range = qrow < p.Lq;
-    bool valid = in_range;
-    if (in_range && p.qbits != nullptr)
-      valid = (__ldg(p.qbits + static_cast<size_t>(b) * p.qwords + (qrow >> 5)) >> (qrow & 31)) & 1u;
-    const float inv_l = (l > 0.f && valid) ? __frcp_rn(l) : 0.f;
-    __nv_bfloat16* dst = nullptr;
-    if (in_range) {
-      if (img_row) {
-        dst = p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg + (qrow % p.oi_seg) * p.oi_t +
-              h * p.oi_h;
-      } else {
-        dst = p.out_txt + b * p.ot_b + static_cast<long long>(qrow - p.Li) * p.ot_t + h * p.ot_h;
+    if (active) {
+      bool have_o = ok && n > 0 && mbar_wait(o_full, 0, abort_flag);
+      have_o = __all_sync(0xffffffffu, have_o);
+      tc_fence_after();
+      const bool in_range = qrow < p.Lq;
+      bool valid = in_range;
+      if (in_range && p.qbits != nullptr)
+        valid = (__ldg(p.qbits + static_cast<size_t>(b) * p.qwords + (qrow >> 5)) >> (qrow & 31)) & 1u;
+      const float inv_l = (l > 0.f && valid) ? __frcp_rn(l) : 0.f;
+      __nv_bfloat16* dst = nullptr;
+      if (in_range) {
+        if (img_row) {
+          dst = p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg + (qrow % p.oi_seg) * p.oi_t +
+                h * p.oi_h;
+        } else {
+          dst = p.out_txt + b * p.ot_b + static_cast<long long>(qrow - p.Li) * p.ot_t + h * p.ot_h;
+        }
       }
-    }
 #pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {
-      uint32_t r[32];
-      if (have_o) {
-        tmem_ld32_wait(t_lane + kTmemO + c4 * 32, r);
-      } else {
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t r[32];
+        if (have_o) {
+          tmem_ld32_wait(t_o + c4 * 32, r);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = 0u;
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          o[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
+        if (dst != nullptr) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        }
       }
-      uint32_t o[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        o[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
-      if (dst != nullptr) {
-        uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      if (p.lse != nullptr && in_range) {
+        p.lse[static_cast<size_t>(bh) * p.Lq + qrow] =
+            (l > 0.f && valid) ? (m_run * kLn2 + __logf(l)) : -INFINITY;
       }
-    }
-    if (p.lse != nullptr && in_range) {
-      p.lse[static_cast<size_t>(bh) * p.Lq + qrow] =
-          (l > 0.f && valid) ? (m_run * kLn2 + __logf(l)) : -INFINITY;
     }
   }
 
@@ -423,22 +471,33 @@ struct StageSeg {
 struct StageParams {
   int B, H, L, nout, nseg;
   StageSeg seg[2][3];
-  __nv_bfloat16* out[2];  // [B, H, L, 128]
+  void* out[2];       // [B, H, L, 128]
+  int out_f16[2];     // 1: output in fp16 (the P.V operand), 0: bf16
 };
 
-__device__ __forceinline__ uint4 load_row8(const StageSeg& s, int b, int t, int h, int sub) {
+// Eight consecutive values of one (batch, token, head) row as fp32: bf16 sources exactly,
+// quantised sources as code * scale (one fp32 multiply, as dequantize_kv does before its
+// single rounding).
+__device__ __forceinline__ void load_row8(const StageSeg& s, int b, int t, int h, int sub, float (&v)[8]) {
   const int bb = s.bcast ? 0 : b;
   if (s.rows != nullptr) t = __ldg(s.rows + t);
   if (s.fmt == HYB_FMT_BF16) {
     const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(s.data) + bb * s.s_b + t * s.s_t +
                                h * s.s_h + sub * 8;
-    return *reinterpret_cast<const uint4*>(src);
+    const uint4 raw = *reinterpret_cast<const uint4*>(src);
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(p2[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+    return;
   }
   const float sc = s.scale[bb * s.c_b + t * s.c_t + h * s.c_h];
   const uint8_t* src = static_cast<const uint8_t*>(s.data) + bb * s.s_b + t * s.s_t + h * s.s_h + sub * 8;
   const uint2 raw = *reinterpret_cast<const uint2*>(src);
   const uint8_t* by = reinterpret_cast<const uint8_t*>(&raw);
-  uint32_t out[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     float a, c;
@@ -452,9 +511,9 @@ __device__ __forceinline__ uint4 load_row8(const StageSeg& s, int b, int t, int 
       a = f.x;
       c = f.y;
     }
-    out[i] = pack_bf16x2(__fmul_rn(a, sc), __fmul_rn(c, sc));
+    v[2 * i] = __fmul_rn(a, sc);
+    v[2 * i + 1] = __fmul_rn(c, sc);
   }
-  return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
@@ -476,7 +535,14 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
 #pragma unroll
     for (int o = 0; o < 2; ++o) {
       if (o < p.nout) {
-        *reinterpret_cast<uint4*>(p.out[o] + out_off) = load_row8(p.seg[o][si], b, t, h, sub);
+        float v[8];
+        load_row8(p.seg[o][si], b, t, h, sub, v);
+        uint4 packed;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&packed);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          w[i] = p.out_f16[o] ? pack_f16x2(v[2 * i], v[2 * i + 1]) : pack_bf16x2(v[2 * i], v[2 * i + 1]);
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out[o]) + out_off) = packed;
       }
     }
   }
@@ -558,15 +624,16 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [BH, L, 128] bf16 head-major tensor, 64 x 128 boxes with 128-byte swizzle.
-int make_map(CUtensorMap* map, const void* base, int BH, int L) {
+// [BH, L, 128] 16-bit head-major tensor (bf16 or f16), 64 x 128 boxes with 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, int BH, int L, bool f16 = false) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return fail(HYB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(L), static_cast<cuuint64_t>(BH)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHD) * 2, static_cast<cuuint64_t>(L) * kHD * 2};
   cuuint32_t box[3] = {64, 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(HYB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
@@ -643,30 +710,41 @@ WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt)
   return w;
 }
 
-template <bool kPInTmem>
-int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnKParams& kp,
-                cudaStream_t stream) {
-  const int smem = 1024 + kTileBytes * (1 + 2 * kStages) + (kPInTmem ? 0 : 2 * kTileBytes) + 256;
+template <int kEmuPer8>
+int launch_attn2_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnKParams& kp,
+                   cudaStream_t stream) {
+  const int smem = 1024 + kTileBytes * (2 + 2 * kStages) + 256 + kMaxSmemBitWords * 4;
   static bool attr_set = false;
   if (!attr_set) {
-    HYB_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_kernel<kPInTmem>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    HYB_CUDA_TRY(cudaFuncSetAttribute(attn_fwd2_kernel<kEmuPer8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      smem));
     attr_set = true;
   }
-  dim3 grid(kp.num_qtiles, kp.H, kp.B);
-  attn_fwd_kernel<kPInTmem><<<grid, kThreads, smem, stream>>>(mq, mk, mv, kp);
+  dim3 grid((kp.num_qtiles + 1) / 2, kp.H, kp.B);
+  attn_fwd2_kernel<kEmuPer8><<<grid, kThreads2, smem, stream>>>(mq, mk, mv, kp);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
 
-// P (softmax probabilities) goes through tensor memory unless HYB_P_SMEM=1 selects the
-// shared-memory operand path (same math; kept to cross-check the tensor-memory A layout).
-bool p_in_tmem() {
-  static int mode = -1;
-  if (mode < 0) {
-    const char* e = getenv("HYB_P_SMEM");
-    mode = (e != nullptr && e[0] == '1') ? 0 : 1;
+// Share of exponentials computed on the FMA pipe, in eighths (HYB_EXP_EMU overrides).
+int exp_emu_per8() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("HYB_EXP_EMU");
+    v = (e != nullptr && e[0] >= '0' && e[0] <= '4') ? (e[0] - '0') : 0;
   }
-  return mode == 1;
+  return v;
+}
+
+int launch_attn2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnKParams& kp,
+                 cudaStream_t stream) {
+  switch (exp_emu_per8()) {
+    case 0: return launch_attn2_t<0>(mq, mk, mv, kp, stream);
+    case 1: return launch_attn2_t<1>(mq, mk, mv, kp, stream);
+    case 3: return launch_attn2_t<3>(mq, mk, mv, kp, stream);
+    case 4: return launch_attn2_t<4>(mq, mk, mv, kp, stream);
+    default: return launch_attn2_t<2>(mq, mk, mv, kp, stream);
+  }
 }
 
 int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
@@ -676,8 +754,8 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
     return fail(HYB_ERR_INVALID_ARG, "attention: inconsistent sizes");
   if (a->Lq == 0) return HYB_OK;
   if (!al16(a->q) || !al16(a->k) || !al16(a->v)) return fail(HYB_ERR_INVALID_ARG, "attention: q/k/v misaligned");
-  if (a->kwords < ((a->Lk + kBN - 1) / kBN) * (kBN / 32))
-    return fail(HYB_ERR_INVALID_ARG, "attention: kbits too short");
+  if (a->kwords < ((a->Lk + kBN - 1) / kBN) * (kBN / 32) || (a->kwords % 4) != 0 || !al16(a->kbits))
+    return fail(HYB_ERR_INVALID_ARG, "attention: kbits must hold 4 aligned words per key tile");
   if (a->img_len > 0) {
     if (a->out_img == nullptr || !al16(a->out_img) || (a->oi_sb % 8) || (a->oi_st % 8) || (a->oi_sh % 8) ||
         (a->oi_sseg % 8) || a->oi_seg <= 0)
@@ -721,7 +799,7 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   kp.lse = a->lse;
   kp.status = a->dev_status;
   kp.num_qtiles = (a->Lq + kBM - 1) / kBM;
-  return p_in_tmem() ? launch_attn<true>(mq, mk, mv, kp, stream) : launch_attn<false>(mq, mk, mv, kp, stream);
+  return launch_attn2(mq, mk, mv, kp, stream);
 }
 
 }  // namespace
@@ -821,6 +899,8 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     }
     sp.out[0] = k_all;
     sp.out[1] = v_all;
+    sp.out_f16[0] = 0;
+    sp.out_f16[1] = 0;
     stage_kernel<<<grid_for(static_cast<long long>(a->B) * a->H * w.Lk * 16, 256), 256, 0, stream>>>(sp);
     HYB_CHECK_LAUNCH();
   }
@@ -835,6 +915,8 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     if (Lt > 0) sp.seg[0][sp.nseg++] = seg_of(a->txt_q, Lt, 0);
     sp.out[0] = q_all;
     sp.out[1] = nullptr;
+    sp.out_f16[0] = 0;
+    sp.out_f16[1] = 0;
     stage_kernel<<<grid_for(static_cast<long long>(a->B) * a->H * w.Lq * 16, 256), 256, 0, stream>>>(sp);
     HYB_CHECK_LAUNCH();
   } else {

@@ -47,3 +47,24 @@ extern "C" int hyb_last_error(char* buf, size_t len) {
 }
 
 extern "C" int hyb_device_supported(void) { return hyb::device_cc_major() == 10 ? 1 : 0; }
+
+namespace hyb {
+namespace {
+__global__ void exp2_poly_kernel(const float* x, float* y, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    y[i] = exp2_poly(x[i]);
+}
+}  // namespace
+}  // namespace hyb
+
+extern "C" int hyb_exp2_poly_eval(const float* x, float* y, int64_t n, void* stream) {
+  if (n < 0 || (n > 0 && (x == nullptr || y == nullptr)))
+    return hyb::fail(HYB_ERR_INVALID_ARG, "exp2_poly_eval: bad arguments");
+  if (n == 0) return HYB_OK;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  hyb::exp2_poly_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}

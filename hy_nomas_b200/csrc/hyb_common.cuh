@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -72,6 +73,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking test of the same condition.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
@@ -169,6 +183,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn, b
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Same with f16 A/B (format code 0).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
 // Bits: [0,14) start >> 4, [16,30) leading-dim byte offset >> 4,
 // [32,46) stride-dim byte offset >> 4, [46,48) version = 1, [61,64) layout (2 = SW128).
@@ -241,6 +261,12 @@ __device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&r)[64
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -250,6 +276,68 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA/ALU pipes (offloads the MUFU unit).  Range reduction x = n + f with
+// n = round-to-nearest(x) (via the 1.5 * 2^23 shifter) and f in [-1/2, 1/2]; 2^f from a
+// degree-3 polynomial fitted here by relative-error-weighted least squares on Chebyshev
+// nodes of [-1/2, 1/2] (max relative error 7.5e-5, far below the 2^-9 rounding of the
+// bf16 P it feeds); 2^n is applied by adding n to the exponent field.  x < -125 gives 0,
+// so masked (-inf) scores contribute nothing.  Valid for x <= 127.
+__device__ __forceinline__ float exp2_poly(float x) {
+  constexpr float kC0 = 0.99992807f;
+  constexpr float kC1 = 0.69326100f;
+  constexpr float kC2 = 0.24261112f;
+  constexpr float kC3 = 0.05517161f;
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  const float xc = fmaxf(x, -127.f);
+  const float t = __fadd_rn(xc, kShift);
+  const float n = __fsub_rn(t, kShift);
+  const float f = __fsub_rn(xc, n);
+  const float p = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
+  const int ni = __float_as_int(t) - 0x4B400000;
+  const float r = __int_as_float(__float_as_int(p) + (ni << 23));
+  return xc < -125.f ? 0.f : r;
+}
+
+// Two base-2 exponentials per MUFU op on a packed f16 pair (f16 in, f16 out).
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// Packed fp32 pair arithmetic (one instruction for two lanes of work on sm_100).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)),
+        "l"(*reinterpret_cast<unsigned long long*>(&c)));
+  return *reinterpret_cast<float2*>(&r);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
+  return *reinterpret_cast<float2*>(&r);
+}
+
+// Three-input max (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float2 unpack_f16x2(uint32_t u) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&u));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -185,6 +185,10 @@ int hyb_ulysses_unpack_o(int32_t P, int32_t B, int32_t Ls, int32_t Ls_max, int32
                          const void* recv, void* out, int64_t o_sb, int64_t o_st, int64_t o_sh,
                          void* stream);
 
+/* Diagnostic: y[i] = the FMA-pipe exp2 approximation the attention softmax uses for a
+ * share of its exponentials (no reference counterpart; used by the accuracy test). */
+int hyb_exp2_poly_eval(const float* x, float* y, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -250,3 +250,20 @@ def test_empty_text_and_single_query(cuda_lib):
     ref_img, _ = oatt.cached_attention(*cur, dk, dv)
     assert out_txt.shape[1] == 0
     assert_close(out_img, ref_img, "single query")
+
+
+def test_exp2_poly_accuracy(cuda_lib):
+    """The FMA-pipe exponential against CUDA's exp2f: relative error <= 1e-4 wherever the
+    result is a normal float, exactly 0 below -125 and for -inf."""
+    from hy_nomas_b200 import _lib
+    dev = torch.device("cuda")
+    x = torch.cat([torch.linspace(-125.0, 12.0, 2_000_001), torch.tensor([-126.0, -1e4, float("-inf")])])
+    x = x.to(dev)
+    y = torch.empty_like(x)
+    _lib.check(cuda_lib.hyb_exp2_poly_eval(x.data_ptr(), y.data_ptr(), x.numel(),
+                                           torch.cuda.current_stream().cuda_stream), "exp2 poly")
+    ref = torch.exp2(x.double())
+    normal = x > -125.0
+    rel = ((y.double() - ref).abs() / ref)[normal]
+    assert rel.max().item() <= 1e-4, rel.max().item()
+    assert torch.all(y[x < -125.0] == 0)
