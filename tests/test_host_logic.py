@@ -1,0 +1,91 @@
+"""Host-side logic without a GPU: the installer's fallback routing, argument validation of
+the drop-in, FLOP accounting and the synthetic-input generator."""
+import types
+
+import pytest
+import torch
+
+from hy_nomas_b200 import attention as hatt
+from hy_nomas_b200 import install as hinst
+from hy_nomas_b200 import kv_cache as kvc
+from hy_nomas_b200.flops import append_bytes, attention_flops
+
+
+def _fake_native():
+    calls = []
+
+    def native(q, k, v, kv_cache, *args):
+        calls.append(args)
+        return "native"
+
+    mod = types.SimpleNamespace(causal_attention_with_cache_mp=native,
+                                get_sequence_parallel_state=lambda: False,
+                                nccl_info=types.SimpleNamespace(sp_group=None, rank_within_spgroup=0))
+    return mod, calls
+
+
+def test_install_routes_cpu_and_unsupported_modes_to_native():
+    mod, calls = _fake_native()
+    original = hinst.install(mod)
+    try:
+        patched = mod.causal_attention_with_cache_mp
+        assert patched.original is original
+        x = torch.zeros(1, 2, 2, 128, dtype=torch.bfloat16)
+        cache = {"k": torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16), "v": torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)}
+        assert patched((x, x), (x, x), (x, x), cache, 0, "flash3") == "native"      # CPU tensors
+        assert patched((x, x), (x, x), (x, x), cache, 0, "flash3", sparse_context={}) == "native"
+        qvg = {"storage_format": "qvg", "k": cache["k"], "v": cache["v"]}
+        assert patched((x, x), (x, x), (x, x), qvg, 0, "flash3") == "native"
+        assert patched.stats["fallbacks"] == 3 and patched.stats["calls"] == 0
+        assert len(calls) == 3 and calls[0][:4] == (0, "flash3", None, False)   # positional order kept
+    finally:
+        hinst.uninstall(mod)
+    assert mod.causal_attention_with_cache_mp is original
+    hatt.set_parallel_state_provider(hatt._ps.get_sequence_parallel_state, hatt._ps.nccl_info)
+
+
+def test_drop_in_validates_before_touching_the_device():
+    x = torch.zeros(1, 2, 2, 128, dtype=torch.bfloat16)
+    cache = {"k": torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16), "v": torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)}
+    with pytest.raises(ValueError, match="seg_ar_attention_backend"):
+        hatt.causal_attention_with_cache_mp((x, x), (x, x), (x, x), cache, seg_ar_attention_backend="bogus")
+    with pytest.raises(NotImplementedError):
+        hatt.causal_attention_with_cache_mp((x, x), (x, x), (x, x), cache, sparse_context={"config": {}})
+    i8 = kvc.make_int8_kv_block(1, 4, 2, 128, device="cpu")
+    with pytest.raises(ValueError, match="no-grad"):
+        with torch.enable_grad():
+            hatt.causal_attention_with_cache_mp((x, x), (x, x), (x, x), i8)
+    mixed = {"k": cache["k"], "v": cache["v"].float()}
+    with pytest.raises(RuntimeError, match="dtype mismatch"):
+        hatt.causal_attention_with_cache_mp((x, x), (x, x), (x, x), mixed)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        with torch.no_grad():
+            hatt.causal_attention_with_cache_mp((x, x), (x, x), (x, x), cache)
+
+
+def test_cache_formats_and_modes():
+    assert kvc.cache_format(kvc.make_int8_kv_block(1, 2, 1, 128, device="cpu")) == "int8"
+    assert kvc.cache_format(kvc.make_fp8_kv_block(1, 2, 1, 128, device="cpu")) == "fp8_e4m3"
+    assert kvc.quantization_mode(types.SimpleNamespace(kv_cache_quantization="fp8_e4m3")) == "fp8_e4m3"
+    with pytest.raises(ValueError):
+        kvc.quantization_mode(types.SimpleNamespace(kv_cache_quantization="fp4"))
+    blk = kvc.make_fp8_kv_block(2, 10, 3, 128, device="cpu")
+    assert kvc.kv_storage_bytes(blk) == 2 * (2 * 10 * 3 * 128) + 2 * (2 * 10 * 3 * 4)
+
+
+def test_flop_and_byte_accounting():
+    assert attention_flops(24960, 6240, 1, 24, 128, True, 1560) == pytest.approx(2.2134e12, rel=1e-4)
+    assert attention_flops(24960, 6240, 1, 24, 128, True, 0) == pytest.approx(2.3928e12, rel=1e-4)
+    # config 1 (CPU): 8 heads, 256 queries against 1024 + 256 keys (+1 text)
+    assert attention_flops(1024, 256, 1, 8) == pytest.approx(4 * 8 * 128 * (257 * 1281), rel=1e-9)
+    assert append_bytes(6241, 24) == 6241 * 24 * 2 * (256 + 128 + 4)   # 116.2 MB
+
+
+def test_synthetic_generator_is_seeded_and_has_outliers():
+    from hy_nomas_b200.synthetic import make_generator, seeded_kv
+    a = seeded_kv((1, 64, 2, 128), make_generator(5))
+    b = seeded_kv((1, 64, 2, 128), make_generator(5))
+    assert torch.equal(a, b)
+    per_channel = a.float().abs().mean(dim=(0, 1))        # [H, D]
+    for h in range(2):
+        assert (per_channel[h] > 4).sum() == 4
