@@ -100,6 +100,7 @@ SIGNATURES = {
     "hyb_kv_dequant": (c_i32, [ctypes.POINTER(Tensor4), c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "hyb_cached_attention_workspace_bytes": (c_i64, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
     "hyb_cached_attention": (c_i32, [ctypes.POINTER(CachedAttnArgs), c_ptr]),
+    "hyb_cached_attention_noalloc": (c_i32, [ctypes.POINTER(CachedAttnArgs), c_ptr]),
     "hyb_attn_fwd": (c_i32, [ctypes.POINTER(AttnArgs), c_ptr]),
     "hyb_lse_merge": (c_i32, [c_i32, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr]),
     "hyb_ulysses_pack_qkv": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,

@@ -17,6 +17,8 @@
 //    position (pad_tokens semantics: masked text queries produce zero rows).
 #include <limits.h>
 
+#include <mutex>
+
 #include "hyb_common.cuh"
 
 namespace hyb {
@@ -954,4 +956,60 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   at.lse = a->lse;
   at.dev_status = a->dev_status;
   return attn_core(&at, stream);
+}
+
+// =========================================================================================
+// Allocation-free variant of hyb_cached_attention.
+//
+// Some callers cannot allocate device memory at the moment they call attention: a serving
+// process whose framework has already reserved (nearly) all of HBM in its own pool for the
+// KV cache and activations, a latency-critical decode loop that must not call cudaMalloc
+// because it can synchronise the whole device, or a plugin host whose FFI passes tensors but
+// no allocator.  For them the staging scratch (head-major Q/K/V and the visibility bitmaps)
+// lives in one fixed device array owned by this library.  The array is static device memory:
+// every GPU on which this library's kernels are loaded holds it until the process exits.
+// Nothing in it has to start at zero: within one call every byte the attention kernel reads
+// is first written by that call's mask and staging kernels.
+// =========================================================================================
+static constexpr long long kNoAllocScratchBytes = 64LL << 20;  // 64 MiB per device
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 128;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};  // device address of g_noalloc_scratch, per device
+}  // namespace
+
+extern "C" int hyb_cached_attention_noalloc(const hyb_cached_attn_args* a, void* stream) {
+  if (a == nullptr || a->abi_version != HYB_ABI_VERSION)
+    return fail(HYB_ERR_INVALID_ARG, "cached attention (no-alloc): null args or ABI version mismatch");
+  const int64_t need = hyb_cached_attention_workspace_bytes(a->B, a->H, a->D, a->valid_len, a->img_len,
+                                                            a->txt_len, a->attend_txt);
+  if (need < 0) return fail(HYB_ERR_UNSUPPORTED, "cached attention (no-alloc): head_dim must be 128");
+  if (need > kNoAllocScratchBytes)
+    return fail(HYB_ERR_WORKSPACE,
+                "cached attention (no-alloc): these sizes need %lld bytes of staging scratch but the "
+                "fixed per-device scratch holds %lld; use hyb_cached_attention with a caller workspace",
+                (long long)need, (long long)kNoAllocScratchBytes);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(HYB_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(HYB_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  void* scratch = nullptr;
+  {
+    // First call on a device (with that device current): resolve the array's device address.
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+      void* addr = nullptr;
+      e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+      if (e != cudaSuccess)
+        return fail(HYB_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+      g_noalloc_addr[dev] = addr;
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+  hyb_cached_attn_args local = *a;
+  local.workspace = scratch;
+  local.workspace_bytes = kNoAllocScratchBytes;
+  return hyb_cached_attention(&local, stream);
 }

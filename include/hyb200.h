@@ -185,6 +185,18 @@ int hyb_ulysses_unpack_o(int32_t P, int32_t B, int32_t Ls, int32_t Ls_max, int32
                          const void* recv, void* out, int64_t o_sb, int64_t o_st, int64_t o_sh,
                          void* stream);
 
+/* hyb_cached_attention for callers that cannot allocate device memory (no counterpart in
+ * the reference).  Same arguments and results; args->workspace / workspace_bytes are
+ * ignored and the staging scratch is a fixed 64 MiB array of static device memory inside
+ * this library, which every GPU that loads the library holds until the process exits.
+ * Sizes whose scratch (hyb_cached_attention_workspace_bytes) exceeds 64 MiB are rejected
+ * with HYB_ERR_WORKSPACE.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first call before any
+ * stream capture.  The function calls no allocator.  All calls on a device share the one
+ * array, so calls that can overlap on the GPU (different streams, or concurrent host
+ * threads) race on it and must be serialised by the caller. */
+int hyb_cached_attention_noalloc(const hyb_cached_attn_args* args, void* stream);
+
 /* Diagnostic: y[i] = the FMA-pipe exp2 approximation the attention softmax uses for a
  * share of its exponentials (no reference counterpart; used by the accuracy test). */
 int hyb_exp2_poly_eval(const float* x, float* y, int64_t n, void* stream);
