@@ -212,7 +212,8 @@ def all_gather(input_: torch.Tensor, dim: int = 1, group=None, sizes=None):
         pad = torch.zeros((max_size - x.shape[0], *x.shape[1:]), dtype=x.dtype, device=x.device)
         x = torch.cat([x, pad], dim=0)
     x = x.contiguous()
-    gathered = torch.empty((world, *x.shape), dtype=x.dtype, device=x.device)
+    gathered = torch.empty((world * x.shape[0], *x.shape[1:]), dtype=x.dtype, device=x.device)
     dist.all_gather_into_tensor(gathered, x, group=group)
+    gathered = gathered.view(world, *x.shape)
     parts = [gathered[r, :sizes[r]] for r in range(world)]
     return torch.cat(parts, dim=0).movedim(0, dim).contiguous()
