@@ -83,6 +83,18 @@ class AttnArgs(ctypes.Structure):
         ("oi_seg", c_i64), ("oi_sseg", c_i64),
         ("out_txt", c_ptr), ("ot_sb", c_i64), ("ot_st", c_i64), ("ot_sh", c_i64),
         ("lse", c_ptr), ("dev_status", c_ptr),
+        ("kv_splits", c_i32), ("pad_", c_i32), ("part_o", c_ptr), ("part_lse", c_ptr),
+    ]
+
+
+class WorkspaceLayout(ctypes.Structure):
+    """``hyb_workspace_layout``."""
+
+    _fields_ = [
+        ("q", c_i64), ("k", c_i64), ("v", c_i64), ("kbits", c_i64), ("qbits", c_i64),
+        ("part_o", c_i64), ("part_lse", c_i64), ("total", c_i64),
+        ("Lq", c_i32), ("Lk", c_i32), ("kwords", c_i32), ("qwords", c_i32), ("kv_splits", c_i32),
+        ("pad_", c_i32),
     ]
 
 
@@ -99,6 +111,8 @@ SIGNATURES = {
     "hyb_check_finite": (c_i32, [ctypes.POINTER(Tensor4), c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "hyb_kv_dequant": (c_i32, [ctypes.POINTER(Tensor4), c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "hyb_cached_attention_workspace_bytes": (c_i64, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "hyb_cached_attention_workspace_layout": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
+                                                       ctypes.POINTER(WorkspaceLayout)]),
     "hyb_cached_attention": (c_i32, [ctypes.POINTER(CachedAttnArgs), c_ptr]),
     "hyb_cached_attention_noalloc": (c_i32, [ctypes.POINTER(CachedAttnArgs), c_ptr]),
     "hyb_attn_fwd": (c_i32, [ctypes.POINTER(AttnArgs), c_ptr]),

@@ -54,29 +54,11 @@ def _new_out(B, L, H, D, device):
     return torch.empty((B, L, H, D), dtype=torch.bfloat16, device=device)
 
 
-def _align256(x: int) -> int:
-    return (x + 255) & ~255
-
-
-def workspace_layout(B, H, Lh, Li, Lt, attend_txt, D=128):
-    """Byte offsets of the staging workspace (mirrors layout_for in csrc/hyb_attn.cu):
-    q [B, H, Lq, D] bf16 | k [B, H, Lk, D] | v | key bitmap [B, kwords] | query bitmap."""
-    Lq = Li + Lt
-    Lk = Lh + Li + (Lt if attend_txt else 0)
-    kwords = -(-Lk // 128) * 4
-    qwords = -(-Lq // 32)
-    off = 0
-    lay = {"Lq": Lq, "Lk": Lk, "kwords": kwords, "qwords": qwords, "q": off}
-    off = _align256(off + B * H * Lq * D * 2)
-    lay["k"] = off
-    off = _align256(off + B * H * Lk * D * 2)
-    lay["v"] = off
-    off = _align256(off + B * H * Lk * D * 2)
-    lay["kbits"] = off
-    off = _align256(off + B * kwords * 4)
-    lay["qbits"] = off
-    off = _align256(off + B * max(qwords, 1) * 4)
-    lay["total"] = off
+def workspace_layout(B, H, Lh, Li, Lt, attend_txt, D=128) -> "_lib.WorkspaceLayout":
+    """Byte offsets of the staging workspace on the current device (from the library)."""
+    lay = _lib.WorkspaceLayout()
+    _lib.check(_lib.load().hyb_cached_attention_workspace_layout(B, H, D, Lh, Li, Lt, int(bool(attend_txt)), lay),
+               "workspace layout")
     return lay
 
 
@@ -184,16 +166,19 @@ def cached_attention_local(
     with torch.cuda.device(dev):
         _lib.check(lib.hyb_cached_attention(args, _lib.stream_ptr(dev)), "cached attention")
     if ws_obj is not None:
-        lay = workspace_layout(B, H, cache_valid_len, Li, Lt, attend_txt, D)
+        with torch.cuda.device(dev):
+            lay = workspace_layout(B, H, cache_valid_len, Li, Lt, attend_txt, D)
         base = workspace.data_ptr()
         at = _lib.AttnArgs()
         at.abi_version = _lib.HYB_ABI_VERSION
-        at.B, at.H, at.D, at.Lq, at.Lk = B, H, D, lay["Lq"], lay["Lk"]
+        at.B, at.H, at.D, at.Lq, at.Lk = B, H, D, lay.Lq, lay.Lk
         at.hist_len, at.img_len, at.group_tokens = cache_valid_len, Li, int(group_tokens)
         at.softmax_scale = args.softmax_scale
-        at.q, at.k, at.v = base + lay["q"], base + lay["k"], base + lay["v"]
-        at.kbits, at.kwords = base + lay["kbits"], lay["kwords"]
-        at.qbits, at.qwords = base + lay["qbits"], lay["qwords"]
+        at.q, at.k, at.v = base + lay.q, base + lay.k, base + lay.v
+        at.kbits, at.kwords = base + lay.kbits, lay.kwords
+        at.qbits, at.qwords = base + lay.qbits, lay.qwords
+        at.kv_splits = lay.kv_splits
+        at.part_o, at.part_lse = base + lay.part_o, base + lay.part_lse
         at.out_img = args.out_img
         at.oi_sb, at.oi_st, at.oi_sh = oi[0], oi[1], oi[2]
         at.oi_seg, at.oi_sseg = (oi[3], oi[4]) if oi[3] > 0 else (max(Li, 1), 0)

@@ -17,6 +17,7 @@
 //    position (pad_tokens semantics: masked text queries produce zero rows).
 #include <limits.h>
 
+#include <cmath>
 #include <mutex>
 
 #include "hyb_common.cuh"
@@ -50,6 +51,12 @@ struct AttnKParams {
   float* lse;
   int* status;
   int num_qtiles;
+  // Split-KV: each CTA covers one of kv_splits contiguous slices of its key-tile list and,
+  // when kv_splits > 1, writes normalised fp32 partial rows part_o [S, B, H, Lq, 128] and
+  // their natural-log LSE part_lse [S, B, H, Lq]; merge_splits_kernel combines them.
+  int kv_splits;
+  float* part_o;
+  float* part_lse;
 };
 
 // Key tiles visited by one query tile: [0, a_end) then [b_begin, b_end).
@@ -138,7 +145,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
   // pair of each head first.
   const int qp = num_pairs - 1 - static_cast<int>(blockIdx.x);
   const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  const int b = static_cast<int>(blockIdx.z) / p.kv_splits;
+  const int split = static_cast<int>(blockIdx.z) % p.kv_splits;
   const int q0 = qp * kPairRows;
   const bool has1 = q0 + kBM < p.Lq;
   const int bh = b * p.H + h;
@@ -176,7 +184,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
   const uint32_t tmem = *tmem_slot;
 
   const TileRange tr = key_tiles(p, q0, kPairRows);
-  const int n = tr.count();
+  // This CTA's slice [j_begin, j_begin + n) of the pair's key-tile list.
+  const int n_all = tr.count();
+  const int j_begin = static_cast<int>((static_cast<long long>(n_all) * split) / p.kv_splits);
+  const int n = static_cast<int>((static_cast<long long>(n_all) * (split + 1)) / p.kv_splits) - j_begin;
 
   if (warp < 4) {
     if (warp == 0 && lane == 0) {
@@ -193,7 +204,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       }
       int issued = 0;
       for (int j = 0; j < n; ++j) {
-        const int k0 = tr.tile(j) * kBN;
+        const int k0 = tr.tile(j_begin + j) * kBN;
         const int st = j % kStages;
         const uint32_t ph = (j / kStages) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag)) break;
@@ -311,7 +322,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     float l = 0.f;
     bool ok = true;
     for (int j = 0; active && j < n; ++j) {
-      const int k0 = tr.tile(j) * kBN;
+      const int k0 = tr.tile(j_begin + j) * kBN;
       uint4 w4 = bits_in_smem ? reinterpret_cast<const uint4*>(sBits)[k0 >> 7]
                               : __ldg(reinterpret_cast<const uint4*>(kb_glob) + (k0 >> 7));
       const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
@@ -413,41 +424,67 @@ __global__ void __launch_bounds__(kThreads2, 1)
       have_o = __all_sync(0xffffffffu, have_o);
       tc_fence_after();
       const bool in_range = qrow < p.Lq;
-      bool valid = in_range;
-      if (in_range && p.qbits != nullptr)
-        valid = (__ldg(p.qbits + static_cast<size_t>(b) * p.qwords + (qrow >> 5)) >> (qrow & 31)) & 1u;
-      const float inv_l = (l > 0.f && valid) ? __frcp_rn(l) : 0.f;
-      __nv_bfloat16* dst = nullptr;
-      if (in_range) {
-        if (img_row) {
-          dst = p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg + (qrow % p.oi_seg) * p.oi_t +
-                h * p.oi_h;
-        } else {
-          dst = p.out_txt + b * p.ot_b + static_cast<long long>(qrow - p.Li) * p.ot_t + h * p.ot_h;
+      if (p.kv_splits > 1) {
+        // Partial result of this key slice: O / l in fp32 and its LSE (-inf when the slice
+        // saw no visible key); query validity is applied by the merge.
+        const float inv_l = l > 0.f ? __frcp_rn(l) : 0.f;
+        const size_t prow = ((static_cast<size_t>(split) * p.B + b) * p.H + h) * p.Lq + qrow;
+        float* dst = in_range ? p.part_o + prow * kHD : nullptr;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t r[32];
+          if (have_o) {
+            tmem_ld32_wait(t_o + c4 * 32, r);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
+          }
+          if (dst != nullptr) {
+            float4* d4 = reinterpret_cast<float4*>(dst + c4 * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              d4[i] = make_float4(__uint_as_float(r[4 * i]) * inv_l, __uint_as_float(r[4 * i + 1]) * inv_l,
+                                  __uint_as_float(r[4 * i + 2]) * inv_l, __uint_as_float(r[4 * i + 3]) * inv_l);
+          }
         }
-      }
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t r[32];
-        if (have_o) {
-          tmem_ld32_wait(t_o + c4 * 32, r);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        if (in_range) p.part_lse[prow] = l > 0.f ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+      } else {
+        bool valid = in_range;
+        if (in_range && p.qbits != nullptr)
+          valid = (__ldg(p.qbits + static_cast<size_t>(b) * p.qwords + (qrow >> 5)) >> (qrow & 31)) & 1u;
+        const float inv_l = (l > 0.f && valid) ? __frcp_rn(l) : 0.f;
+        __nv_bfloat16* dst = nullptr;
+        if (in_range) {
+          if (img_row) {
+            dst = p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg + (qrow % p.oi_seg) * p.oi_t +
+                  h * p.oi_h;
+          } else {
+            dst = p.out_txt + b * p.ot_b + static_cast<long long>(qrow - p.Li) * p.ot_t + h * p.ot_h;
+          }
         }
-        uint32_t o[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          o[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
-        if (dst != nullptr) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t r[32];
+          if (have_o) {
+            tmem_ld32_wait(t_o + c4 * 32, r);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
+          }
+          uint32_t o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            o[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
+          if (dst != nullptr) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          }
         }
-      }
-      if (p.lse != nullptr && in_range) {
-        p.lse[static_cast<size_t>(bh) * p.Lq + qrow] =
-            (l > 0.f && valid) ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+        if (p.lse != nullptr && in_range) {
+          p.lse[static_cast<size_t>(bh) * p.Lq + qrow] =
+              (l > 0.f && valid) ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+        }
       }
     }
   }
@@ -457,6 +494,50 @@ __global__ void __launch_bounds__(kThreads2, 1)
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
   if (threadIdx.x == 0 && *abort_flag && p.status != nullptr) atomicOr(p.status, HYB_DEV_TIMEOUT);
+}
+
+
+// Combine the kv_splits partial results of every (batch, head, query row): LSE-weighted sum of
+// the normalised partial rows, written as bf16 at the row's final position (zero for padded
+// text queries), plus the final LSE when requested.  One warp per row, 4 dims per lane.
+__global__ void __launch_bounds__(256) merge_splits_kernel(const AttnKParams p) {
+  const long long rows = static_cast<long long>(p.B) * p.H * p.Lq;
+  const int lane = threadIdx.x & 31;
+  const long long slice = static_cast<long long>(p.B) * p.H * p.Lq;
+  for (long long r = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5; r < rows;
+       r += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const int qrow = static_cast<int>(r % p.Lq);
+    const long long bh = r / p.Lq;
+    const int h = static_cast<int>(bh % p.H);
+    const int b = static_cast<int>(bh / p.H);
+    bool valid = true;
+    if (p.qbits != nullptr)
+      valid = (__ldg(p.qbits + static_cast<size_t>(b) * p.qwords + (qrow >> 5)) >> (qrow & 31)) & 1u;
+    float m = -INFINITY;
+    for (int sp = 0; sp < p.kv_splits; ++sp) m = fmaxf(m, __ldg(p.part_lse + sp * slice + r));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float wsum = 0.f;
+    if (m != -INFINITY) {
+      for (int sp = 0; sp < p.kv_splits; ++sp) {
+        const float w = __expf(__ldg(p.part_lse + sp * slice + r) - m);
+        wsum += w;
+        const float4 o = __ldg(reinterpret_cast<const float4*>(p.part_o + (sp * slice + r) * kHD) + lane);
+        acc.x += w * o.x;
+        acc.y += w * o.y;
+        acc.z += w * o.z;
+        acc.w += w * o.w;
+      }
+    }
+    const float inv = (wsum > 0.f && valid) ? 1.f / wsum : 0.f;
+    __nv_bfloat16* dst = qrow < p.Li
+                             ? p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg + (qrow % p.oi_seg) * p.oi_t +
+                                   h * p.oi_h
+                             : p.out_txt + b * p.ot_b + static_cast<long long>(qrow - p.Li) * p.ot_t + h * p.ot_h;
+    *reinterpret_cast<uint2*>(dst + lane * 4) =
+        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+    if (p.lse != nullptr && lane == 0)
+      p.lse[r] = (wsum > 0.f && valid) ? (m + __logf(wsum)) : -INFINITY;
+  }
 }
 
 // ------------------------------------------------------------------ staging kernels
@@ -687,11 +768,52 @@ StageSeg seg_of(const hyb_tensor4& v, int len, int bcast, const int* rows = null
 long long align256(long long x) { return (x + 255) & ~255LL; }
 
 struct WorkspaceLayout {
-  long long q, k, v, kbits, qbits, total;
-  int Lq, Lk, kwords, qwords;
+  long long q, k, v, kbits, qbits, part_o, part_lse, total;
+  int Lq, Lk, kwords, qwords, kv_splits;
 };
 
-WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt) {
+// Multiprocessor count of the current device (148 on B200; 148 when no device is visible).
+int device_sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return 148;
+  }
+  return n;
+}
+
+// Key-slice count per query pair.  One pair-CTA per (pair, head, batch) leaves the last wave
+// of CTAs partly empty; slicing the key range multiplies the CTAs by S at the price of
+// writing and re-reading fp32 partial rows.  Estimated time: attention at ~1 PFLOP/s scaled
+// by the wave quantisation ceil(c S / sms) / (c S / sms), plus the partial traffic at ~6 TB/s
+// and a merge launch.  HYB_KV_SPLITS overrides (1..16).
+int choose_kv_splits(int B, int H, int Lq, int Lk, int sms) {
+  const char* e = getenv("HYB_KV_SPLITS");
+  if (e != nullptr) {
+    const int v = atoi(e);
+    if (v >= 1 && v <= 16) return v;
+  }
+  const long long ctas = static_cast<long long>((Lq + kPairRows - 1) / kPairRows) * H * B;
+  const int tiles = (Lk + kBN - 1) / kBN;
+  if (ctas <= 0 || tiles <= 0) return 1;
+  const double attn_us = 4.0 * 128.0 * H * B * static_cast<double>(Lq) * Lk / 1e15 * 1e6 * 0.75;
+  const double rows = static_cast<double>(B) * H * Lq;
+  int best = 1;
+  double best_t = 1e300;
+  for (int sp = 1; sp <= 16; ++sp) {
+    if (sp > 1 && tiles / sp < 16) break;  // keep at least 16 key tiles per slice
+    const double w = static_cast<double>(ctas) * sp / sms;
+    const double t = attn_us * std::ceil(w) / w + (sp > 1 ? sp * rows * 1032.0 / 6e12 * 1e6 + 5.0 : 0.0);
+    if (t < best_t * 0.98) {
+      best_t = t;
+      best = sp;
+    }
+  }
+  return best;
+}
+
+WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt, int sms) {
   WorkspaceLayout w;
   w.Lq = Li + Lt;
   w.Lk = Lh + Li + (attend_txt ? Lt : 0);
@@ -708,6 +830,14 @@ WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt)
   off = align256(off + static_cast<long long>(B) * w.kwords * 4);
   w.qbits = off;
   off = align256(off + static_cast<long long>(B) * (w.qwords > 0 ? w.qwords : 1) * 4);
+  w.kv_splits = choose_kv_splits(B, H, w.Lq, w.Lk, sms);
+  w.part_o = off;
+  w.part_lse = off;
+  if (w.kv_splits > 1) {
+    off = align256(off + static_cast<long long>(w.kv_splits) * B * H * w.Lq * kHD * 4);
+    w.part_lse = off;
+    off = align256(off + static_cast<long long>(w.kv_splits) * B * H * w.Lq * 4);
+  }
   w.total = off;
   return w;
 }
@@ -722,7 +852,7 @@ int launch_attn2_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
                                       smem));
     attr_set = true;
   }
-  dim3 grid((kp.num_qtiles + 1) / 2, kp.H, kp.B);
+  dim3 grid((kp.num_qtiles + 1) / 2, kp.H, kp.B * kp.kv_splits);
   attn_fwd2_kernel<kEmuPer8><<<grid, kThreads2, smem, stream>>>(mq, mk, mv, kp);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
@@ -801,7 +931,17 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   kp.lse = a->lse;
   kp.status = a->dev_status;
   kp.num_qtiles = (a->Lq + kBM - 1) / kBM;
-  return launch_attn2(mq, mk, mv, kp, stream);
+  kp.kv_splits = a->kv_splits > 1 ? a->kv_splits : 1;
+  kp.part_o = a->part_o;
+  kp.part_lse = a->part_lse;
+  if (kp.kv_splits > 1 && (a->part_o == nullptr || a->part_lse == nullptr || !al16(a->part_o)))
+    return fail(HYB_ERR_INVALID_ARG, "attention: kv_splits > 1 needs 16-byte aligned partial buffers");
+  int rc2 = launch_attn2(mq, mk, mv, kp, stream);
+  if (rc2 != HYB_OK || kp.kv_splits == 1) return rc2;
+  const long long rows = static_cast<long long>(kp.B) * kp.H * kp.Lq;
+  merge_splits_kernel<<<grid_for(rows * 32, 256), 256, 0, stream>>>(kp);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
 }
 
 }  // namespace
@@ -818,7 +958,32 @@ extern "C" int hyb_attn_fwd(const hyb_attn_args* a, void* stream) {
 extern "C" int64_t hyb_cached_attention_workspace_bytes(int32_t B, int32_t H, int32_t D, int32_t valid_len,
                                                         int32_t img_len, int32_t txt_len, int32_t attend_txt) {
   if (D != kHD || B < 0 || H < 0 || valid_len < 0 || img_len < 0 || txt_len < 0) return -1;
-  return layout_for(B, H, valid_len, img_len, txt_len, attend_txt).total;
+  return layout_for(B, H, valid_len, img_len, txt_len, attend_txt, device_sm_count()).total;
+}
+
+extern "C" int hyb_cached_attention_workspace_layout(int32_t B, int32_t H, int32_t D, int32_t valid_len,
+                                                     int32_t img_len, int32_t txt_len, int32_t attend_txt,
+                                                     hyb_workspace_layout* out) {
+  if (out == nullptr) return fail(HYB_ERR_INVALID_ARG, "workspace layout: null output");
+  if (D != kHD) return fail(HYB_ERR_UNSUPPORTED, "workspace layout: head_dim %d != 128", D);
+  if (B < 0 || H < 0 || valid_len < 0 || img_len < 0 || txt_len < 0)
+    return fail(HYB_ERR_INVALID_ARG, "workspace layout: negative sizes");
+  const WorkspaceLayout w = layout_for(B, H, valid_len, img_len, txt_len, attend_txt, device_sm_count());
+  out->q = w.q;
+  out->k = w.k;
+  out->v = w.v;
+  out->kbits = w.kbits;
+  out->qbits = w.qbits;
+  out->part_o = w.part_o;
+  out->part_lse = w.part_lse;
+  out->total = w.total;
+  out->Lq = w.Lq;
+  out->Lk = w.Lk;
+  out->kwords = w.kwords;
+  out->qwords = w.qwords;
+  out->kv_splits = w.kv_splits;
+  out->pad_ = 0;
+  return HYB_OK;
 }
 
 extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_ptr) {
@@ -831,7 +996,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     return fail(HYB_ERR_INVALID_ARG, "KV-cache batch mismatch: current=%d, cache=%d", a->B, a->cache_batch);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const int Lh = a->valid_len, Li = a->img_len, Lt = a->txt_len;
-  const WorkspaceLayout w = layout_for(a->B, a->H, Lh, Li, Lt, a->attend_txt);
+  const WorkspaceLayout w = layout_for(a->B, a->H, Lh, Li, Lt, a->attend_txt, device_sm_count());
   if (a->workspace == nullptr || a->workspace_bytes < w.total || !al16(a->workspace))
     return fail(HYB_ERR_WORKSPACE, "cached attention: workspace %lld bytes < %lld needed",
                 (long long)a->workspace_bytes, (long long)w.total);
@@ -955,6 +1120,9 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   at.ot_sh = a->ot_sh;
   at.lse = a->lse;
   at.dev_status = a->dev_status;
+  at.kv_splits = w.kv_splits;
+  at.part_o = reinterpret_cast<float*>(ws + w.part_o);
+  at.part_lse = reinterpret_cast<float*>(ws + w.part_lse);
   return attn_core(&at, stream);
 }
 

@@ -139,6 +139,16 @@ int hyb_kv_dequant(const hyb_tensor4* src, int32_t B, int32_t valid, int32_t H, 
 int64_t hyb_cached_attention_workspace_bytes(int32_t B, int32_t H, int32_t D, int32_t valid_len,
                                              int32_t img_len, int32_t txt_len, int32_t attend_txt);
 
+/* Byte offsets of the staging workspace of hyb_cached_attention for these sizes on the
+ * current device (the key-slice count kv_splits depends on its multiprocessor count). */
+typedef struct hyb_workspace_layout {
+  int64_t q, k, v, kbits, qbits, part_o, part_lse, total;
+  int32_t Lq, Lk, kwords, qwords, kv_splits, pad_;
+} hyb_workspace_layout;
+int hyb_cached_attention_workspace_layout(int32_t B, int32_t H, int32_t D, int32_t valid_len,
+                                          int32_t img_len, int32_t txt_len, int32_t attend_txt,
+                                          hyb_workspace_layout* out);
+
 /* The whole single-rank cached attention (stage + tcgen05 attention kernel). */
 int hyb_cached_attention(const hyb_cached_attn_args* args, void* stream);
 
@@ -158,6 +168,10 @@ typedef struct hyb_attn_args {
   void* out_txt; int64_t ot_sb, ot_st, ot_sh;
   float* lse;
   int32_t* dev_status;
+  int32_t kv_splits;         /* >1: each query pair's key tiles are split into this many slices */
+  int32_t pad_;
+  float* part_o;             /* fp32 [kv_splits, B, H, Lq, D] partial rows (kv_splits > 1) */
+  float* part_lse;           /* fp32 [kv_splits, B, H, Lq] partial LSE (kv_splits > 1) */
 } hyb_attn_args;
 int hyb_attn_fwd(const hyb_attn_args* args, void* stream);
 

@@ -42,10 +42,12 @@ def visibility(Lh: int, Li: int, Lt: int, attend_txt: bool, group_tokens: int,
 
 def cached_attention(img_q, img_k, img_v, txt_q, txt_k, txt_v, hist_k, hist_v, *,
                      history_mask=None, text_mask=None, attend_txt=True, group_tokens=0,
-                     softmax_scale=None, return_lse=False):
+                     softmax_scale=None, return_lse=False, return_magnitude=False):
     """Reference output of one rank's cached attention, fp32 [B, Li, H, D] / [B, Lt, H, D].
 
-    ``hist_k`` / ``hist_v`` are the bf16 history (already decoded), batch B or 1."""
+    ``hist_k`` / ``hist_v`` are the bf16 history (already decoded), batch B or 1.
+    ``return_magnitude`` also returns softmax(S) @ |V| (the weighted magnitude of the values
+    each output element sums, which scales the rounding error of a bf16 P)."""
     B, Li, H, D = img_q.shape
     Lt = txt_q.shape[1]
     Lh = hist_k.shape[1]
@@ -69,6 +71,7 @@ def cached_attention(img_q, img_k, img_v, txt_q, txt_k, txt_v, hist_k, hist_v, *
     p = torch.exp(s - m)
     l = p.sum(dim=-1, keepdim=True)
     o = torch.matmul(p, vh) / torch.where(l > 0, l, torch.ones_like(l))
+    mag = torch.matmul(p, vh.abs()) / torch.where(l > 0, l, torch.ones_like(l)) if return_magnitude else None
     lse = (m + torch.log(l)).squeeze(-1)               # [B, H, Lq]
     o = o.permute(0, 2, 1, 3)                          # [B, Lq, H, D]
     qvalid = torch.ones(B, Li + Lt, dtype=torch.bool)
@@ -77,7 +80,12 @@ def cached_attention(img_q, img_k, img_v, txt_q, txt_k, txt_v, hist_k, hist_v, *
     o = o * qvalid[:, :, None, None]
     lse = torch.where(qvalid[:, None, :] & (l.squeeze(-1) > 0), lse, torch.full_like(lse, float("-inf")))
     out = (o[:, :Li], o[:, Li:])
-    return (out + (lse,)) if return_lse else out
+    if return_lse:
+        out = out + (lse,)
+    if return_magnitude:
+        mag = mag.permute(0, 2, 1, 3)
+        out = out + ((mag[:, :Li], mag[:, Li:]),)
+    return out
 
 
 def reference_sdpa_path(img_q, img_k, img_v, txt_q, txt_k, txt_v, hist_k, hist_v, *,

@@ -47,7 +47,9 @@ int main(void) {
   F(hyb_cached_attn_args, out_txt) F(hyb_cached_attn_args, lse) F(hyb_cached_attn_args, workspace_bytes)
   F(hyb_cached_attn_args, dev_status)
   F(hyb_attn_args, q) F(hyb_attn_args, kwords) F(hyb_attn_args, qbits) F(hyb_attn_args, oi_sseg)
-  F(hyb_attn_args, lse) F(hyb_attn_args, dev_status)
+  F(hyb_attn_args, lse) F(hyb_attn_args, dev_status) F(hyb_attn_args, kv_splits) F(hyb_attn_args, part_lse)
+  printf("hyb_workspace_layout %zu\n", sizeof(hyb_workspace_layout));
+  F(hyb_workspace_layout, total) F(hyb_workspace_layout, kv_splits)
   return 0;
 }
 """
@@ -62,7 +64,7 @@ def test_ctypes_layouts_match_c(tmp_path):
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
     c = dict(line.rsplit(" ", 1) for line in out.strip().splitlines())
     types = {"hyb_tensor4": _lib.Tensor4, "hyb_cached_attn_args": _lib.CachedAttnArgs,
-             "hyb_attn_args": _lib.AttnArgs}
+             "hyb_attn_args": _lib.AttnArgs, "hyb_workspace_layout": _lib.WorkspaceLayout}
     for key, val in c.items():
         if "." in key:
             t, m = key.split(".")
@@ -114,10 +116,17 @@ def test_no_device_is_reported_not_faked():
     assert lib.hyb_device_supported() == 0
 
 
-def test_python_workspace_layout_mirrors_c():
+def test_workspace_layout_is_consistent():
     from hy_nomas_b200.attention import workspace_layout
     lib = _lib.load()
-    for args in [(1, 24, 24960, 6240, 1, 1), (2, 3, 0, 130, 2, 0), (1, 1, 7, 1, 0, 1), (3, 5, 1000, 384, 9, 1)]:
+    for args in [(1, 24, 24960, 6240, 1, 1), (2, 3, 0, 130, 2, 0), (1, 1, 7, 1, 0, 1), (3, 5, 1000, 384, 9, 1),
+                 (1, 3, 74880, 6240, 1, 1)]:
         B, H, Lh, Li, Lt, att = args
-        assert workspace_layout(B, H, Lh, Li, Lt, att)["total"] == \
-            lib.hyb_cached_attention_workspace_bytes(B, H, 128, Lh, Li, Lt, att)
+        lay = workspace_layout(B, H, Lh, Li, Lt, att)
+        assert lay.total == lib.hyb_cached_attention_workspace_bytes(B, H, 128, Lh, Li, Lt, att)
+        assert lay.Lq == Li + Lt and lay.Lk == Lh + Li + (Lt if att else 0)
+        assert lay.q == 0 < lay.k < lay.v < lay.kbits < lay.qbits <= lay.part_o <= lay.part_lse <= lay.total
+        assert all(x % 256 == 0 for x in (lay.k, lay.v, lay.kbits, lay.qbits, lay.part_o, lay.part_lse))
+        assert 1 <= lay.kv_splits <= 16
+        if lay.kv_splits > 1:
+            assert lay.part_lse - lay.part_o >= lay.kv_splits * B * H * lay.Lq * 128 * 4
