@@ -122,13 +122,27 @@ def dist_setup(n_gpus):
     import torch.distributed as dist
     if n_gpus <= 1:
         return 0, 1, 0
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        os.environ["NCCL_DEBUG"] = "WARN"   # keep stdout to the one JSON line
     import datetime
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                            device_id=torch.device("cuda", local))
+    # The communicator prints a version banner on stdout during its first use; route fd 1 to
+    # stderr while it is created so rank 0's stdout carries only the JSON line.
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        dist.barrier()
+        torch.cuda.synchronize()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
     return rank, world, local
 
 
@@ -175,13 +189,20 @@ def run_b200(args):
     img, txt = prob["img"], prob["txt"]
     flops_total = attention_flops(Lh, Li, TXT, H_TOTAL, D, True, T)
     stream = torch.cuda.current_stream(device)
+    sp_metadata = None
+    if world > 1:
+        # Computed once per model forward and passed to every layer, as the reference's
+        # forward_with_cache does (nomas_cpt.py:3486-3488).
+        from hy_nomas_b200 import communications as comm
+        sp_metadata = comm.prepare_sp_communication(Ls, H_TOTAL, device, ps.nccl_info.sp_group)
 
     def step(q_img, k_img, v_img, q_txt, k_txt, v_txt):
         with torch.no_grad():
             return hatt.causal_attention_with_cache_mp(
                 (q_img, q_txt), (k_img, k_txt), (v_img, v_txt), cache, cache_valid_len=Lh,
                 attn_mode="flash3", update_cache=True, cache_txt=True, cache_mask=cmask,
-                tokens_per_frame=T, seg_ar_attention_backend="b200", chunk_causal_frames=1)
+                tokens_per_frame=T, seg_ar_attention_backend="b200", sp_metadata=sp_metadata,
+                chunk_causal_frames=1)
 
     for _ in range(args.warmup):
         step(*img, *txt)
