@@ -56,6 +56,7 @@ class CachedAttnArgs(ctypes.Structure):
         ("abi_version", c_i32), ("B", c_i32), ("H", c_i32), ("D", c_i32),
         ("cache_batch", c_i32), ("valid_len", c_i32), ("img_len", c_i32), ("txt_len", c_i32),
         ("attend_txt", c_i32), ("group_tokens", c_i32), ("softmax_scale", ctypes.c_float),
+        ("q_pos0", c_i32), ("k_pos0", c_i32),
         ("hist_k", Tensor4), ("hist_v", Tensor4),
         ("img_q", Tensor4), ("img_k", Tensor4), ("img_v", Tensor4),
         ("txt_q", Tensor4), ("txt_k", Tensor4), ("txt_v", Tensor4),
@@ -75,7 +76,7 @@ class AttnArgs(ctypes.Structure):
     _fields_ = [
         ("abi_version", c_i32), ("B", c_i32), ("H", c_i32), ("D", c_i32), ("Lq", c_i32),
         ("Lk", c_i32), ("hist_len", c_i32), ("img_len", c_i32), ("group_tokens", c_i32),
-        ("softmax_scale", ctypes.c_float),
+        ("softmax_scale", ctypes.c_float), ("q_pos0", c_i32), ("k_pos0", c_i32),
         ("q", c_ptr), ("k", c_ptr), ("v", c_ptr),
         ("kbits", c_ptr), ("kwords", c_i32),
         ("qbits", c_ptr), ("qwords", c_i32),

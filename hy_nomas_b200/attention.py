@@ -81,7 +81,7 @@ def cached_attention_local(
     img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, cache_valid_len, *,
     history_mask=None, text_mask=None, attend_txt=True, group_tokens=0,
     softmax_scale=None, out_img=None, out_img_strides=None, out_txt=None, lse=None,
-    hist_rows=None, workspace=None,
+    hist_rows=None, workspace=None, q_pos0=0, k_pos0=0, img_kv_fmt=None,
 ):
     """Single-rank attention of the current chunk over [history | image | text].
 
@@ -93,11 +93,16 @@ def cached_attention_local(
     [B, L, H, D]; ``out_img`` may be supplied pre-allocated with custom element
     strides ``(sb, st, sh)`` or ``(sb, st, sh, seg, sseg)`` where image row t lands at
     ``(t // seg) * sseg + (t % seg) * st`` (e.g. the Ulysses O send buffer).
+    ``q_pos0`` / ``k_pos0`` shift the block-causal rule to global positions (ring steps);
+    with ``img_kv_fmt`` (HYB_FMT_E4M3 / HYB_FMT_INT8) ``img_k`` / ``img_v`` are
+    ``(codes, scale)`` pairs of a quantised block.
     """
     lib = _lib.load()
     B, Li, H, D = img_q.shape
     Lt = txt_q.shape[1]
     dev = img_q.device
+    if kv_cache is None:   # no history: a zero-length bf16 placeholder
+        kv_cache = {"k": img_q[:, :0], "v": img_q[:, :0]}
     fmt_name = kvc.cache_format(kv_cache)
     if fmt_name == "none":
         hk, hv = kv_cache["k"], kv_cache["v"]
@@ -141,9 +146,15 @@ def cached_attention_local(
     args.group_tokens = int(group_tokens)
     args.softmax_scale = float(softmax_scale) if softmax_scale else 0.0
     args.hist_k, args.hist_v = hist_k, hist_v
+    args.q_pos0, args.k_pos0 = int(q_pos0), int(k_pos0)
     args.img_q = _lib.bf16_view(img_q) if Li else empty
-    args.img_k = _lib.bf16_view(img_k) if Li else empty
-    args.img_v = _lib.bf16_view(img_v) if Li else empty
+    if img_kv_fmt is None:
+        args.img_k = _lib.bf16_view(img_k) if Li else empty
+        args.img_v = _lib.bf16_view(img_v) if Li else empty
+    else:
+        # quantised current keys/values: (codes, scale) pairs in the given format
+        args.img_k = _lib.coded_view(img_k[0], img_k[1], img_kv_fmt) if Li else empty
+        args.img_v = _lib.coded_view(img_v[0], img_v[1], img_kv_fmt) if Li else empty
     args.txt_q = _lib.bf16_view(txt_q) if Lt else empty
     args.txt_k = _lib.bf16_view(txt_k) if Lt else empty
     args.txt_v = _lib.bf16_view(txt_v) if Lt else empty
@@ -174,6 +185,7 @@ def cached_attention_local(
         at.B, at.H, at.D, at.Lq, at.Lk = B, H, D, lay.Lq, lay.Lk
         at.hist_len, at.img_len, at.group_tokens = cache_valid_len, Li, int(group_tokens)
         at.softmax_scale = args.softmax_scale
+        at.q_pos0, at.k_pos0 = args.q_pos0, args.k_pos0
         at.q, at.k, at.v = base + lay.q, base + lay.k, base + lay.v
         at.kbits, at.kwords = base + lay.kbits, lay.kwords
         at.qbits, at.qwords = base + lay.qbits, lay.qwords

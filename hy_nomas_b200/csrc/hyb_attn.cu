@@ -39,6 +39,10 @@ constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
 struct AttnKParams {
   int B, H, Lq, Lk, Lh, Li, gtok;
+  // Global token positions of image query 0 and image key 0 for the block-causal rule:
+  // image query i sees image key j iff (k_pos0 + j) / gtok <= (q_pos0 + i) / gtok.
+  // Both are 0 for a chunk attending to itself; ring steps pass the shard offsets.
+  int q_pos0, k_pos0;
   float scale_log2;
   const uint32_t* kbits;
   int kwords;
@@ -72,8 +76,9 @@ __device__ TileRange key_tiles(const AttnKParams& p, int q0, int rows = kBM) {
   const int ntk = (p.Lk + kBN - 1) / kBN;
   int img_vis_end = p.Lh + p.Li;
   if (p.gtok > 0 && q_last < p.Li) {
-    const long long lim = static_cast<long long>(q_last / p.gtok + 1) * p.gtok;
-    img_vis_end = p.Lh + static_cast<int>(lim < p.Li ? lim : p.Li);
+    long long lim = static_cast<long long>((p.q_pos0 + q_last) / p.gtok + 1) * p.gtok - p.k_pos0;
+    lim = lim < 0 ? 0 : (lim < p.Li ? lim : p.Li);
+    img_vis_end = p.Lh + static_cast<int>(lim);
   }
   TileRange r;
   r.a_end = min((img_vis_end + kBN - 1) / kBN, ntk);
@@ -315,8 +320,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const uint32_t t_s = t_lane + static_cast<uint32_t>(qi) * 128u;
     const uint32_t t_o = t_lane + kTmemO + static_cast<uint32_t>(qi) * 128u;
     const bool img_row = qrow < p.Li;
-    const int row_lim = (p.gtok > 0 && img_row) ? (qrow / p.gtok + 1) * p.gtok : INT_MAX;
-    const int cta_lim = (p.gtok > 0 && qt0 < p.Li) ? (qt0 / p.gtok + 1) * p.gtok : INT_MAX;
+    // First invisible image key (index relative to the image keys) of this row and of the
+    // tile's first row; negative when the whole image segment is in the future.
+    const int row_lim =
+        (p.gtok > 0 && img_row) ? ((p.q_pos0 + qrow) / p.gtok + 1) * p.gtok - p.k_pos0 : INT_MAX;
+    const int cta_lim =
+        (p.gtok > 0 && qt0 < p.Li) ? ((p.q_pos0 + qt0) / p.gtok + 1) * p.gtok - p.k_pos0 : INT_MAX;
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY;
     float l = 0.f;
@@ -912,6 +921,8 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   kp.Lh = a->hist_len;
   kp.Li = a->img_len;
   kp.gtok = a->group_tokens;
+  kp.q_pos0 = a->q_pos0;
+  kp.k_pos0 = a->k_pos0;
   const float scale = a->softmax_scale > 0.f ? a->softmax_scale : 1.0f / sqrtf(static_cast<float>(kHD));
   kp.scale_log2 = scale * kLog2e;
   kp.kbits = a->kbits;
@@ -1008,8 +1019,8 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   }
   if (Li > 0) {
     if ((rc = check_view(a->img_q, "img_q", false)) != HYB_OK) return rc;
-    if ((rc = check_view(a->img_k, "img_k", false)) != HYB_OK) return rc;
-    if ((rc = check_view(a->img_v, "img_v", false)) != HYB_OK) return rc;
+    if ((rc = check_view(a->img_k, "img_k", true)) != HYB_OK) return rc;
+    if ((rc = check_view(a->img_v, "img_v", true)) != HYB_OK) return rc;
   }
   if (Lt > 0) {
     if ((rc = check_view(a->txt_q, "txt_q", false)) != HYB_OK) return rc;
@@ -1101,6 +1112,8 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   at.img_len = Li;
   at.group_tokens = a->group_tokens;
   at.softmax_scale = a->softmax_scale;
+  at.q_pos0 = a->q_pos0;
+  at.k_pos0 = a->k_pos0;
   at.q = q_all;
   at.k = k_all;
   at.v = v_all;

@@ -88,8 +88,11 @@ typedef struct hyb_cached_attn_args {
   int32_t attend_txt;      /* 1: current text keys are attended (cache_txt or update_cache) */
   int32_t group_tokens;    /* block-causal granularity in tokens (G frames x tokens/frame), 0 = off */
   float softmax_scale;     /* <= 0 selects 1/sqrt(D) */
+  int32_t q_pos0, k_pos0;  /* global positions of image query 0 / image key 0 for the block-causal
+                              rule: query i sees key j iff (k_pos0+j)/G <= (q_pos0+i)/G (0, 0 for a
+                              chunk attending to itself; ring steps pass shard offsets) */
   hyb_tensor4 hist_k, hist_v;                 /* cache: BF16 / E4M3 / INT8 */
-  hyb_tensor4 img_q, img_k, img_v;            /* BF16 [B, img_len, H, D] */
+  hyb_tensor4 img_q, img_k, img_v;            /* Q BF16 [B, img_len, H, D]; K/V BF16, E4M3 or INT8 */
   hyb_tensor4 txt_q, txt_k, txt_v;            /* BF16 [B, txt_len, H, D] */
   const int32_t* hist_rows; /* [valid_len] cache row of composed history position t, or NULL
                                (identity); sink + sliding-window rings use it */
@@ -160,6 +163,7 @@ typedef struct hyb_attn_args {
   int32_t abi_version;
   int32_t B, H, D, Lq, Lk, hist_len, img_len, group_tokens;
   float softmax_scale;
+  int32_t q_pos0, k_pos0;   /* as in hyb_cached_attn_args */
   const void* q; const void* k; const void* v;
   const uint32_t* kbits; int32_t kwords;
   const uint32_t* qbits; int32_t qwords;

@@ -88,6 +88,21 @@ def main():
         if not torch.equal(mask, full_mask):
             print("cache mask mismatch")
             ok = False
+    # ---- ring (KV passing) over all ranks: equals the emulated single-process schedule
+    from hy_nomas_b200 import ring
+    Lr, Tr = 8 * 96, 96
+    rq, rk, rv = (seeded_kv((1, Lr, 4, D), make_generator(77 + i)) for i in range(3))
+    Lsr = Lr // world
+    shard = lambda x, i: x[:, i * Lsr:(i + 1) * Lsr].to(dev)
+    out_ring = ring.ring_attention(shard(rq, rank), shard(rk, rank), shard(rv, rank), None, tokens_per_frame=Tr)
+    emu = ring.ring_attention_emulated([shard(rq, i) for i in range(world)], [shard(rk, i) for i in range(world)],
+                                       [shard(rv, i) for i in range(world)], tokens_per_frame=Tr)
+    if not torch.equal(out_ring, emu[rank]):
+        print("ring mismatch on rank", rank, (out_ring.float() - emu[rank].float()).abs().max().item())
+        ok = False
+    ok_t = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
+    ok = bool(ok_t.item())
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.broadcast(flag, 0)
     ps.destroy_sequence_parallel_group()

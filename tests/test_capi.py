@@ -42,7 +42,8 @@ int main(void) {
   printf("hyb_cached_attn_args %zu\n", sizeof(hyb_cached_attn_args));
   printf("hyb_attn_args %zu\n", sizeof(hyb_attn_args));
   F(hyb_tensor4, scale) F(hyb_tensor4, ss_h)
-  F(hyb_cached_attn_args, softmax_scale) F(hyb_cached_attn_args, hist_k) F(hyb_cached_attn_args, txt_v)
+  F(hyb_cached_attn_args, softmax_scale) F(hyb_cached_attn_args, k_pos0) F(hyb_cached_attn_args, hist_k)
+  F(hyb_cached_attn_args, txt_v) F(hyb_attn_args, k_pos0)
   F(hyb_cached_attn_args, hist_rows) F(hyb_cached_attn_args, cache_mask) F(hyb_cached_attn_args, oi_seg)
   F(hyb_cached_attn_args, out_txt) F(hyb_cached_attn_args, lse) F(hyb_cached_attn_args, workspace_bytes)
   F(hyb_cached_attn_args, dev_status)

@@ -107,3 +107,31 @@ def test_lse_merge_kernel_matches_oracle(cuda_lib):
     torch.testing.assert_close(acc.cpu().double(), ref_out, rtol=1e-5, atol=1e-5)
     # and against the reference's own merged output
     torch.testing.assert_close(acc.cpu().double(), torch.from_numpy(g["out"])[0], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("P,frames,T", [(1, 5, 64), (4, 21, 48), (3, 7, 100)])
+def test_ring_schedule_matches_frame_causal_oracle(cuda_lib, P, frames, T):
+    """The ring's per-step attention + LSE merge over P emulated ranks equals frame-causal
+    attention over the whole sequence (shards not aligned to frames when L / P % T != 0)."""
+    from hy_nomas_b200 import ring
+    from oracle import attention as oatt
+    from oracle import quant as oq
+    dev = torch.device("cuda")
+    H, L = 2, frames * T
+    L -= L % P
+    Ls = L // P
+    gen = make_generator(900 + P)
+    q, k, v = (seeded_kv((1, L, H, 128), gen) for _ in range(3))
+    sh = lambda x: [x[:, i * Ls:(i + 1) * Ls].to(dev) for i in range(P)]
+    outs = ring.ring_attention_emulated(sh(q), sh(k), sh(v), tokens_per_frame=T)
+    got = torch.cat([o.cpu() for o in outs], dim=1)
+    # keys and values as the blocks carry them: e4m3 per shard, decoded
+    kd = torch.cat([oq.dequantize(*oq.quantize_e4m3(k[:, i * Ls:(i + 1) * Ls])) for i in range(P)], 1)
+    vd = torch.cat([oq.dequantize(*oq.quantize_e4m3(v[:, i * Ls:(i + 1) * Ls])) for i in range(P)], 1)
+    e = q[:, :0]
+    ref, _, (mag, _) = oatt.cached_attention(q, kd, vd, e, e, e, kd[:, :0], vd[:, :0], attend_txt=False,
+                                             group_tokens=T, return_magnitude=True)
+    o, r = got.float().flatten(), ref.flatten()
+    bound = 2e-2 + 2.0 ** -7 * r.abs() + 2.0 ** -8 * mag.flatten()
+    assert ((o - r).abs() <= bound).all(), ((o - r).abs() - bound).max()
+    assert torch.nn.functional.cosine_similarity(o[None], r[None]).item() >= 0.9995
