@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config2", choices=["config2", "ring"],
+                    help="config2: 4-frame chunk vs 16-frame FP8 cache (Ulysses for N > 1); "
+                         "ring: config 3, 32,760-token frame-causal sequence, ring SP over N ranks")
     return ap.parse_args()
 
 
@@ -310,6 +313,143 @@ def run_b200(args):
     print(json.dumps(line), flush=True)
 
 
+RING_FRAMES = 21
+RING_METRIC = "chunk-causal attn TFLOP/s (config 3: ring SP, 21 x 1560-token frame-causal sequence, FP8 KV blocks)"
+
+
+def run_ring(args):
+    """Config 3: frame-causal self-attention of 21 frames x 1560 tokens (32,760), 24 heads,
+    zig-zag sharded over N ranks; FP8 K/V blocks travel the ring (strong scaling)."""
+    from hy_nomas_b200 import _lib
+    from hy_nomas_b200 import ring
+    from hy_nomas_b200.flops import attention_flops
+    from hy_nomas_b200.synthetic import make_generator, seeded_kv
+    import torch.distributed as dist
+
+    rank, world, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    L = RING_FRAMES * T
+    plan = ring.RingPlan(L, world, "zigzag")
+    gen = make_generator(1237, device=device)
+    # the same global sequence on every rank (seeded), each rank keeps its shard
+    full = [seeded_kv((1, L, H_TOTAL, D), gen, device=device) for _ in range(3)]
+    q, k, v = (plan.shard(x, rank).contiguous() for x in full)
+    del full
+    torch.cuda.empty_cache()
+    flops_total = attention_flops(0, L, 0, H_TOTAL, D, False, T)
+    group = None
+    state = ring.ring_plan_state(q, seq_len=L, world=world, rank=rank, tokens_per_frame=T)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(device)
+
+    def step(q_, k_, v_):
+        return ring.ring_attention(q_, k_, v_, group, seq_len=L, tokens_per_frame=T, out=out)
+
+    for _ in range(args.warmup):
+        step(q, k, v)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(q, k, v)
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    launches_per_step = state.launches
+    # attention launches alone (events on the caller's stream after each step's input is ready)
+    state.event_log = []
+    for _ in range(max(1, args.steps // 2)):
+        step(q, k, v)
+    torch.cuda.synchronize(device)
+    n_timed = max(1, args.steps // 2)
+    kern_ms = sum(a.elapsed_time(b) for a, b in state.event_log) / n_timed
+    state.event_log = None
+    if world > 1:
+        tt = torch.tensor([ms, kern_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms, kern_ms_max = tt.tolist()
+    else:
+        kern_ms_max = kern_ms
+    _lib.check_device_status(device)
+    value = flops_total / (ms * 1e-3) / 1e12
+
+    # end to end: pinned host shards in, output shard back, every step
+    host_in = [t.cpu().pin_memory() for t in (q, k, v)]
+    host_out = torch.empty(out.shape, dtype=torch.bfloat16).pin_memory()
+    dev_in = [torch.empty_like(t, device=device) for t in host_in]
+
+    def e2e_step():
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+        o = step(*dev_in)
+        host_out.copy_(o, non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    ems = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ems], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ems = tt.item()
+    h2d = sum(t.numel() * t.element_size() for t in host_in) * world
+    d2h = host_out.numel() * 2 * world
+    peak_bf16, _, peak_src = load_peaks()
+    local_flops = flops_total / world
+    achieved = local_flops / (kern_ms * 1e-3) / 1e12
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": RING_METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 MMA / fp32 softmax; e4m3 KV blocks on the ring",
+        "data": "synthetic (seeded N(0,1), 4 outlier channels/head x8)",
+        "config": {"workload": "config 3: ring SP, 21 frames x 1560 tokens, frame-causal", "heads": H_TOTAL,
+                   "head_dim": D, "seq_len": L, "tokens_per_frame": T, "layout": "zig-zag (2N chunks)",
+                   "parallelism": f"ring_sp{world}" if world > 1 else "single",
+                   "kv_block": "fp8_e4m3 codes + fp32 per-(token, head) scales, quantised each step",
+                   "l2": "inputs larger than L2 (201 MB bf16 per tensor over the job)",
+                   "tflop_per_step": round(flops_total / 1e12, 4)},
+        "gpu_launches": launches_per_step * args.steps,
+        "e2e": {"value": round(flops_total / (ems * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "ms_per_step": round(ems, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_bf16, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak_bf16, 4), "traffic": None,
+                     "kernel": "attn_fwd2_kernel ring steps (tcgen05 kind::f16, bf16 operands)",
+                     "kernel_ms_per_step": round(kern_ms, 4), "kernel_ms_max_rank": round(kern_ms_max, 4),
+                     "peak_source": f"{peak_src} bf16 dense (cuBLAS)",
+                     "algorithmic_unit": "4*H*D FLOP per visible (query, key) pair"},
+        "cpu_baseline": None,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def time_attention_kernel(prob, device, iters):
     """CUDA-event time of the attention kernel launch alone on the staged workspace."""
     from hy_nomas_b200 import _lib
@@ -416,6 +556,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "ring":
+        run_ring(args)
     else:
         run_b200(args)
 

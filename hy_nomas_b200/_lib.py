@@ -16,7 +16,7 @@ import torch
 PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libhyb200.so"
 
-HYB_ABI_VERSION = 1
+HYB_ABI_VERSION = 2
 
 HYB_OK = 0
 HYB_ERR_INVALID_ARG = -1
@@ -77,6 +77,8 @@ class AttnArgs(ctypes.Structure):
         ("abi_version", c_i32), ("B", c_i32), ("H", c_i32), ("D", c_i32), ("Lq", c_i32),
         ("Lk", c_i32), ("hist_len", c_i32), ("img_len", c_i32), ("group_tokens", c_i32),
         ("softmax_scale", ctypes.c_float), ("q_pos0", c_i32), ("k_pos0", c_i32),
+        ("img_k_len", c_i32), ("q_seg", c_i32), ("q_pos1", c_i32), ("k_seg", c_i32), ("k_pos1", c_i32),
+        ("pad1_", c_i32),
         ("q", c_ptr), ("k", c_ptr), ("v", c_ptr),
         ("kbits", c_ptr), ("kwords", c_i32),
         ("qbits", c_ptr), ("qwords", c_i32),
@@ -85,6 +87,7 @@ class AttnArgs(ctypes.Structure):
         ("out_txt", c_ptr), ("ot_sb", c_i64), ("ot_st", c_i64), ("ot_sh", c_i64),
         ("lse", c_ptr), ("dev_status", c_ptr),
         ("kv_splits", c_i32), ("pad_", c_i32), ("part_o", c_ptr), ("part_lse", c_ptr),
+        ("acc_o", c_ptr), ("acc_lse", c_ptr), ("acc_mode", c_i32), ("pad2_", c_i32),
     ]
 
 
@@ -101,6 +104,9 @@ class WorkspaceLayout(ctypes.Structure):
 
 # name -> (restype, argtypes); every symbol declared in include/hyb200.h
 SIGNATURES = {
+    "hyb_stage_head_major": (c_i32, [c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(Tensor4),
+                                     ctypes.POINTER(Tensor4), c_ptr, c_ptr, c_ptr]),
+    "hyb_fill_key_bits": (c_i32, [c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "hyb_version": (c_i32, []),
     "hyb_last_error": (c_i32, [ctypes.c_char_p, ctypes.c_size_t]),
     "hyb_device_supported": (c_i32, []),

@@ -38,11 +38,14 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
 struct AttnKParams {
-  int B, H, Lq, Lk, Lh, Li, gtok;
-  // Global token positions of image query 0 and image key 0 for the block-causal rule:
-  // image query i sees image key j iff (k_pos0 + j) / gtok <= (q_pos0 + i) / gtok.
-  // Both are 0 for a chunk attending to itself; ring steps pass the shard offsets.
-  int q_pos0, k_pos0;
+  // Lq queries: Li image rows then text rows.  Lk keys: Lh history, Lik image, then text.
+  int B, H, Lq, Lk, Lh, Li, Lik, gtok;
+  // Global token positions for the block-causal rule: image query i sees image key j iff
+  // kpos(j) / gtok <= qpos(i) / gtok.  Positions come in up to two increasing segments
+  // (a zig-zag ring shard holds two chunks of the sequence): qpos(i) = q_pos0 + i for
+  // i < q_seg, else q_pos1 + (i - q_seg); kpos likewise with k_seg / k_pos1.  A chunk
+  // attending to itself has one segment at 0.
+  int q_pos0, k_pos0, q_seg, q_pos1, k_seg, k_pos1;
   float scale_log2;
   const uint32_t* kbits;
   int kwords;
@@ -61,7 +64,54 @@ struct AttnKParams {
   int kv_splits;
   float* part_o;
   float* part_lse;
+  // Ring accumulator (all queries image rows): acc_o fp32 [B, Lq, H, 128], acc_lse fp32
+  // [B, H, Lq].  acc_mode bit 0: merge with its contents; bit 1: write the merged rows as
+  // bf16 to out_img (+ lse) instead of back to the accumulator.
+  float* acc_o;
+  float* acc_lse;
+  int acc_mode;
 };
+
+__device__ __forceinline__ long long q_position(const AttnKParams& p, int i) {
+  return i < p.q_seg ? static_cast<long long>(p.q_pos0) + i : static_cast<long long>(p.q_pos1) + (i - p.q_seg);
+}
+
+// Image keys visible to an image query at global position qpos.  Key positions increase with
+// the key index, so the visible image keys are the prefix [0, count).
+__device__ __forceinline__ int img_keys_visible(const AttnKParams& p, long long qpos) {
+  const long long lim = (qpos / p.gtok + 1) * p.gtok;  // first position of a later group
+  long long a = lim - p.k_pos0;
+  a = a < 0 ? 0 : (a > p.k_seg ? p.k_seg : a);
+  const long long n1 = p.Lik - p.k_seg;
+  long long c = lim - p.k_pos1;
+  c = c < 0 ? 0 : (c > n1 ? n1 : c);
+  return static_cast<int>(a + c);
+}
+
+// Log-sum-exp merge of a running ring output (LSE lse_a) with one step's normalised rows
+// (LSE lse_b): merged = wa * acc + wb * step, LSE of the union.  Both weights are zero when
+// neither side has seen a visible key.
+struct AccWeights {
+  float wa, wb, lse;
+};
+__device__ __forceinline__ AccWeights acc_weights(float lse_a, float lse_b) {
+  AccWeights w;
+  const float m = fmaxf(lse_a, lse_b);
+  if (m == -INFINITY) {
+    w.wa = 0.f;
+    w.wb = 0.f;
+    w.lse = -INFINITY;
+    return w;
+  }
+  const float ea = __expf(lse_a - m);
+  const float eb = __expf(lse_b - m);
+  const float sum = ea + eb;
+  const float inv = 1.f / sum;
+  w.wa = ea * inv;
+  w.wb = eb * inv;
+  w.lse = m + __logf(sum);
+  return w;
+}
 
 // Key tiles visited by one query tile: [0, a_end) then [b_begin, b_end).
 // Image keys past the block-causal limit of the tile's last row are never loaded.
@@ -74,15 +124,11 @@ struct TileRange {
 __device__ TileRange key_tiles(const AttnKParams& p, int q0, int rows = kBM) {
   const int q_last = min(q0 + rows, p.Lq) - 1;
   const int ntk = (p.Lk + kBN - 1) / kBN;
-  int img_vis_end = p.Lh + p.Li;
-  if (p.gtok > 0 && q_last < p.Li) {
-    long long lim = static_cast<long long>((p.q_pos0 + q_last) / p.gtok + 1) * p.gtok - p.k_pos0;
-    lim = lim < 0 ? 0 : (lim < p.Li ? lim : p.Li);
-    img_vis_end = p.Lh + static_cast<int>(lim);
-  }
+  int img_vis_end = p.Lh + p.Lik;
+  if (p.gtok > 0 && q_last < p.Li) img_vis_end = p.Lh + img_keys_visible(p, q_position(p, q_last));
   TileRange r;
   r.a_end = min((img_vis_end + kBN - 1) / kBN, ntk);
-  const int txt_begin = p.Lh + p.Li;
+  const int txt_begin = p.Lh + p.Lik;
   if (txt_begin < p.Lk) {
     r.b_begin = max(txt_begin / kBN, r.a_end);
     r.b_end = ntk;
@@ -322,10 +368,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const bool img_row = qrow < p.Li;
     // First invisible image key (index relative to the image keys) of this row and of the
     // tile's first row; negative when the whole image segment is in the future.
-    const int row_lim =
-        (p.gtok > 0 && img_row) ? ((p.q_pos0 + qrow) / p.gtok + 1) * p.gtok - p.k_pos0 : INT_MAX;
-    const int cta_lim =
-        (p.gtok > 0 && qt0 < p.Li) ? ((p.q_pos0 + qt0) / p.gtok + 1) * p.gtok - p.k_pos0 : INT_MAX;
+    const int row_lim = (p.gtok > 0 && img_row) ? img_keys_visible(p, q_position(p, qrow)) : INT_MAX;
+    const int cta_lim = (p.gtok > 0 && qt0 < p.Li) ? img_keys_visible(p, q_position(p, qt0)) : INT_MAX;
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY;
     float l = 0.f;
@@ -350,12 +394,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
       // Mask: visibility bits of the tile's keys, then this row's block-causal interval
       // [ca, cb) of invisible image keys.
       const bool causal_tile = (cta_lim != INT_MAX) && (k0 + kBN > p.Lh + cta_lim) &&
-                               (k0 < p.Lh + p.Li);
+                               (k0 < p.Lh + p.Lik);
       if (causal_tile || (w[0] & w[1] & w[2] & w[3]) != 0xffffffffu) {
         int ca = kBN, cb = 0;
         if (row_lim != INT_MAX) {
           ca = min(max(p.Lh + row_lim - k0, 0), kBN);
-          cb = min(max(p.Lh + p.Li - k0, 0), kBN);
+          cb = min(max(p.Lh + p.Lik - k0, 0), kBN);
         }
 #pragma unroll
         for (int c = 0; c < kBN; ++c) {
@@ -457,6 +501,64 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
         }
         if (in_range) p.part_lse[prow] = l > 0.f ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+      } else if (p.acc_o != nullptr) {
+        // Ring step: merge this launch's rows into the running output.
+        const bool merge = (p.acc_mode & 1) != 0;
+        const bool fin = (p.acc_mode & 2) != 0;
+        const size_t lrow = static_cast<size_t>(bh) * p.Lq + qrow;
+        const float lse_b = l > 0.f ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+        const float lse_a = (in_range && merge) ? p.acc_lse[lrow] : -INFINITY;
+        const AccWeights aw = acc_weights(lse_a, lse_b);
+        const float cb = l > 0.f ? aw.wb * __frcp_rn(l) : 0.f;
+        float* arow = in_range ? p.acc_o + ((static_cast<size_t>(b) * p.Lq + qrow) * p.H + h) * kHD : nullptr;
+        __nv_bfloat16* dst = (in_range && fin) ? p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg +
+                                                     (qrow % p.oi_seg) * p.oi_t + h * p.oi_h
+                                               : nullptr;
+        const bool read_acc = arow != nullptr && aw.wa != 0.f;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t r[32];
+          if (have_o) {
+            tmem_ld32_wait(t_o + c4 * 32, r);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
+          }
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * cb;
+          if (read_acc) {
+            const float4* s4 = reinterpret_cast<const float4*>(arow + c4 * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 a4 = s4[i];
+              v[4 * i] = fmaf(aw.wa, a4.x, v[4 * i]);
+              v[4 * i + 1] = fmaf(aw.wa, a4.y, v[4 * i + 1]);
+              v[4 * i + 2] = fmaf(aw.wa, a4.z, v[4 * i + 2]);
+              v[4 * i + 3] = fmaf(aw.wa, a4.w, v[4 * i + 3]);
+            }
+          }
+          if (fin) {
+            if (dst != nullptr) {
+              uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                d4[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                                   pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+            }
+          } else if (arow != nullptr) {
+            float4* d4 = reinterpret_cast<float4*>(arow + c4 * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          }
+        }
+        if (in_range) {
+          if (!fin) {
+            p.acc_lse[lrow] = aw.lse;
+          } else if (p.lse != nullptr) {
+            p.lse[lrow] = aw.lse;
+          }
+        }
       } else {
         bool valid = in_range;
         if (in_range && p.qbits != nullptr)
@@ -536,6 +638,34 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const AttnKParams p) 
         acc.z += w * o.z;
         acc.w += w * o.w;
       }
+    }
+    if (p.acc_o != nullptr) {
+      // Ring step: the merged slices are this step's rows; fold them into the accumulator.
+      const bool merge = (p.acc_mode & 1) != 0;
+      const bool fin = (p.acc_mode & 2) != 0;
+      const float lse_b = wsum > 0.f ? m + __logf(wsum) : -INFINITY;
+      const AccWeights aw = acc_weights(merge ? p.acc_lse[r] : -INFINITY, lse_b);
+      const float cb = wsum > 0.f ? aw.wb / wsum : 0.f;
+      float* arow = p.acc_o + ((static_cast<size_t>(b) * p.Lq + qrow) * p.H + h) * kHD;
+      float4 v = make_float4(acc.x * cb, acc.y * cb, acc.z * cb, acc.w * cb);
+      if (aw.wa != 0.f) {
+        const float4 a4 = reinterpret_cast<const float4*>(arow)[lane];
+        v.x = fmaf(aw.wa, a4.x, v.x);
+        v.y = fmaf(aw.wa, a4.y, v.y);
+        v.z = fmaf(aw.wa, a4.z, v.z);
+        v.w = fmaf(aw.wa, a4.w, v.w);
+      }
+      if (fin) {
+        __nv_bfloat16* dst = p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg + (qrow % p.oi_seg) * p.oi_t +
+                             h * p.oi_h;
+        *reinterpret_cast<uint2*>(dst + lane * 4) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+        if (p.lse != nullptr && lane == 0) p.lse[r] = aw.lse;
+      } else {
+        reinterpret_cast<float4*>(arow)[lane] = v;
+        __syncwarp();
+        if (lane == 0) p.acc_lse[r] = aw.lse;
+      }
+      continue;
     }
     const float inv = (wsum > 0.f && valid) ? 1.f / wsum : 0.f;
     __nv_bfloat16* dst = qrow < p.Li
@@ -637,6 +767,24 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
         *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out[o]) + out_off) = packed;
       }
     }
+  }
+}
+
+// Visibility bitmap with the first Lk keys of every batch row set (ring blocks: every key
+// of the block is valid; the block-causal rule is applied by the attention kernel).
+__global__ void __launch_bounds__(256) key_bits_kernel(int B, int Lk, int kwords, uint32_t* bits) {
+  const long long n = static_cast<long long>(B) * kwords;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int w = static_cast<int>(i % kwords);
+    const int lo = w * 32;
+    uint32_t word = 0u;
+    if (Lk >= lo + 32) {
+      word = 0xffffffffu;
+    } else if (Lk > lo) {
+      word = (1u << (Lk - lo)) - 1u;
+    }
+    bits[i] = word;
   }
 }
 
@@ -890,9 +1038,20 @@ int launch_attn2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap
 
 int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   if (a->D != kHD) return fail(HYB_ERR_UNSUPPORTED, "attention: head_dim %d != 128", a->D);
+  const int Lik = a->img_k_len > 0 ? a->img_k_len : a->img_len;
   if (a->B <= 0 || a->H <= 0 || a->Lq < 0 || a->Lk < 0 || a->hist_len < 0 || a->img_len < 0 ||
-      a->hist_len + a->img_len > a->Lk || a->img_len > a->Lq || a->group_tokens < 0)
+      a->img_k_len < 0 || a->hist_len + Lik > a->Lk || a->img_len > a->Lq || a->group_tokens < 0)
     return fail(HYB_ERR_INVALID_ARG, "attention: inconsistent sizes");
+  const bool two_q = a->q_seg > 0 && a->q_seg < a->img_len;
+  const bool two_k = a->k_seg > 0 && a->k_seg < Lik;
+  if ((two_q && static_cast<long long>(a->q_pos1) < static_cast<long long>(a->q_pos0) + a->q_seg) ||
+      (two_k && static_cast<long long>(a->k_pos1) < static_cast<long long>(a->k_pos0) + a->k_seg) ||
+      a->q_pos0 < 0 || a->k_pos0 < 0 || (two_q && a->q_pos1 < 0) || (two_k && a->k_pos1 < 0))
+    return fail(HYB_ERR_INVALID_ARG, "attention: position segments must be nonnegative and increasing");
+  if (a->acc_o != nullptr &&
+      (a->acc_lse == nullptr || !al16(a->acc_o) || a->Lq != a->img_len || a->acc_mode < 0 || a->acc_mode > 3))
+    return fail(HYB_ERR_INVALID_ARG,
+                "attention: the ring accumulator needs acc_lse, 16-byte alignment, image queries only, mode 0..3");
   if (a->Lq == 0) return HYB_OK;
   if (!al16(a->q) || !al16(a->k) || !al16(a->v)) return fail(HYB_ERR_INVALID_ARG, "attention: q/k/v misaligned");
   if (a->kwords < ((a->Lk + kBN - 1) / kBN) * (kBN / 32) || (a->kwords % 4) != 0 || !al16(a->kbits))
@@ -920,9 +1079,17 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   kp.Lk = a->Lk;
   kp.Lh = a->hist_len;
   kp.Li = a->img_len;
+  kp.Lik = Lik;
   kp.gtok = a->group_tokens;
   kp.q_pos0 = a->q_pos0;
   kp.k_pos0 = a->k_pos0;
+  kp.q_seg = two_q ? a->q_seg : a->img_len;
+  kp.q_pos1 = two_q ? a->q_pos1 : 0;
+  kp.k_seg = two_k ? a->k_seg : Lik;
+  kp.k_pos1 = two_k ? a->k_pos1 : 0;
+  kp.acc_o = a->acc_o;
+  kp.acc_lse = a->acc_lse;
+  kp.acc_mode = a->acc_mode;
   const float scale = a->softmax_scale > 0.f ? a->softmax_scale : 1.0f / sqrtf(static_cast<float>(kHD));
   kp.scale_log2 = scale * kLog2e;
   kp.kbits = a->kbits;
@@ -964,6 +1131,43 @@ extern "C" int hyb_attn_fwd(const hyb_attn_args* a, void* stream) {
   if (a == nullptr || a->abi_version != HYB_ABI_VERSION)
     return fail(HYB_ERR_INVALID_ARG, "attention: null args or ABI version mismatch");
   return attn_core(a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hyb_stage_head_major(int32_t B, int32_t L, int32_t H, int32_t D, const hyb_tensor4* src_k,
+                                    const hyb_tensor4* src_v, void* dst_k, void* dst_v, void* stream) {
+  if (D != kHD) return fail(HYB_ERR_UNSUPPORTED, "stage: head_dim %d != 128", D);
+  if (B <= 0 || H <= 0 || L < 0 || src_k == nullptr || dst_k == nullptr || ((src_v == nullptr) != (dst_v == nullptr)))
+    return fail(HYB_ERR_INVALID_ARG, "stage: bad sizes or null tensors");
+  if (L == 0) return HYB_OK;
+  int rc;
+  if ((rc = check_view(*src_k, "stage src_k", true)) != HYB_OK) return rc;
+  if (src_v != nullptr && (rc = check_view(*src_v, "stage src_v", true)) != HYB_OK) return rc;
+  if (!al16(dst_k) || (dst_v != nullptr && !al16(dst_v)))
+    return fail(HYB_ERR_INVALID_ARG, "stage: destinations must be 16-byte aligned");
+  StageParams sp{};
+  sp.B = B;
+  sp.H = H;
+  sp.L = L;
+  sp.nout = src_v != nullptr ? 2 : 1;
+  sp.nseg = 1;
+  sp.seg[0][0] = seg_of(*src_k, L, 0);
+  if (src_v != nullptr) sp.seg[1][0] = seg_of(*src_v, L, 0);
+  sp.out[0] = dst_k;
+  sp.out[1] = dst_v;
+  stage_kernel<<<grid_for(static_cast<long long>(B) * H * L * 16, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      sp);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
+
+extern "C" int hyb_fill_key_bits(int32_t B, int32_t Lk, int32_t kwords, uint32_t* bits, void* stream) {
+  if (B <= 0 || Lk < 0 || kwords < 0 || static_cast<long long>(kwords) * 32 < Lk || (bits == nullptr && kwords > 0))
+    return fail(HYB_ERR_INVALID_ARG, "key bits: %d words cannot hold %d keys", kwords, Lk);
+  if (kwords == 0) return HYB_OK;
+  key_bits_kernel<<<grid_for(static_cast<long long>(B) * kwords, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      B, Lk, kwords, bits);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
 }
 
 extern "C" int64_t hyb_cached_attention_workspace_bytes(int32_t B, int32_t H, int32_t D, int32_t valid_len,
@@ -1101,7 +1305,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     return HYB_OK;
   }
 
-  hyb_attn_args at;
+  hyb_attn_args at{};
   at.abi_version = HYB_ABI_VERSION;
   at.B = a->B;
   at.H = a->H;

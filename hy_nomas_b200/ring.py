@@ -1,45 +1,114 @@
 """Ring (KV-passing) sequence parallelism with frame-level causal masking.
 
-Each rank holds a contiguous shard of the sequence (queries, keys and values).  Its keys and
-values are quantised once to an e4m3 (or int8) block — codes and per-(token, head) scales in
-one byte buffer — and the blocks travel around the ring: at step s a rank attends its queries
-to the block of rank (r - s) mod P while NCCL moves the next block from rank r - 1 into the
-other half of a double buffer (point-to-point copies over NVLink on a side stream, overlapped
-with the attention of the current block).  Partial outputs are merged by log-sum-exp.
+The sequence of ``seq_len`` tokens is sharded over the P ranks of a group.  The default
+layout is zig-zag: the sequence is cut into 2P near-equal chunks and rank r holds chunks r
+and 2P-1-r (concatenated in that order), so that under the causal mask every rank does the
+same work.  ``layout="contiguous"`` gives rank r the r-th of P chunks.
+
+Each rank quantises its own K/V once into an e4m3 (or int8) block: codes and per-(token,
+head) scales in one byte buffer, the message of one ring hop.  At step s rank r attends its
+queries to the block of rank (r - s) mod P while NCCL moves the next block from rank r - 1
+into the other half of a double buffer.  The transfer and the decode of the received block
+into head-major bf16 tiles run on a side stream, overlapped with the current step's
+attention on the caller's stream; the two streams are joined by events, with no host sync.
+Every step is one attention launch whose epilogue merges its rows into a running fp32
+output by log-sum-exp (the last step writes the bf16 output), so no separate merge pass
+runs between steps.
 
 Transport and merge follow the reference's ring (``DynamicRingAttention.forward``,
 hymm/models/dit/modules/attention/dynamic_ring_attention.py:115-286: isend/irecv to
-``(idx + 1) % P`` / from ``(idx - 1) % P``, double-buffered, ``flash_attn_fwd_out_correction``
-/ ``_softmax_lse_correction`` merges :86-105).  The reference ring is non-causal and serves
-the non-cached path; the frame-level causal mask is the chunk-causal rule of
+``(idx + 1) % P`` / from ``(idx - 1) % P``, double-buffered; ``flash_attn_fwd_out_correction``
+/ ``_softmax_lse_correction`` merges :86-105).  The reference ring is non-causal and carries
+bf16 K/V; the frame-level causal mask is the chunk-causal rule of
 ``create_magi_mp_causal_ranges`` (attention/magi_attn.py:290-309): query frame f sees key
 frames <= f.  Blocks entirely in a query shard's future are not computed.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
 from . import _lib
-from . import attention as _att
 from . import kv_cache as _kvc
 
 _FMT = {"fp8_e4m3": (_lib.HYB_FMT_E4M3, torch.float8_e4m3fn), "int8": (_lib.HYB_FMT_INT8, torch.int8)}
+_D = 128
+
+
+class RingPlan:
+    """Token ownership of a ring over ``world`` ranks: per rank one or two contiguous segments
+    of the global sequence, in increasing position order."""
+
+    def __init__(self, seq_len: int, world: int, layout: str = "zigzag"):
+        if seq_len < 0 or world <= 0:
+            raise ValueError("ring plan needs seq_len >= 0 and world >= 1")
+        if layout not in ("zigzag", "contiguous"):
+            raise ValueError(f"unknown ring layout {layout!r}")
+        self.seq_len, self.world, self.layout = seq_len, world, layout
+        n = 2 * world if layout == "zigzag" else world
+        bounds = [(i * seq_len) // n for i in range(n + 1)]
+        chunk = [(bounds[i], bounds[i + 1] - bounds[i]) for i in range(n)]
+        if layout == "zigzag":
+            self.segments = [(chunk[r], chunk[n - 1 - r]) for r in range(world)]
+        else:
+            self.segments = [(chunk[r], (bounds[r + 1], 0)) for r in range(world)]
+
+    def length(self, rank: int) -> int:
+        return sum(n for _, n in self.segments[rank])
+
+    def max_length(self) -> int:
+        return max(self.length(r) for r in range(self.world))
+
+    def positions(self, rank: int):
+        """(seg0_len, pos0, pos1) of the rank's tokens: token i is at pos0 + i for i < seg0_len,
+        else at pos1 + (i - seg0_len)."""
+        (p0, n0), (p1, _) = self.segments[rank]
+        return n0, p0, p1
+
+    def shard(self, x: torch.Tensor, rank: int, dim: int = 1) -> torch.Tensor:
+        parts = [x.narrow(dim, p, n) for p, n in self.segments[rank] if n > 0]
+        if not parts:
+            return x.narrow(dim, 0, 0)
+        return torch.cat(parts, dim) if len(parts) > 1 else parts[0]
+
+    def unshard(self, shards, dim: int = 1) -> torch.Tensor:
+        pieces = []
+        for r, s in enumerate(shards):
+            off = 0
+            for p, n in self.segments[r]:
+                if n > 0:
+                    pieces.append((p, s.narrow(dim, off, n)))
+                off += n
+        pieces.sort(key=lambda t: t[0])
+        return torch.cat([t for _, t in pieces], dim)
+
+    def visible(self, q_rank: int, k_rank: int, group_tokens: int) -> bool:
+        """False when every key of k_rank's shard is in a later causal group than every query of
+        q_rank's shard (the step is skipped)."""
+        if group_tokens <= 0:
+            return True
+        q_last = max(p + n - 1 for p, n in self.segments[q_rank] if n > 0) if self.length(q_rank) else -1
+        k_first = min(p for p, n in self.segments[k_rank] if n > 0) if self.length(k_rank) else None
+        if q_last < 0 or k_first is None:
+            return False
+        return k_first // group_tokens <= q_last // group_tokens
 
 
 class KVBlock:
-    """Quantised K/V of one shard in a single contiguous byte buffer (one P2P message)."""
+    """Quantised K/V of one shard in a single contiguous byte buffer (one P2P message), sized
+    for ``L`` tokens; a shard of fewer tokens uses the leading rows."""
 
-    def __init__(self, L: int, H: int, device, fmt: str = "fp8_e4m3", buf: torch.Tensor | None = None):
+    def __init__(self, L: int, H: int, device, fmt: str = "fp8_e4m3"):
         self.L, self.H, self.fmt = L, H, fmt
         self.code_fmt, dtype = _FMT[fmt]
-        n_codes = L * H * 128
+        n_codes = L * H * _D
         n_scale = L * H * 4
-        self.nbytes = 2 * (n_codes + n_scale)
-        self.buf = buf if buf is not None else torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+        self.buf = torch.empty(2 * (n_codes + n_scale), dtype=torch.uint8, device=device)
         b = self.buf
-        self.k = b[:n_codes].view(dtype).view(1, L, H, 128)
-        self.v = b[n_codes:2 * n_codes].view(dtype).view(1, L, H, 128)
+        self.k = b[:n_codes].view(dtype).view(1, L, H, _D)
+        self.v = b[n_codes:2 * n_codes].view(dtype).view(1, L, H, _D)
         self.k_scale = b[2 * n_codes:2 * n_codes + n_scale].view(torch.float32).view(1, L, H, 1)
         self.v_scale = b[2 * n_codes + n_scale:].view(torch.float32).view(1, L, H, 1)
 
@@ -50,91 +119,221 @@ class KVBlock:
         return d
 
     def fill(self, k: torch.Tensor, v: torch.Tensor) -> None:
-        """Quantise-on-write of this shard's bf16 K/V (assumed finite)."""
+        """Quantise-on-write of this shard's bf16 K/V into rows [0, len) (assumed finite)."""
         _kvc.quantize_kv_pair_into(self.cache(), k, v, 0, assume_finite=True)
 
 
-def frames_visible(q_start: int, q_len: int, k_start: int, group_tokens: int) -> bool:
-    """False when every key of the block lies in a later causal group than every query."""
-    if group_tokens <= 0 or q_len == 0:
-        return True
-    return k_start // group_tokens <= (q_start + q_len - 1) // group_tokens
+class RingAttention:
+    """Buffers and launch state of one ring geometry (plan, heads, device, KV format).
+    ``__call__`` runs one ring pass; ``steps`` lists the ring steps this rank computes."""
+
+    def __init__(self, plan: RingPlan, rank: int, heads: int, device, *, tokens_per_frame: int,
+                 causal_frames: int = 1, kv_format: str = "fp8_e4m3", softmax_scale: float | None = None):
+        self.plan, self.rank, self.H, self.device = plan, rank, heads, torch.device(device)
+        self.G = int(causal_frames) * int(tokens_per_frame)
+        self.scale = float(softmax_scale) if softmax_scale else 0.0
+        self.kv_format = kv_format
+        self.lib = _lib.load()
+        P, H, dev = plan.world, heads, self.device
+        Lmax = plan.max_length()
+        self.Lmax = Lmax
+        self.blocks = [KVBlock(Lmax, H, dev, kv_format), KVBlock(Lmax, H, dev, kv_format)]
+        # head-major bf16 operands: K at [0], V at [1], each [H, L_src, 128] in its region
+        self.kvh = [torch.empty((2, H * Lmax * _D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        Ls = plan.length(rank)
+        self.Ls = Ls
+        self.qh = torch.empty((H * max(Ls, 1) * _D,), dtype=torch.bfloat16, device=dev)
+        self.acc = torch.empty((max(Ls, 1), H, _D), dtype=torch.float32, device=dev)
+        self.acc_lse = torch.empty((H, max(Ls, 1)), dtype=torch.float32, device=dev)
+        self.kwords = ((Lmax + 127) // 128) * 4
+        self.bits = {}
+        with torch.cuda.device(dev):
+            stream = _lib.stream_ptr(dev)
+            for r in range(P):
+                Lk = plan.length(r)
+                if Lk not in self.bits:
+                    t = torch.empty(max(self.kwords, 4), dtype=torch.int32, device=dev)
+                    _lib.check(self.lib.hyb_fill_key_bits(1, Lk, self.kwords, t.data_ptr(), stream), "key bits")
+                    self.bits[Lk] = t
+            lay = _lib.WorkspaceLayout()
+            _lib.check(self.lib.hyb_cached_attention_workspace_layout(1, H, _D, 0, max(Ls, 1), 0, 0,
+                                                                      ctypes.byref(lay)), "ring layout")
+        self.kv_splits = max(1, lay.kv_splits)
+        if self.kv_splits > 1:
+            self.part_o = torch.empty((self.kv_splits * H * Ls * _D,), dtype=torch.float32, device=dev)
+            self.part_lse = torch.empty((self.kv_splits * H * Ls,), dtype=torch.float32, device=dev)
+        else:
+            self.part_o = self.part_lse = None
+        self.comm_stream = torch.cuda.Stream(device=dev)
+        self.status = _lib.device_status(dev)
+        self.steps = [s for s in range(P) if plan.visible(rank, (rank - s) % P, self.G)]
+        self.launches = 0
+        # Optional instrumentation: when a list, each attention launch appends its (start, end)
+        # CUDA events recorded on the caller's stream after the step's input is ready.
+        self.event_log = None
+
+    # ---------------------------------------------------------------- pieces of one step
+    def _stage_block(self, block: KVBlock, Lk: int, kvh: torch.Tensor, stream: int) -> None:
+        kv = _lib.coded_view(block.k, block.k_scale, block.code_fmt)
+        vv = _lib.coded_view(block.v, block.v_scale, block.code_fmt)
+        _lib.check(self.lib.hyb_stage_head_major(1, Lk, self.H, _D, ctypes.byref(kv), ctypes.byref(vv),
+                                                 kvh[0].data_ptr(), kvh[1].data_ptr(), stream), "ring stage kv")
+        self.launches += 1
+
+    def _attend(self, src: int, kvh: torch.Tensor, out: torch.Tensor, lse, mode: int, stream: int) -> None:
+        plan, H, Ls = self.plan, self.H, self.Ls
+        Lk = plan.length(src)
+        a = _lib.AttnArgs()
+        a.abi_version = _lib.HYB_ABI_VERSION
+        a.B, a.H, a.D, a.Lq, a.Lk = 1, H, _D, Ls, Lk
+        a.hist_len, a.img_len, a.img_k_len = 0, Ls, Lk
+        a.group_tokens = self.G
+        a.softmax_scale = self.scale
+        a.q_seg, a.q_pos0, a.q_pos1 = plan.positions(self.rank)
+        a.k_seg, a.k_pos0, a.k_pos1 = plan.positions(src)
+        a.q, a.k, a.v = self.qh.data_ptr(), kvh[0].data_ptr(), kvh[1].data_ptr()
+        a.kbits, a.kwords = self.bits[Lk].data_ptr(), self.kwords
+        a.qbits, a.qwords = None, 0
+        a.out_img = out.data_ptr()
+        a.oi_sb, a.oi_st, a.oi_sh = out.stride(0), out.stride(1), out.stride(2)
+        a.oi_seg, a.oi_sseg = Ls, 0
+        a.lse = lse.data_ptr() if lse is not None else None
+        a.dev_status = self.status.data_ptr()
+        a.kv_splits = self.kv_splits
+        if self.kv_splits > 1:
+            a.part_o, a.part_lse = self.part_o.data_ptr(), self.part_lse.data_ptr()
+        a.acc_o, a.acc_lse, a.acc_mode = self.acc.data_ptr(), self.acc_lse.data_ptr(), mode
+        _lib.check(self.lib.hyb_attn_fwd(ctypes.byref(a), stream), "ring attention step")
+        self.launches += 2 if self.kv_splits > 1 else 1
+
+    def _modes(self):
+        """acc_mode per computed step: bit 0 merge with the accumulator, bit 1 final."""
+        modes = {}
+        for i, s in enumerate(self.steps):
+            modes[s] = (1 if i > 0 else 0) | (2 if i == len(self.steps) - 1 else 0)
+        return modes
+
+    # ---------------------------------------------------------------- one ring pass
+    def __call__(self, q, k, v, group=None, *, out=None, lse=None):
+        """This rank's shard q/k/v bf16 [1, Ls, H, 128] -> out bf16 [1, Ls, H, 128] (and the
+        natural-log LSE [1, H, Ls] into ``lse`` when given)."""
+        P, r, H, Ls, dev = self.plan.world, self.rank, self.H, self.Ls, self.device
+        if q.shape != (1, Ls, H, _D) or k.shape != q.shape or v.shape != q.shape:
+            raise ValueError(f"ring shard must be [1, {Ls}, {H}, {_D}] on rank {r}")
+        if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+            raise ValueError("ring attention takes bf16 q/k/v")
+        out = out if out is not None else torch.empty_like(q)
+        ranks = dist.get_process_group_ranks(group) if (P > 1 and group is not None) else list(range(P))
+        nxt, prv = ranks[(r + 1) % P], ranks[(r - 1) % P]
+        compute = torch.cuda.current_stream(dev)
+        comm = self.comm_stream
+        cs, ms = compute.cuda_stream, comm.cuda_stream
+        modes = self._modes()
+        self.launches = 0
+        if Ls == 0:
+            return out
+        with torch.cuda.device(dev):
+            # own block: quantise-on-write, then decode it and stage Q (caller's stream)
+            self.blocks[0].fill(k, v)
+            self.launches += 1
+            qv = _lib.bf16_view(q)
+            _lib.check(self.lib.hyb_stage_head_major(1, Ls, H, _D, ctypes.byref(qv), None, self.qh.data_ptr(),
+                                                     None, cs), "ring stage q")
+            self.launches += 1
+            self._stage_block(self.blocks[0], Ls, self.kvh[0], cs)
+            ready = [torch.cuda.Event() for _ in range(P)]
+            done = [torch.cuda.Event() for _ in range(P)]
+            comm.wait_stream(compute)
+            for s in range(P):
+                src = (r - s) % P
+                if s + 1 < P:
+                    nsrc = (r - s - 1) % P
+                    with torch.cuda.stream(comm):
+                        ops = [dist.P2POp(dist.isend, self.blocks[s % 2].buf, nxt, group),
+                               dist.P2POp(dist.irecv, self.blocks[(s + 1) % 2].buf, prv, group)]
+                        for req in dist.batch_isend_irecv(ops):
+                            req.wait()
+                        if s >= 1:
+                            comm.wait_event(done[s - 1])   # kvh[(s+1)%2] was read by step s-1
+                        self._stage_block(self.blocks[(s + 1) % 2], self.plan.length(nsrc), self.kvh[(s + 1) % 2], ms)
+                        ready[s + 1].record(comm)
+                if s >= 1:
+                    compute.wait_event(ready[s])
+                if s in modes:
+                    if self.event_log is not None:
+                        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                        ev[0].record(compute)
+                    self._attend(src, self.kvh[s % 2], out, lse, modes[s], cs)
+                    if self.event_log is not None:
+                        ev[1].record(compute)
+                        self.event_log.append(ev)
+                done[s].record(compute)
+            compute.wait_stream(comm)
+        return out
 
 
-def ring_step(q, block: KVBlock, acc, lse_acc, *, q_start: int, k_start: int, group_tokens: int,
-              out=None, lse=None):
-    """Attend the shard's queries ``q`` [1, Lq, H, D] to one block and merge the partial result
-    into ``acc`` (fp32 [Lq, H, D]) / ``lse_acc`` (fp32 [H, Lq]) in place."""
-    Lq, H = q.shape[1], q.shape[2]
-    if not frames_visible(q_start, Lq, k_start, group_tokens):
-        return
-    if block.L != Lq:
-        raise ValueError("ring blocks must have the query shard's length")
-    empty = q[:, :0]
-    out = out if out is not None else torch.empty_like(q)
-    lse = lse if lse is not None else torch.empty((1, H, Lq), dtype=torch.float32, device=q.device)
-    _att.cached_attention_local(
-        q, (block.k, block.k_scale), (block.v, block.v_scale), empty, empty, empty, None, 0,
-        attend_txt=False, group_tokens=group_tokens, out_img=out, lse=lse, q_pos0=q_start,
-        k_pos0=k_start, img_kv_fmt=block.code_fmt)
-    lib = _lib.load()
-    with torch.cuda.device(q.device):
-        _lib.check(lib.hyb_lse_merge(Lq, H, 128, acc.data_ptr(), lse_acc.data_ptr(), out.data_ptr(), 0,
-                                     lse.data_ptr(), _lib.stream_ptr(q.device)), "ring merge")
+_PLANS: dict = {}
 
 
-def ring_attention(q, k, v, group=None, *, tokens_per_frame: int, causal_frames: int = 1,
-                   kv_format: str = "fp8_e4m3"):
-    """Frame-causal self-attention of a sequence sharded contiguously over the ranks of
-    ``group`` (every rank holds the same number of tokens).  Returns this rank's output
-    [1, Ls, H, D] bf16."""
-    P = dist.get_world_size(group)
-    r = dist.get_rank(group)
-    ranks = dist.get_process_group_ranks(group) if group is not None else list(range(P))
-    _, Ls, H, D = q.shape
-    if D != 128:
-        raise ValueError("head_dim must be 128")
-    G = int(causal_frames) * int(tokens_per_frame)
-    dev = q.device
-    blocks = [KVBlock(Ls, H, dev, kv_format), KVBlock(Ls, H, dev, kv_format)]
-    blocks[0].fill(k, v)
-    acc = torch.zeros((Ls, H, D), dtype=torch.float32, device=dev)
-    lse_acc = torch.full((H, Ls), float("-inf"), dtype=torch.float32, device=dev)
-    out = torch.empty_like(q)
-    lse = torch.empty((1, H, Ls), dtype=torch.float32, device=dev)
-    nxt, prv = ranks[(r + 1) % P], ranks[(r - 1) % P]
-    for s in range(P):
-        cur = blocks[s % 2]
-        reqs = []
-        if s + 1 < P:
-            ops = [dist.P2POp(dist.isend, cur.buf, nxt, group), dist.P2POp(dist.irecv, blocks[(s + 1) % 2].buf, prv, group)]
-            reqs = dist.batch_isend_irecv(ops)
-        src = (r - s) % P
-        ring_step(q, cur, acc, lse_acc, q_start=r * Ls, k_start=src * Ls, group_tokens=G, out=out, lse=lse)
-        for req in reqs:
-            req.wait()
-    return acc.view(1, Ls, H, D).to(torch.bfloat16)
+def ring_attention(q, k, v, group=None, *, seq_len: int, tokens_per_frame: int, causal_frames: int = 1,
+                   kv_format: str = "fp8_e4m3", layout: str = "zigzag", softmax_scale: float | None = None,
+                   out=None, lse=None):
+    """Frame-causal self-attention of a sequence of ``seq_len`` tokens sharded over the ranks
+    of ``group`` by ``RingPlan(seq_len, P, layout)``.  q/k/v: this rank's shard bf16
+    [1, Ls, H, 128].  Returns this rank's output [1, Ls, H, 128] bf16."""
+    P = dist.get_world_size(group) if dist.is_initialized() else 1
+    r = dist.get_rank(group) if dist.is_initialized() else 0
+    ra = ring_plan_state(q, seq_len=seq_len, world=P, rank=r, tokens_per_frame=tokens_per_frame,
+                         causal_frames=causal_frames, kv_format=kv_format, layout=layout,
+                         softmax_scale=softmax_scale)
+    return ra(q, k, v, group, out=out, lse=lse)
 
 
-def ring_attention_emulated(q_shards, k_shards, v_shards, *, tokens_per_frame: int, causal_frames: int = 1,
-                            kv_format: str = "fp8_e4m3"):
-    """The same schedule for P emulated ranks in one process (one GPU): every rank's queries
-    meet every block in ring order.  Used to test the per-step math without a transport."""
-    P = len(q_shards)
-    G = int(causal_frames) * int(tokens_per_frame)
-    Ls, H = q_shards[0].shape[1], q_shards[0].shape[2]
-    dev = q_shards[0].device
+def ring_plan_state(q, *, seq_len, world, rank, tokens_per_frame, causal_frames=1, kv_format="fp8_e4m3",
+                    layout="zigzag", softmax_scale=None) -> RingAttention:
+    """The cached ``RingAttention`` of this geometry (buffers are reused across calls)."""
+    P, r = world, rank
+    key = (seq_len, P, layout, r, q.shape[2], q.device, tokens_per_frame, causal_frames, kv_format, softmax_scale)
+    ra = _PLANS.get(key)
+    if ra is None:
+        ra = RingAttention(RingPlan(seq_len, P, layout), r, q.shape[2], q.device, tokens_per_frame=tokens_per_frame,
+                           causal_frames=causal_frames, kv_format=kv_format, softmax_scale=softmax_scale)
+        _PLANS.clear()
+        _PLANS[key] = ra
+    return ra
+
+
+def ring_attention_emulated(q, k, v, world: int, *, tokens_per_frame: int, causal_frames: int = 1,
+                            kv_format: str = "fp8_e4m3", layout: str = "zigzag", softmax_scale=None):
+    """The ring schedule for ``world`` emulated ranks in one process on one GPU: q/k/v are the
+    full sequence [1, L, H, 128]; every rank's queries meet every block in ring order with the
+    same kernels and accumulator modes as ``ring_attention``.  Returns the full output."""
+    plan = RingPlan(q.shape[1], world, layout)
+    H, dev = q.shape[2], q.device
+    rings = [RingAttention(plan, r, H, dev, tokens_per_frame=tokens_per_frame, causal_frames=causal_frames,
+                           kv_format=kv_format, softmax_scale=softmax_scale) for r in range(world)]
     blocks = []
-    for kk, vv in zip(k_shards, v_shards):
-        b = KVBlock(Ls, H, dev, kv_format)
-        b.fill(kk, vv)
+    for r in range(world):
+        b = KVBlock(plan.max_length(), H, dev, kv_format)
+        if plan.length(r):
+            b.fill(plan.shard(k, r), plan.shard(v, r))
         blocks.append(b)
     outs = []
-    for r in range(P):
-        acc = torch.zeros((Ls, H, 128), dtype=torch.float32, device=dev)
-        lse_acc = torch.full((H, Ls), float("-inf"), dtype=torch.float32, device=dev)
-        for s in range(P):
-            src = (r - s) % P
-            ring_step(q_shards[r], blocks[src], acc, lse_acc, q_start=r * Ls, k_start=src * Ls, group_tokens=G)
-        outs.append(acc.view(1, Ls, H, 128).to(torch.bfloat16))
-    return outs
+    cs = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        for r, ra in enumerate(rings):
+            Ls = plan.length(r)
+            out = torch.empty((1, Ls, H, _D), dtype=torch.bfloat16, device=dev)
+            if Ls:
+                qs = plan.shard(q, r).contiguous()
+                qv = _lib.bf16_view(qs)
+                _lib.check(ra.lib.hyb_stage_head_major(1, Ls, H, _D, ctypes.byref(qv), None, ra.qh.data_ptr(),
+                                                       None, cs), "ring stage q")
+                modes = ra._modes()
+                for s in range(world):
+                    src = (r - s) % world
+                    if s in modes:
+                        ra._stage_block(blocks[src], plan.length(src), ra.kvh[0], cs)
+                        ra._attend(src, ra.kvh[0], out, None, modes[s], cs)
+            outs.append(out)
+    return plan.unshard(outs)

@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define HYB_ABI_VERSION 1
+#define HYB_ABI_VERSION 2
 
 /* status codes */
 #define HYB_OK 0
@@ -164,6 +164,13 @@ typedef struct hyb_attn_args {
   int32_t B, H, D, Lq, Lk, hist_len, img_len, group_tokens;
   float softmax_scale;
   int32_t q_pos0, k_pos0;   /* as in hyb_cached_attn_args */
+  int32_t img_k_len;        /* image keys [hist_len, hist_len + img_k_len); 0 means img_len */
+  int32_t q_seg, q_pos1;    /* two-segment query positions (zig-zag ring shards): image query i
+                               is at q_pos0 + i for i < q_seg, else at q_pos1 + (i - q_seg);
+                               q_seg <= 0 means one segment */
+  int32_t k_seg, k_pos1;    /* the same for image keys; positions must increase
+                               (k_pos1 >= k_pos0 + k_seg) so that every query sees a key prefix */
+  int32_t pad1_;
   const void* q; const void* k; const void* v;
   const uint32_t* kbits; int32_t kwords;
   const uint32_t* qbits; int32_t qwords;
@@ -176,8 +183,32 @@ typedef struct hyb_attn_args {
   int32_t pad_;
   float* part_o;             /* fp32 [kv_splits, B, H, Lq, D] partial rows (kv_splits > 1) */
   float* part_lse;           /* fp32 [kv_splits, B, H, Lq] partial LSE (kv_splits > 1) */
+  /* Running output of a ring (KV-passing) schedule, or NULL.  With acc_o set, every query is an
+     image query (Lq == img_len) and this launch's rows are merged by log-sum-exp with
+     acc_o fp32 [B, Lq, H, D] / acc_lse fp32 [B, H, Lq] (natural log).  acc_mode bit 0: merge
+     with the accumulator's contents (else this launch starts it); bit 1: final step — write
+     the merged rows as bf16 to out_img (and the LSE to lse when non-NULL) instead of acc_o. */
+  float* acc_o;
+  float* acc_lse;
+  int32_t acc_mode;
+  int32_t pad2_;
 } hyb_attn_args;
 int hyb_attn_fwd(const hyb_attn_args* args, void* stream);
+
+/* Decode a K/V block (or one Q tensor) [B, L, H, D] in BF16, E4M3 or INT8 with per-(token,
+ * head) scales into head-major bf16 [B, H, L, 128], the operand layout hyb_attn_fwd reads
+ * (codes times scale in fp32, one rounding, as dequantize_kv).  src_v and dst_v may both be
+ * NULL (one tensor).  Replaces, for callers that keep operands staged across calls (the ring),
+ * dequantize_kv + torch.cat of the reference's cached path (int8_kv_cache.py:182-205,
+ * nomas_cpt.py:614-649) and the q/k/v layout copies before flash_attn_func in
+ * dynamic_ring_attention.py:45-83. */
+int hyb_stage_head_major(int32_t B, int32_t L, int32_t H, int32_t D, const hyb_tensor4* src_k,
+                         const hyb_tensor4* src_v, void* dst_k, void* dst_v, void* stream);
+
+/* Key-visibility bitmap for hyb_attn_fwd with keys [0, Lk) of every batch row visible:
+ * bits [B, kwords] uint32.  No reference counterpart (the reference ring attends every key of
+ * a block; flash_attn_func takes no key mask). */
+int hyb_fill_key_bits(int32_t B, int32_t Lk, int32_t kwords, uint32_t* bits, void* stream);
 
 /* Ring merge of two partial attentions (fp32 LSE in natural log):
  * lse = log(exp(lse_a) + exp(lse_b)); out = out_a * exp(lse_a - lse) + out_b * exp(lse_b - lse).

@@ -90,16 +90,20 @@ def main():
             ok = False
     # ---- ring (KV passing) over all ranks: equals the emulated single-process schedule
     from hy_nomas_b200 import ring
-    Lr, Tr = 8 * 96, 96
-    rq, rk, rv = (seeded_kv((1, Lr, 4, D), make_generator(77 + i)) for i in range(3))
-    Lsr = Lr // world
-    shard = lambda x, i: x[:, i * Lsr:(i + 1) * Lsr].to(dev)
-    out_ring = ring.ring_attention(shard(rq, rank), shard(rk, rank), shard(rv, rank), None, tokens_per_frame=Tr)
-    emu = ring.ring_attention_emulated([shard(rq, i) for i in range(world)], [shard(rk, i) for i in range(world)],
-                                       [shard(rv, i) for i in range(world)], tokens_per_frame=Tr)
-    if not torch.equal(out_ring, emu[rank]):
-        print("ring mismatch on rank", rank, (out_ring.float() - emu[rank].float()).abs().max().item())
-        ok = False
+    Lr, Tr = 8 * 96 + 5, 96
+    rq, rk, rv = (seeded_kv((1, Lr, 4, D), make_generator(77 + i)).to(dev) for i in range(3))
+    emu = ring.ring_attention_emulated(rq, rk, rv, world, tokens_per_frame=Tr)
+    for layout in ("zigzag", "contiguous"):
+        plan = ring.RingPlan(Lr, world, layout)
+        emu = ring.ring_attention_emulated(rq, rk, rv, world, tokens_per_frame=Tr, layout=layout)
+        for _ in range(2):   # second pass reuses the cached plan and buffers
+            out_ring = ring.ring_attention(plan.shard(rq, rank).contiguous(), plan.shard(rk, rank).contiguous(),
+                                           plan.shard(rv, rank).contiguous(), None, seq_len=Lr,
+                                           tokens_per_frame=Tr, layout=layout)
+        if not torch.equal(out_ring, plan.shard(emu, rank)):
+            print("ring mismatch on rank", rank, layout,
+                  (out_ring.float() - plan.shard(emu, rank).float()).abs().max().item())
+            ok = False
     ok_t = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
     ok = bool(ok_t.item())

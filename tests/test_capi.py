@@ -49,6 +49,7 @@ int main(void) {
   F(hyb_cached_attn_args, dev_status)
   F(hyb_attn_args, q) F(hyb_attn_args, kwords) F(hyb_attn_args, qbits) F(hyb_attn_args, oi_sseg)
   F(hyb_attn_args, lse) F(hyb_attn_args, dev_status) F(hyb_attn_args, kv_splits) F(hyb_attn_args, part_lse)
+  F(hyb_attn_args, img_k_len) F(hyb_attn_args, k_pos1) F(hyb_attn_args, acc_o) F(hyb_attn_args, acc_mode)
   printf("hyb_workspace_layout %zu\n", sizeof(hyb_workspace_layout));
   F(hyb_workspace_layout, total) F(hyb_workspace_layout, kv_splits)
   return 0;

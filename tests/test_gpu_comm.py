@@ -109,29 +109,44 @@ def test_lse_merge_kernel_matches_oracle(cuda_lib):
     torch.testing.assert_close(acc.cpu().double(), torch.from_numpy(g["out"])[0], rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("P,frames,T", [(1, 5, 64), (4, 21, 48), (3, 7, 100)])
-def test_ring_schedule_matches_frame_causal_oracle(cuda_lib, P, frames, T):
-    """The ring's per-step attention + LSE merge over P emulated ranks equals frame-causal
-    attention over the whole sequence (shards not aligned to frames when L / P % T != 0)."""
+@pytest.mark.parametrize("P,frames,T,layout", [(1, 5, 64, "zigzag"), (4, 21, 48, "zigzag"),
+                                               (3, 7, 100, "zigzag"), (3, 7, 100, "contiguous"),
+                                               (8, 21, 39, "zigzag")])
+def test_ring_schedule_matches_frame_causal_oracle(cuda_lib, P, frames, T, layout):
+    """The ring's per-step attention launches with the accumulating epilogue, over P emulated
+    ranks, equal frame-causal attention over the whole sequence (shards not aligned to frames,
+    ragged zig-zag chunks when L is not a multiple of 2P)."""
     from hy_nomas_b200 import ring
     from oracle import attention as oatt
     from oracle import quant as oq
     dev = torch.device("cuda")
-    H, L = 2, frames * T
-    L -= L % P
-    Ls = L // P
+    H, L = 2, frames * T - 1
     gen = make_generator(900 + P)
     q, k, v = (seeded_kv((1, L, H, 128), gen) for _ in range(3))
-    sh = lambda x: [x[:, i * Ls:(i + 1) * Ls].to(dev) for i in range(P)]
-    outs = ring.ring_attention_emulated(sh(q), sh(k), sh(v), tokens_per_frame=T)
-    got = torch.cat([o.cpu() for o in outs], dim=1)
-    # keys and values as the blocks carry them: e4m3 per shard, decoded
-    kd = torch.cat([oq.dequantize(*oq.quantize_e4m3(k[:, i * Ls:(i + 1) * Ls])) for i in range(P)], 1)
-    vd = torch.cat([oq.dequantize(*oq.quantize_e4m3(v[:, i * Ls:(i + 1) * Ls])) for i in range(P)], 1)
+    got = ring.ring_attention_emulated(q.to(dev), k.to(dev), v.to(dev), P, tokens_per_frame=T, layout=layout)
+    # keys and values as the blocks carry them: e4m3 per (token, head), decoded
+    kd = oq.dequantize(*oq.quantize_e4m3(k))
+    vd = oq.dequantize(*oq.quantize_e4m3(v))
     e = q[:, :0]
     ref, _, (mag, _) = oatt.cached_attention(q, kd, vd, e, e, e, kd[:, :0], vd[:, :0], attend_txt=False,
                                              group_tokens=T, return_magnitude=True)
-    o, r = got.float().flatten(), ref.flatten()
+    o, r = got.cpu().float().flatten(), ref.flatten()
     bound = 2e-2 + 2.0 ** -7 * r.abs() + 2.0 ** -8 * mag.flatten()
     assert ((o - r).abs() <= bound).all(), ((o - r).abs() - bound).max()
     assert torch.nn.functional.cosine_similarity(o[None], r[None]).item() >= 0.9995
+
+
+def test_stage_head_major_matches_dequant(cuda_lib):
+    """hyb_stage_head_major decodes e4m3 blocks exactly as the oracle dequantiser, head-major."""
+    from oracle import quant as oq
+    dev = torch.device("cuda")
+    gen = make_generator(5)
+    x = seeded_kv((1, 77, 3, 128), gen)
+    codes, scale = oq.quantize_e4m3(x)
+    c_dev, s_dev = codes.to(dev), scale.to(dev)
+    out = torch.empty((3, 77, 128), dtype=torch.bfloat16, device=dev)
+    tv = _lib.coded_view(c_dev, s_dev, _lib.HYB_FMT_E4M3)
+    _lib.check(cuda_lib.hyb_stage_head_major(1, 77, 3, 128, ctypes.byref(tv), None, out.data_ptr(), None,
+                                             _stream()), "stage")
+    ref = oq.dequantize(codes, scale)[0].permute(1, 0, 2).contiguous()
+    assert torch.equal(out.cpu().view(torch.int16), ref.view(torch.int16))

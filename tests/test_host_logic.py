@@ -89,3 +89,45 @@ def test_synthetic_generator_is_seeded_and_has_outliers():
     per_channel = a.float().abs().mean(dim=(0, 1))        # [H, D]
     for h in range(2):
         assert (per_channel[h] > 4).sum() == 4
+
+
+@pytest.mark.parametrize("L,P,layout", [(32760, 8, "zigzag"), (32760, 2, "zigzag"), (1001, 3, "zigzag"),
+                                        (1001, 3, "contiguous"), (5, 4, "zigzag"), (0, 2, "zigzag")])
+def test_ring_plan_partitions_the_sequence(L, P, layout):
+    """Every token belongs to exactly one rank, segments increase, shard/unshard round-trips,
+    and zig-zag balances the frame-causal work to within one frame-row per rank pair."""
+    from hy_nomas_b200.ring import RingPlan
+    plan = RingPlan(L, P, layout)
+    owned = []
+    for r in range(P):
+        n0, p0, p1 = plan.positions(r)
+        segs = [(p, n) for p, n in plan.segments[r] if n > 0]
+        assert all(a[0] + a[1] <= b[0] for a, b in zip(segs, segs[1:]))
+        if len([1 for _, n in plan.segments[r] if n > 0]) == 2:
+            assert p1 >= p0 + n0
+        for p, n in segs:
+            owned.extend(range(p, p + n))
+    assert sorted(owned) == list(range(L))
+    assert max(plan.length(r) for r in range(P)) - min(plan.length(r) for r in range(P)) <= 2
+    if L:
+        x = torch.arange(L).view(1, L, 1, 1)
+        assert torch.equal(plan.unshard([plan.shard(x, r) for r in range(P)]), x)
+    if layout == "zigzag" and L >= 1000 and P > 1:
+        T = 39
+        def work(r):   # visible (query, key) pairs of rank r under the frame-causal rule
+            tot = 0
+            for p, n in plan.segments[r]:
+                for i in range(p, p + n):
+                    tot += (i // T + 1) * T if (i // T + 1) * T <= L else L
+            return tot
+        w = [work(r) for r in range(P)]
+        assert max(w) / (sum(w) / P) < 1.02
+
+
+def test_ring_plan_visibility_skips_future_blocks():
+    from hy_nomas_b200.ring import RingPlan
+    plan = RingPlan(400, 4, "contiguous")
+    assert plan.visible(0, 0, 100) and not plan.visible(0, 1, 100) and plan.visible(3, 0, 100)
+    assert plan.visible(0, 3, 0)            # no causal rule: every block is computed
+    zz = RingPlan(400, 4, "zigzag")
+    assert all(zz.visible(r, s, 50) for r in range(4) for s in range(4))
