@@ -107,6 +107,7 @@ SIGNATURES = {
     "hyb_stage_head_major": (c_i32, [c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(Tensor4),
                                      ctypes.POINTER(Tensor4), c_ptr, c_ptr, c_ptr]),
     "hyb_fill_key_bits": (c_i32, [c_i32, c_i32, c_i32, c_ptr, c_ptr]),
+    "hyb_attn_work_plan": (c_i32, [ctypes.POINTER(AttnArgs), c_i32, ctypes.POINTER(c_i32), c_i32]),
     "hyb_version": (c_i32, []),
     "hyb_last_error": (c_i32, [ctypes.c_char_p, ctypes.c_size_t]),
     "hyb_device_supported": (c_i32, []),

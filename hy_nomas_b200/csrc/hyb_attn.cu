@@ -18,7 +18,11 @@
 #include <limits.h>
 
 #include <cmath>
+#include <cstring>
+#include <map>
 #include <mutex>
+#include <queue>
+#include <vector>
 
 #include "hyb_common.cuh"
 
@@ -58,8 +62,8 @@ struct AttnKParams {
   float* lse;
   int* status;
   int num_qtiles;
-  // Split-KV: each CTA covers one of kv_splits contiguous slices of its key-tile list and,
-  // when kv_splits > 1, writes normalised fp32 partial rows part_o [S, B, H, Lq, 128] and
+  // Split-KV: a query pair split into k > 1 key slices writes, per slice, normalised fp32
+  // partial rows part_o [S, B, H, Lq, 128] (S = kv_splits, the buffers' capacity, >= k) and
   // their natural-log LSE part_lse [S, B, H, Lq]; merge_splits_kernel combines them.
   int kv_splits;
   float* part_o;
@@ -72,13 +76,16 @@ struct AttnKParams {
   int acc_mode;
 };
 
-__device__ __forceinline__ long long q_position(const AttnKParams& p, int i) {
+__host__ __device__ __forceinline__ int imin(int a, int b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int imax(int a, int b) { return a > b ? a : b; }
+
+__host__ __device__ __forceinline__ long long q_position(const AttnKParams& p, int i) {
   return i < p.q_seg ? static_cast<long long>(p.q_pos0) + i : static_cast<long long>(p.q_pos1) + (i - p.q_seg);
 }
 
 // Image keys visible to an image query at global position qpos.  Key positions increase with
 // the key index, so the visible image keys are the prefix [0, count).
-__device__ __forceinline__ int img_keys_visible(const AttnKParams& p, long long qpos) {
+__host__ __device__ __forceinline__ int img_keys_visible(const AttnKParams& p, long long qpos) {
   const long long lim = (qpos / p.gtok + 1) * p.gtok;  // first position of a later group
   long long a = lim - p.k_pos0;
   a = a < 0 ? 0 : (a > p.k_seg ? p.k_seg : a);
@@ -117,26 +124,65 @@ __device__ __forceinline__ AccWeights acc_weights(float lse_a, float lse_b) {
 // Image keys past the block-causal limit of the tile's last row are never loaded.
 struct TileRange {
   int a_end, b_begin, b_end;
-  __device__ int count() const { return a_end + (b_end - b_begin); }
-  __device__ int tile(int j) const { return j < a_end ? j : b_begin + (j - a_end); }
+  __host__ __device__ int count() const { return a_end + (b_end - b_begin); }
+  __host__ __device__ int tile(int j) const { return j < a_end ? j : b_begin + (j - a_end); }
 };
 
-__device__ TileRange key_tiles(const AttnKParams& p, int q0, int rows = kBM) {
-  const int q_last = min(q0 + rows, p.Lq) - 1;
+__host__ __device__ TileRange key_tiles(const AttnKParams& p, int q0, int rows = kBM) {
+  const int q_last = imin(q0 + rows, p.Lq) - 1;
   const int ntk = (p.Lk + kBN - 1) / kBN;
   int img_vis_end = p.Lh + p.Lik;
   if (p.gtok > 0 && q_last < p.Li) img_vis_end = p.Lh + img_keys_visible(p, q_position(p, q_last));
   TileRange r;
-  r.a_end = min((img_vis_end + kBN - 1) / kBN, ntk);
+  r.a_end = imin((img_vis_end + kBN - 1) / kBN, ntk);
   const int txt_begin = p.Lh + p.Lik;
   if (txt_begin < p.Lk) {
-    r.b_begin = max(txt_begin / kBN, r.a_end);
+    r.b_begin = imax(txt_begin / kBN, r.a_end);
     r.b_end = ntk;
   } else {
     r.b_begin = 0;
     r.b_end = 0;
   }
   return r;
+}
+
+// Work list of one launch.  CTA x runs unit x of the head-major list
+//   for bh in [0, B*H):  for i in [0, npairs) (query pair npairs-1-i: heaviest first):
+//     for k in [0, k_i):  key slice k of k_i of that pair
+// so that a heavy pair is cut into more slices than a light one and every CTA gets about the
+// same number of key tiles.  prefix[i] = k_0 + ... + k_{i-1}; per_bh = prefix[npairs].
+// uniform > 0 stands for k_i = uniform for every pair (no table).
+constexpr int kMaxPairTab = 512;
+struct UnitMap {
+  int npairs, per_bh, uniform, max_k;
+  int prefix[kMaxPairTab + 1];
+};
+
+__device__ __forceinline__ int splits_of_pair(const UnitMap& um, int i) {
+  return um.uniform > 0 ? um.uniform : um.prefix[i + 1] - um.prefix[i];
+}
+
+__device__ __forceinline__ void unit_of(const UnitMap& um, int x, int& bh, int& i, int& k, int& ki) {
+  bh = x / um.per_bh;
+  const int r = x - bh * um.per_bh;
+  if (um.uniform > 0) {
+    i = r / um.uniform;
+    k = r - i * um.uniform;
+    ki = um.uniform;
+    return;
+  }
+  int lo = 0, hi = um.npairs - 1;  // largest i with prefix[i] <= r (prefix increases strictly)
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (um.prefix[mid] <= r) {
+      lo = mid;
+    } else {
+      hi = mid - 1;
+    }
+  }
+  i = lo;
+  k = r - um.prefix[i];
+  ki = um.prefix[i + 1] - um.prefix[i];
 }
 
 // Bounded wait that ignores the abort flag (used to drain in-flight async work on exit).
@@ -168,7 +214,8 @@ constexpr int kMaxSmemBitWords = 4096;
 template <int kEmuPer8>
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, const AttnKParams p) {
+                     const __grid_constant__ CUtensorMap tmV, const AttnKParams p,
+                     const __grid_constant__ UnitMap um) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -191,16 +238,15 @@ __global__ void __launch_bounds__(kThreads2, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_pairs = (p.num_qtiles + 1) / 2;
-  // Head-major grid (CTAs resident together share one head's K/V in L2), heaviest query
-  // pair of each head first.
-  const int qp = num_pairs - 1 - static_cast<int>(blockIdx.x);
-  const int h = blockIdx.y;
-  const int b = static_cast<int>(blockIdx.z) / p.kv_splits;
-  const int split = static_cast<int>(blockIdx.z) % p.kv_splits;
+  // Head-major work list (CTAs resident together share one head's K/V in L2), heaviest
+  // query pair of each head first.
+  int bh, ipair, split, nsplit;
+  unit_of(um, static_cast<int>(blockIdx.x), bh, ipair, split, nsplit);
+  const int qp = um.npairs - 1 - ipair;
+  const int h = bh % p.H;
+  const int b = bh / p.H;
   const int q0 = qp * kPairRows;
   const bool has1 = q0 + kBM < p.Lq;
-  const int bh = b * p.H + h;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -237,8 +283,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
   const TileRange tr = key_tiles(p, q0, kPairRows);
   // This CTA's slice [j_begin, j_begin + n) of the pair's key-tile list.
   const int n_all = tr.count();
-  const int j_begin = static_cast<int>((static_cast<long long>(n_all) * split) / p.kv_splits);
-  const int n = static_cast<int>((static_cast<long long>(n_all) * (split + 1)) / p.kv_splits) - j_begin;
+  const int j_begin = static_cast<int>((static_cast<long long>(n_all) * split) / nsplit);
+  const int n = static_cast<int>((static_cast<long long>(n_all) * (split + 1)) / nsplit) - j_begin;
 
   if (warp < 4) {
     if (warp == 0 && lane == 0) {
@@ -477,7 +523,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       have_o = __all_sync(0xffffffffu, have_o);
       tc_fence_after();
       const bool in_range = qrow < p.Lq;
-      if (p.kv_splits > 1) {
+      if (nsplit > 1) {
         // Partial result of this key slice: O / l in fp32 and its LSE (-inf when the slice
         // saw no visible key); query validity is applied by the merge.
         const float inv_l = l > 0.f ? __frcp_rn(l) : 0.f;
@@ -611,7 +657,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
 // Combine the kv_splits partial results of every (batch, head, query row): LSE-weighted sum of
 // the normalised partial rows, written as bf16 at the row's final position (zero for padded
 // text queries), plus the final LSE when requested.  One warp per row, 4 dims per lane.
-__global__ void __launch_bounds__(256) merge_splits_kernel(const AttnKParams p) {
+__global__ void __launch_bounds__(256) merge_splits_kernel(const AttnKParams p, const __grid_constant__ UnitMap um) {
   const long long rows = static_cast<long long>(p.B) * p.H * p.Lq;
   const int lane = threadIdx.x & 31;
   const long long slice = static_cast<long long>(p.B) * p.H * p.Lq;
@@ -621,15 +667,17 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const AttnKParams p) 
     const long long bh = r / p.Lq;
     const int h = static_cast<int>(bh % p.H);
     const int b = static_cast<int>(bh / p.H);
+    const int ns = splits_of_pair(um, um.npairs - 1 - qrow / kPairRows);
+    if (ns <= 1) continue;  // the attention kernel wrote this row's final result
     bool valid = true;
     if (p.qbits != nullptr)
       valid = (__ldg(p.qbits + static_cast<size_t>(b) * p.qwords + (qrow >> 5)) >> (qrow & 31)) & 1u;
     float m = -INFINITY;
-    for (int sp = 0; sp < p.kv_splits; ++sp) m = fmaxf(m, __ldg(p.part_lse + sp * slice + r));
+    for (int sp = 0; sp < ns; ++sp) m = fmaxf(m, __ldg(p.part_lse + sp * slice + r));
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float wsum = 0.f;
     if (m != -INFINITY) {
-      for (int sp = 0; sp < p.kv_splits; ++sp) {
+      for (int sp = 0; sp < ns; ++sp) {
         const float w = __expf(__ldg(p.part_lse + sp * slice + r) - m);
         wsum += w;
         const float4 o = __ldg(reinterpret_cast<const float4*>(p.part_o + (sp * slice + r) * kHD) + lane);
@@ -970,6 +1018,152 @@ int choose_kv_splits(int B, int H, int Lq, int Lk, int sms) {
   return best;
 }
 
+// Capacity of the partial buffers: the most key slices any query pair may be cut into (the
+// per-pair counts are chosen at launch by plan_units).  The dense estimate above, raised to 4
+// when the launch has fewer than 8 waves of pair-CTAs (its tail is then a large share), and
+// bounded to 1 GiB of partial rows.
+int split_capacity(int B, int H, int Lq, int Lk, int sms) {
+  const char* e = getenv("HYB_KV_SPLITS");
+  if (e != nullptr) {
+    const int v = atoi(e);
+    if (v >= 1 && v <= 16) return v;
+  }
+  const long long ctas = static_cast<long long>((Lq + kPairRows - 1) / kPairRows) * H * B;
+  const int tiles = (Lk + kBN - 1) / kBN;
+  if (ctas <= 0 || tiles < 32) return 1;
+  int cap = choose_kv_splits(B, H, Lq, Lk, sms);
+  if (ctas < 8LL * sms) cap = imax(cap, 4);
+  cap = imin(cap, imax(1, tiles / 8));
+  while (cap > 1 && static_cast<long long>(cap) * B * H * Lq * (kHD * 4 + 4) > (1LL << 30)) --cap;
+  return cap;
+}
+
+// Per-pair key-slice counts of one launch, chosen by simulating the in-order dispatch of the
+// work list onto the SMs: a unit costs its key tiles plus a fixed ~2 tiles (tensor-memory
+// setup, Q load, epilogue); a split pair adds its fp32 partial rows written and merged at
+// ~6 TB/s and the merge launch.  Candidate slice lengths U give k_i = ceil(n_i / U) <= cap.
+// Plans are cached per launch geometry.
+struct PlanKey {
+  long long v[17];
+  bool operator<(const PlanKey& o) const {
+    for (int i = 0; i < 17; ++i)
+      if (v[i] != o.v[i]) return v[i] < o.v[i];
+    return false;
+  }
+};
+std::mutex g_plan_mu;
+std::map<PlanKey, UnitMap> g_plans;
+
+UnitMap plan_units(const AttnKParams& kp, int cap, int sms) {
+  UnitMap um;
+  memset(&um, 0, sizeof(um));
+  const int np = (kp.num_qtiles + 1) / 2;
+  um.npairs = np;
+  cap = imax(cap, 1);
+  const char* e = getenv("HYB_KV_SPLITS");
+  const int forced = e != nullptr ? atoi(e) : 0;
+  int uniform = 0;
+  if (forced >= 1) {
+    uniform = imin(forced, cap);
+  } else if (cap <= 1) {
+    uniform = 1;
+  } else if (np > kMaxPairTab) {
+    uniform = imin(cap, choose_kv_splits(kp.B, kp.H, kp.Lq, kp.Lk, sms));
+  }
+  if (uniform > 0 || np == 0) {
+    um.uniform = imax(uniform, 1);
+    um.per_bh = np * um.uniform;
+    um.max_k = um.uniform;
+    return um;
+  }
+  const PlanKey key = {{kp.B, kp.H, kp.Lq, kp.Lk, kp.Lh, kp.Li, kp.Lik, kp.gtok, kp.q_pos0, kp.k_pos0, kp.q_seg,
+                        kp.q_pos1, kp.k_seg, kp.k_pos1, cap, sms, 1}};
+  {
+    std::lock_guard<std::mutex> lock(g_plan_mu);
+    auto it = g_plans.find(key);
+    if (it != g_plans.end()) return it->second;
+  }
+  std::vector<int> n(np), rows(np);
+  int nmax = 0;
+  long long total = 0;
+  for (int i = 0; i < np; ++i) {
+    const int qp = np - 1 - i;
+    n[i] = key_tiles(kp, qp * kPairRows, kPairRows).count();
+    rows[i] = imin(kPairRows, kp.Lq - qp * kPairRows);
+    nmax = imax(nmax, n[i]);
+    total += n[i];
+  }
+  const int BH = kp.B * kp.H;
+  std::vector<int> cands;
+  for (int sp = 1; sp <= cap; ++sp) cands.push_back(imax(1, (nmax + sp - 1) / sp));
+  for (int w = 1; w <= 64; ++w) {
+    const long long u = (total * BH + static_cast<long long>(w) * sms - 1) / (static_cast<long long>(w) * sms);
+    if (u >= 4 && u < nmax) cands.push_back(static_cast<int>(u));
+  }
+  // Second family: a total of M units per (b, h) aimed at whole waves, slices handed to the
+  // pairs in proportion to their tiles (k_i = round(n_i M / sum n)).
+  std::vector<int> totals;
+  for (int w = 1; w <= 64; ++w) {
+    const long long m = (static_cast<long long>(w) * sms) / BH;
+    for (long long d = -1; d <= 0; ++d)
+      if (m + d >= np && m + d <= static_cast<long long>(np) * cap) totals.push_back(static_cast<int>(m + d));
+  }
+  const int n_cands = static_cast<int>(cands.size());
+  const double c_fix = 2.0;
+  const double t_tile = 2.0e-6;
+  double best_t = 1e300;
+  std::vector<int> best_k(np, 1), k(np);
+  for (int c = 0; c < n_cands + static_cast<int>(totals.size()); ++c) {
+    bool any_split = false;
+    double over = 0.0;
+    for (int i = 0; i < np; ++i) {
+      if (c < n_cands) {
+        const int U = cands[c];
+        k[i] = imin(cap, imax(1, (n[i] + U - 1) / U));
+      } else {
+        const double share = total > 0 ? static_cast<double>(n[i]) * totals[c - n_cands] / total : 1.0;
+        k[i] = imin(cap, imax(1, static_cast<int>(share + 0.5)));
+      }
+      if (k[i] > 1) {
+        any_split = true;
+        over += static_cast<double>(rows[i]) * BH * k[i] * (kHD * 4 + 4) * 2.0 / 6e12 / t_tile;
+      }
+    }
+    if (any_split) over += 2.0;
+    std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+    for (int sm = 0; sm < sms; ++sm) free_at.push(0.0);
+    double makespan = 0.0;
+    for (int bh = 0; bh < BH; ++bh) {
+      for (int i = 0; i < np; ++i) {
+        for (int kk = 0; kk < k[i]; ++kk) {
+          const long long len = (static_cast<long long>(n[i]) * (kk + 1)) / k[i] - (static_cast<long long>(n[i]) * kk) / k[i];
+          const double t = free_at.top() + static_cast<double>(len) + c_fix;
+          free_at.pop();
+          free_at.push(t);
+          if (t > makespan) makespan = t;
+        }
+      }
+    }
+    const double t = makespan + over;
+    if (t < best_t * 0.99) {
+      best_t = t;
+      best_k = k;
+    }
+  }
+  um.prefix[0] = 0;
+  um.max_k = 1;
+  for (int i = 0; i < np; ++i) {
+    um.prefix[i + 1] = um.prefix[i] + best_k[i];
+    um.max_k = imax(um.max_k, best_k[i]);
+  }
+  um.per_bh = um.prefix[np];
+  um.uniform = 0;
+  std::lock_guard<std::mutex> lock(g_plan_mu);
+  if (g_plans.size() > 1024) g_plans.clear();
+  g_plans[key] = um;
+  return um;
+}
+
 WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt, int sms) {
   WorkspaceLayout w;
   w.Lq = Li + Lt;
@@ -987,7 +1181,7 @@ WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt,
   off = align256(off + static_cast<long long>(B) * w.kwords * 4);
   w.qbits = off;
   off = align256(off + static_cast<long long>(B) * (w.qwords > 0 ? w.qwords : 1) * 4);
-  w.kv_splits = choose_kv_splits(B, H, w.Lq, w.Lk, sms);
+  w.kv_splits = split_capacity(B, H, w.Lq, w.Lk, sms);
   w.part_o = off;
   w.part_lse = off;
   if (w.kv_splits > 1) {
@@ -1001,7 +1195,7 @@ WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt,
 
 template <int kEmuPer8>
 int launch_attn2_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnKParams& kp,
-                   cudaStream_t stream) {
+                   const UnitMap& um, cudaStream_t stream) {
   const int smem = 1024 + kTileBytes * (2 + 2 * kStages) + 256 + kMaxSmemBitWords * 4;
   static bool attr_set = false;
   if (!attr_set) {
@@ -1009,8 +1203,9 @@ int launch_attn2_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
                                       smem));
     attr_set = true;
   }
-  dim3 grid((kp.num_qtiles + 1) / 2, kp.H, kp.B * kp.kv_splits);
-  attn_fwd2_kernel<kEmuPer8><<<grid, kThreads2, smem, stream>>>(mq, mk, mv, kp);
+  const long long units = static_cast<long long>(kp.B) * kp.H * um.per_bh;
+  if (units <= 0 || units > INT_MAX) return fail(HYB_ERR_UNSUPPORTED, "attention: %lld work units", units);
+  attn_fwd2_kernel<kEmuPer8><<<static_cast<unsigned>(units), kThreads2, smem, stream>>>(mq, mk, mv, kp, um);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
@@ -1026,17 +1221,19 @@ int exp_emu_per8() {
 }
 
 int launch_attn2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnKParams& kp,
-                 cudaStream_t stream) {
+                 const UnitMap& um, cudaStream_t stream) {
   switch (exp_emu_per8()) {
-    case 0: return launch_attn2_t<0>(mq, mk, mv, kp, stream);
-    case 1: return launch_attn2_t<1>(mq, mk, mv, kp, stream);
-    case 3: return launch_attn2_t<3>(mq, mk, mv, kp, stream);
-    case 4: return launch_attn2_t<4>(mq, mk, mv, kp, stream);
-    default: return launch_attn2_t<2>(mq, mk, mv, kp, stream);
+    case 0: return launch_attn2_t<0>(mq, mk, mv, kp, um, stream);
+    case 1: return launch_attn2_t<1>(mq, mk, mv, kp, um, stream);
+    case 3: return launch_attn2_t<3>(mq, mk, mv, kp, um, stream);
+    case 4: return launch_attn2_t<4>(mq, mk, mv, kp, um, stream);
+    default: return launch_attn2_t<2>(mq, mk, mv, kp, um, stream);
   }
 }
 
-int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
+// Validate the arguments and translate them into kernel parameters (no device access).
+int fill_params(const hyb_attn_args* a, AttnKParams& kp) {
+  memset(&kp, 0, sizeof(kp));
   if (a->D != kHD) return fail(HYB_ERR_UNSUPPORTED, "attention: head_dim %d != 128", a->D);
   const int Lik = a->img_k_len > 0 ? a->img_k_len : a->img_len;
   if (a->B <= 0 || a->H <= 0 || a->Lq < 0 || a->Lk < 0 || a->hist_len < 0 || a->img_len < 0 ||
@@ -1065,14 +1262,6 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
     if (a->out_txt == nullptr || !al16(a->out_txt) || (a->ot_sb % 8) || (a->ot_st % 8) || (a->ot_sh % 8))
       return fail(HYB_ERR_INVALID_ARG, "attention: text output misaligned");
   }
-  if (device_cc_major() != 10) return fail(HYB_ERR_UNSUPPORTED, "attention: requires an sm_100 GPU");
-  const int BH = a->B * a->H;
-  CUtensorMap mq, mk, mv;
-  int rc;
-  if ((rc = make_map(&mq, a->q, BH, a->Lq)) != HYB_OK) return rc;
-  if ((rc = make_map(&mk, a->k, BH, a->Lk > 0 ? a->Lk : 1)) != HYB_OK) return rc;
-  if ((rc = make_map(&mv, a->v, BH, a->Lk > 0 ? a->Lk : 1)) != HYB_OK) return rc;
-  AttnKParams kp;
   kp.B = a->B;
   kp.H = a->H;
   kp.Lq = a->Lq;
@@ -1114,10 +1303,24 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   kp.part_lse = a->part_lse;
   if (kp.kv_splits > 1 && (a->part_o == nullptr || a->part_lse == nullptr || !al16(a->part_o)))
     return fail(HYB_ERR_INVALID_ARG, "attention: kv_splits > 1 needs 16-byte aligned partial buffers");
-  int rc2 = launch_attn2(mq, mk, mv, kp, stream);
-  if (rc2 != HYB_OK || kp.kv_splits == 1) return rc2;
+  return HYB_OK;
+}
+
+int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
+  AttnKParams kp;
+  int rc = fill_params(a, kp);
+  if (rc != HYB_OK || a->Lq == 0) return rc;
+  if (device_cc_major() != 10) return fail(HYB_ERR_UNSUPPORTED, "attention: requires an sm_100 GPU");
+  const int BH = a->B * a->H;
+  CUtensorMap mq, mk, mv;
+  if ((rc = make_map(&mq, a->q, BH, a->Lq)) != HYB_OK) return rc;
+  if ((rc = make_map(&mk, a->k, BH, a->Lk > 0 ? a->Lk : 1)) != HYB_OK) return rc;
+  if ((rc = make_map(&mv, a->v, BH, a->Lk > 0 ? a->Lk : 1)) != HYB_OK) return rc;
+  const UnitMap um = plan_units(kp, kp.kv_splits, device_sm_count());
+  int rc2 = launch_attn2(mq, mk, mv, kp, um, stream);
+  if (rc2 != HYB_OK || um.max_k <= 1) return rc2;
   const long long rows = static_cast<long long>(kp.B) * kp.H * kp.Lq;
-  merge_splits_kernel<<<grid_for(rows * 32, 256), 256, 0, stream>>>(kp);
+  merge_splits_kernel<<<grid_for(rows * 32, 256), 256, 0, stream>>>(kp, um);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
@@ -1131,6 +1334,20 @@ extern "C" int hyb_attn_fwd(const hyb_attn_args* a, void* stream) {
   if (a == nullptr || a->abi_version != HYB_ABI_VERSION)
     return fail(HYB_ERR_INVALID_ARG, "attention: null args or ABI version mismatch");
   return attn_core(a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hyb_attn_work_plan(const hyb_attn_args* a, int32_t sms, int32_t* splits, int32_t n) {
+  if (a == nullptr || a->abi_version != HYB_ABI_VERSION)
+    return fail(HYB_ERR_INVALID_ARG, "work plan: null args or ABI version mismatch");
+  AttnKParams kp;
+  const int rc = fill_params(a, kp);
+  if (rc != HYB_OK) return rc;
+  const UnitMap um = plan_units(kp, kp.kv_splits, sms > 0 ? sms : device_sm_count());
+  for (int qp = 0; qp < um.npairs && qp < n; ++qp) {
+    const int i = um.npairs - 1 - qp;
+    splits[qp] = um.uniform > 0 ? um.uniform : um.prefix[i + 1] - um.prefix[i];
+  }
+  return um.npairs;
 }
 
 extern "C" int hyb_stage_head_major(int32_t B, int32_t L, int32_t H, int32_t D, const hyb_tensor4* src_k,

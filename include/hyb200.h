@@ -195,6 +195,14 @@ typedef struct hyb_attn_args {
 } hyb_attn_args;
 int hyb_attn_fwd(const hyb_attn_args* args, void* stream);
 
+/* Launch plan of hyb_attn_fwd for these arguments on a device with `sms` multiprocessors
+ * (sms <= 0: the current device): splits[i] = number of key slices query pair i (rows
+ * [256 i, 256 i + 256)) is cut into, for i < n; at most args->kv_splits.  Returns the number of
+ * query pairs, or a negative status.  Host only, no device work.  No reference counterpart
+ * (launch planning of this kernel: a heavy pair is cut into more slices so that every CTA of
+ * the launch gets about the same number of key tiles). */
+int hyb_attn_work_plan(const hyb_attn_args* args, int32_t sms, int32_t* splits, int32_t n);
+
 /* Decode a K/V block (or one Q tensor) [B, L, H, D] in BF16, E4M3 or INT8 with per-(token,
  * head) scales into head-major bf16 [B, H, L, 128], the operand layout hyb_attn_fwd reads
  * (codes times scale in fp32, one rounding, as dequantize_kv).  src_v and dst_v may both be

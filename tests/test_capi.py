@@ -132,3 +132,37 @@ def test_workspace_layout_is_consistent():
         assert 1 <= lay.kv_splits <= 16
         if lay.kv_splits > 1:
             assert lay.part_lse - lay.part_o >= lay.kv_splits * B * H * lay.Lq * 128 * 4
+
+
+def _plan_args(Lh, Li, Lt, H, G, cap):
+    a = _lib.AttnArgs()
+    a.abi_version = _lib.HYB_ABI_VERSION
+    a.B, a.H, a.D = 1, H, 128
+    a.Lq, a.Lk, a.hist_len, a.img_len, a.group_tokens = Li + Lt, Lh + Li + Lt, Lh, Li, G
+    a.q = a.k = a.v = a.kbits = a.out_img = a.out_txt = a.part_o = a.part_lse = 256  # never dereferenced
+    a.kwords = ((a.Lk + 127) // 128) * 4
+    a.oi_sb = a.oi_st = a.oi_sh = a.ot_sb = a.ot_st = a.ot_sh = 8
+    a.oi_seg = max(Li, 1)
+    a.kv_splits = cap
+    return a
+
+
+@pytest.mark.parametrize("H,cap", [(24, 4), (3, 7), (2, 1)])
+def test_work_plan_is_bounded_and_covers_every_pair(H, cap, monkeypatch):
+    """The host-side launch planner: one slice count per query pair, within the partial-buffer
+    capacity, heavier pairs never cut into fewer slices than lighter ones of the same chunk;
+    HYB_KV_SPLITS forces a uniform count."""
+    monkeypatch.delenv("HYB_KV_SPLITS", raising=False)
+    lib = _lib.load()
+    a = _plan_args(24960, 6240, 1, H, 1560, cap)
+    ks = (ctypes.c_int32 * 64)()
+    n = lib.hyb_attn_work_plan(ctypes.byref(a), 148, ks, 64)
+    assert n == 25
+    k = list(ks[:n])
+    assert all(1 <= x <= cap for x in k)
+    assert k == sorted(k)            # later query pairs see more frames of the chunk
+    monkeypatch.setenv("HYB_KV_SPLITS", "3")
+    n = lib.hyb_attn_work_plan(ctypes.byref(a), 148, ks, 64)
+    assert list(ks[:n]) == [min(3, cap)] * 25
+    a.D = 64
+    assert lib.hyb_attn_work_plan(ctypes.byref(a), 148, ks, 64) == _lib.HYB_ERR_UNSUPPORTED

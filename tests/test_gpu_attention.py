@@ -311,3 +311,26 @@ def test_key_slices_merge_to_the_same_result(cuda_lib, splits, monkeypatch):
     fin = torch.isfinite(ref_lse)
     assert torch.equal(torch.isfinite(lse.cpu()), fin)
     assert (lse.cpu()[fin] - ref_lse[fin]).abs().max() < 1e-3
+
+
+def test_balanced_work_list_matches_oracle(cuda_lib, monkeypatch):
+    """Without a forced split count the launch planner cuts query pairs into different numbers
+    of key slices; the merged result still equals the oracle."""
+    import ctypes
+    monkeypatch.delenv("HYB_KV_SPLITS", raising=False)
+    dev = torch.device("cuda")
+    B, Lh, Li, Lt, H, G = 1, 3000, 2000, 3, 2, 500
+    cache, cur, dk, dv = make_case(B, 1, Lh, Li, Lt, H, "fp8_e4m3", seed=611)
+    lse = torch.empty(B, H, Li + Lt, dtype=torch.float32, device=dev)
+    ws = hatt.Workspace()
+    out_img, out_txt = hatt.cached_attention_local(*(t.to(dev) for t in cur), to_dev(cache, dev), Lh,
+                                                   group_tokens=G, lse=lse, workspace=ws)
+    ks = (ctypes.c_int32 * 64)()
+    n = cuda_lib.hyb_attn_work_plan(ctypes.byref(ws.attn_args), 0, ks, 64)
+    assert n == (Li + Lt + 255) // 256
+    assert len(set(ks[:n])) > 1 and max(ks[:n]) > 1, list(ks[:n])
+    ref_img, ref_txt, ref_lse, (mag_img, mag_txt) = oatt.cached_attention(
+        *cur, dk, dv, group_tokens=G, return_lse=True, return_magnitude=True)
+    assert_close(out_img, ref_img, "image rows, balanced slices", mag_img)
+    assert_close(out_txt, ref_txt, "text rows", mag_txt)
+    assert (lse.cpu() - ref_lse).abs().max() < 1e-3
