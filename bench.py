@@ -37,6 +37,8 @@ sys.path.insert(0, str(REPO))
 H_TOTAL, D, T = 24, 128, 1560
 HIST_FRAMES, CHUNK_FRAMES, TXT = 16, 4, 1
 METRIC = "chunk-causal attn TFLOP/s (config 2: 4-frame chunk vs 16-frame FP8 KV cache, frame-causal)"
+METRIC4 = "chunk-causal attn TFLOP/s (config 4: 4-frame chunk vs 48-frame FP8 KV cache, frame-causal)"
+METRIC5 = "long-rollout attn TFLOP/s (config 5: 1-frame chunks vs sink + 32-frame window FP8 cache, append each step)"
 
 
 def parse():
@@ -47,9 +49,11 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config2", choices=["config2", "ring"],
+    ap.add_argument("--workload", default="config2", choices=["config2", "config4", "ring", "rollout"],
                     help="config2: 4-frame chunk vs 16-frame FP8 cache (Ulysses for N > 1); "
-                         "ring: config 3, 32,760-token frame-causal sequence, ring SP over N ranks")
+                         "config4: the same chunk vs a 48-frame cache; "
+                         "ring: config 3, 32,760-token frame-causal sequence, ring SP over N ranks; "
+                         "rollout: config 5, 1-frame chunks vs sink + 32-frame window, append each step")
     return ap.parse_args()
 
 
@@ -210,11 +214,12 @@ def dist_setup(n_gpus):
     return rank, world, local
 
 
-def build_problem(rank, world, device):
-    """Global chunk of config 2 split for Ulysses SP over `world` ranks."""
+def build_problem(rank, world, device, hist_frames=HIST_FRAMES):
+    """Global chunk of config 2 (config 4: 48 history frames) split for Ulysses SP over
+    `world` ranks."""
     from hy_nomas_b200 import kv_cache as kvc
     from hy_nomas_b200.synthetic import make_generator, seeded_kv
-    Lh = HIST_FRAMES * T
+    Lh = hist_frames * T
     Li = CHUNK_FRAMES * T
     Hl = H_TOTAL // world
     gen = make_generator(1236 + rank, device=device)
@@ -247,7 +252,8 @@ def run_b200(args):
     if world > 1:
         ps.initialize_sequence_parallel_group()
     os.environ["HYB_ASSUME_FINITE_KV"] = "1"   # validation stays on the device (status word)
-    prob = build_problem(rank, world, device)
+    hist_frames = 48 if args.workload == "config4" else HIST_FRAMES
+    prob = build_problem(rank, world, device, hist_frames)
     Lh, Li, Ls, Hl = prob["Lh"], prob["Li"], prob["Ls"], prob["Hl"]
     cache, cmask = prob["cache"], prob["cache_mask"]
     img, txt = prob["img"], prob["txt"]
@@ -302,6 +308,7 @@ def run_b200(args):
 
     # ---- dominant kernel alone: the tcgen05 attention launch over the staged buffers
     kern = time_attention_kernel(prob, device, args.steps)
+    cfg_no = 4 if args.workload == "config4" else 2
     peak_bf16, peak_hbm, peak_src = load_peaks()
     local_flops = attention_flops(Lh, Li, TXT, Hl, D, True, T)
     achieved = local_flops / (kern["ms"] * 1e-3) / 1e12
@@ -320,16 +327,18 @@ def run_b200(args):
     if rank != 0:
         return
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "metric": METRIC if cfg_no == 2 else METRIC4, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "bf16 MMA / fp32 softmax; e4m3 KV cache", "data": "synthetic (seeded N(0,1), 4 outlier channels/head x8)",
-        "config": {"workload": "config 2: 1x B200 single block (N>1: Ulysses SP over the same chunk)",
+        "config": {"workload": ("config 2: 1x B200 single block (N>1: Ulysses SP over the same chunk)" if cfg_no == 2
+                                else "config 4: 4-frame chunk vs 48-frame FP8 cache (N>1: Ulysses SP)"),
                    "heads": H_TOTAL, "head_dim": D, "history_tokens": Lh, "chunk_image_tokens": Li,
                    "text_tokens": TXT, "tokens_per_frame": T, "mask": "frame-level block-causal (G=1)",
                    "kv_cache": "fp8_e4m3 per-token-per-head scale", "append": "quantise-on-write of the chunk each step",
                    "parallelism": f"ulysses_sp{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (153 MB FP8 history + 115 MB bf16 chunk per step)",
+                   "l2": f"inputs larger than L2 ({2 * Lh * H_TOTAL * D / 1e6:.0f} MB FP8 history + 115 MB bf16 chunk "
+                         "per step)",
                    "tflop_per_step": round(flops_total / 1e12, 4)},
         # per step: append, mask, stage K/V, stage Q, attention (+ split merge), and for N > 1
         # the Ulysses pack and unpack kernels
@@ -461,6 +470,107 @@ def run_ring(args):
     print(json.dumps(line), flush=True)
 
 
+SINK, KEEP, PREFILL = 1, 32, 64
+
+
+def run_rollout(args):
+    """Config 5: a 64-frame rollout history kept as first-frame sink + the last 32 frames;
+    every step attends one new 1560-token frame (24 heads) to the 33 history frames and
+    itself, then appends the frame into the window ring (quantise-on-write).  N > 1: Ulysses
+    SP, each rank holds its heads' window and 1560/N of the frame's tokens."""
+    from hy_nomas_b200 import _lib
+    from hy_nomas_b200 import attention as hatt
+    from hy_nomas_b200 import parallel_states as ps
+    from hy_nomas_b200.flops import attention_flops
+    from hy_nomas_b200.synthetic import make_generator, seeded_kv
+    from hy_nomas_b200.window import SinkWindowKVCache
+    import torch.distributed as dist
+
+    rank, world, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        ps.initialize_sequence_parallel_group()
+    os.environ["HYB_ASSUME_FINITE_KV"] = "1"
+    Hl = H_TOTAL // world
+    Ls = T // world
+    gen = make_generator(1238 + rank, device=device)
+    win = SinkWindowKVCache(1, Hl, T, SINK, KEEP, device=device)
+    with torch.no_grad():
+        for _ in range(PREFILL):   # rollout history (untimed): 64 frames through the ring
+            win.append(seeded_kv((1, T, Hl, D), gen, device=device), seeded_kv((1, T, Hl, D), gen, device=device),
+                       assume_finite=True)
+    img = [seeded_kv((1, Ls, H_TOTAL, D), gen, device=device) for _ in range(3)]
+    txt = [img[0][:, :0] for _ in range(3)]
+    Lh = (SINK + KEEP) * T
+    flops_total = attention_flops(Lh, T, 0, H_TOTAL, D, True, 0)
+    sp_metadata = None
+    if world > 1:
+        from hy_nomas_b200 import communications as comm
+        sp_metadata = comm.prepare_sp_communication(Ls, H_TOTAL, device, ps.nccl_info.sp_group)
+    stream = torch.cuda.current_stream(device)
+
+    def step(q_img, k_img, v_img, q_txt, k_txt, v_txt):
+        with torch.no_grad():
+            return hatt.causal_attention_with_cache_mp(
+                (q_img, q_txt), (k_img, k_txt), (v_img, v_txt), win.view(), cache_valid_len=win.valid_len,
+                update_cache=True, cache_txt=False, tokens_per_frame=T, seg_ar_attention_backend="b200",
+                sp_metadata=sp_metadata, chunk_causal_frames=1)
+
+    for _ in range(args.warmup):
+        step(*img, *txt)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(*img, *txt)
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = tt.item()
+    _lib.check_device_status(device)
+    value = flops_total / (ms * 1e-3) / 1e12
+    host_in = [t.cpu().pin_memory() for t in (*img, *txt)]
+    ems, h2d, d2h = e2e_pipelined(lambda *x: step(*x), host_in, device, args.steps, args.warmup, world)
+    if world > 1:
+        ps.destroy_sequence_parallel_group()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC5, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "bf16 MMA / fp32 softmax; e4m3 KV cache", "data": "synthetic (seeded N(0,1), 4 outlier channels/head x8)",
+        "config": {"workload": "config 5: long rollout, 1-frame chunks, sink 1 + window 32 of a 64-frame history",
+                   "heads": H_TOTAL, "head_dim": D, "tokens_per_frame": T, "history_tokens": Lh,
+                   "visible_keys": Lh + T, "sink_frames": SINK, "window_frames": KEEP, "prefill_frames": PREFILL,
+                   "append": "quantise-on-write of each frame into its ring slot (no memmove)",
+                   "parallelism": f"ulysses_sp{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (155 MB FP8 window + 10 MB bf16 frame per step)",
+                   "tflop_per_step": round(flops_total / 1e12, 4)},
+        "gpu_launches": args.steps * (6 + (2 if world > 1 else 0)),
+        "e2e": {"value": round(flops_total / (ems * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "ms_per_step": round(ems, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": None,
+        "cpu_baseline": None,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def time_attention_kernel(prob, device, iters):
     """CUDA-event time of the attention kernel launch alone on the staged workspace."""
     from hy_nomas_b200 import _lib
@@ -573,6 +683,8 @@ def main():
         run_reference(args)
     elif args.workload == "ring":
         run_ring(args)
+    elif args.workload == "rollout":
+        run_rollout(args)
     else:
         run_b200(args)
 

@@ -311,7 +311,14 @@ def causal_attention_with_cache_mp(
         raise ValueError("Invalid KV valid length")
 
     # ---- cache write (validated before either payload is touched)
-    if update_cache:
+    # A window ring cache is written after the attention has staged its history (the slot a new
+    # frame takes may hold the oldest frame this call still attends).
+    window = kv_cache.get("window")
+    if update_cache and "history_rows" in kv_cache and window is None:
+        raise NotImplementedError("a ring cache without its SinkWindowKVCache cannot be written")
+    if update_cache and window is not None and cache_txt and txt_k.shape[1] > 0:
+        raise NotImplementedError("window caches hold whole image frames; pass cache_txt=False")
+    if update_cache and window is None:
         seg_k = [img_k, txt_k] if cache_txt else [img_k]
         seg_v = [img_v, txt_v] if cache_txt else [img_v]
         write_tokens = sum(t.shape[1] for t in seg_k)
@@ -335,7 +342,15 @@ def causal_attention_with_cache_mp(
                 cache_mask[:, cache_valid_len:new_end] = True
         stats["writes"] += 1
 
-    history_mask = cache_mask[:, :cache_valid_len] if (cache_mask is not None and cache_valid_len > 0) else None
+    # A sink + sliding-window ring cache (window.SinkWindowKVCache.view) carries the row map of
+    # its history; its cache_mask, if given, is indexed by cache row.
+    hist_rows = kv_cache.get("history_rows")
+    if hist_rows is not None:
+        if hist_rows.numel() != cache_valid_len:
+            raise ValueError("cache_valid_len must equal the window cache's history length")
+        history_mask = cache_mask if (cache_mask is not None and cache_valid_len > 0) else None
+    else:
+        history_mask = cache_mask[:, :cache_valid_len] if (cache_mask is not None and cache_valid_len > 0) else None
     attend_txt = bool(cache_txt or update_cache)
     group_tokens = int(chunk_causal_frames) * int(tokens_per_frame) if chunk_causal_frames else 0
 
@@ -346,8 +361,11 @@ def causal_attention_with_cache_mp(
     out_img, out_txt = cached_attention_local(
         img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, cache_valid_len,
         history_mask=history_mask, text_mask=cur_txt_mask, attend_txt=attend_txt,
-        group_tokens=group_tokens, out_img=o_send, out_img_strides=out_img_strides)
+        group_tokens=group_tokens, out_img=o_send, out_img_strides=out_img_strides, hist_rows=hist_rows)
     stats["calls"] += 1
+    if update_cache and window is not None:
+        window.append(img_k.detach(), img_v.detach(), assume_finite=_assume_finite())
+        stats["writes"] += 1
 
     if is_sp:
         img_attn = comm.all_to_all_o(o_send, group=sp_group, batch=B,
@@ -360,6 +378,6 @@ def causal_attention_with_cache_mp(
         img_attn = img_attn.to(dtype=img_output_dtype)
     if txt_attn.dtype != txt_output_dtype:
         txt_attn = txt_attn.to(dtype=txt_output_dtype)
-    img_attn = img_attn.reshape(img_attn.size(0), img_attn.size(1), -1)
-    txt_attn = txt_attn.reshape(txt_attn.size(0), txt_attn.size(1), -1)
+    img_attn = img_attn.reshape(img_attn.size(0), img_attn.size(1), img_attn.size(2) * img_attn.size(3))
+    txt_attn = txt_attn.reshape(txt_attn.size(0), txt_attn.size(1), txt_attn.size(2) * txt_attn.size(3))
     return img_attn, txt_attn

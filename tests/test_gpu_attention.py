@@ -334,3 +334,45 @@ def test_balanced_work_list_matches_oracle(cuda_lib, monkeypatch):
     assert_close(out_img, ref_img, "image rows, balanced slices", mag_img)
     assert_close(out_txt, ref_txt, "text rows", mag_txt)
     assert (lse.cpu() - ref_lse).abs().max() < 1e-3
+
+
+@pytest.mark.parametrize("sink,keep,fmt,write_in_call", [(1, 3, "fp8_e4m3", True), (2, 2, "int8", False)])
+def test_window_rollout_matches_oracle(cuda_lib, sink, keep, fmt, write_in_call):
+    """Long-rollout loop: every step attends a 1-frame chunk to the sink + sliding-window ring
+    through the drop-in call, then appends the frame (quantise-on-write into the recycled
+    slot).  Each step equals the oracle over the reference's slid history."""
+    from hy_nomas_b200.window import SinkWindowKVCache
+    from oracle import window as ow
+    dev = torch.device("cuda")
+    T, H = 96, 2
+    gen = make_generator(77 + keep)
+    win = SinkWindowKVCache(1, H, T, sink, keep, storage_format=fmt, device=dev)
+    all_k, all_v = [], []
+    for step in range(sink + keep + 4):
+        q, k, v = (seeded_kv((1, T, H, 128), gen) for _ in range(3))
+        tq, tk, tv = (seeded_kv((1, 0 if write_in_call else 1, H, 128), gen) for _ in range(3))
+        with torch.no_grad():
+            out_img, out_txt = hatt.causal_attention_with_cache_mp(
+                (q.to(dev), tq.to(dev)), (k.to(dev), tk.to(dev)), (v.to(dev), tv.to(dev)), win.view(),
+                cache_valid_len=win.valid_len, update_cache=write_in_call, cache_txt=not write_in_call,
+                tokens_per_frame=T, seg_ar_attention_backend="b200")
+            if not write_in_call:
+                win.append(k.to(dev), v.to(dev))
+        # oracle: history = the reference slide of every frame so far, decoded
+        frames = len(all_k)
+        if frames:
+            hk, _ = ow.slide(torch.cat(all_k, 1), frames, sink, keep, T)
+            hv, kept = ow.slide(torch.cat(all_v, 1), frames, sink, keep, T)
+            hk, hv = hk[:, :kept * T], hv[:, :kept * T]
+        else:
+            hk = hv = k[:, :0]
+        ref_img, ref_txt, _, (mag_img, mag_txt) = oatt.cached_attention(
+            q, k, v, tq, tk, tv, hk, hv, attend_txt=True, return_lse=True, return_magnitude=True)
+        assert_close(out_img.view(1, T, H, 128), ref_img, f"window step {step} image", mag_img)
+        assert out_txt.shape == (1, tq.shape[1], H * 128)
+        assert_close(out_txt.view(1, tq.shape[1], H, 128), ref_txt, f"window step {step} text", mag_txt)
+        ck, sk = oq.quantize(k, fmt)
+        cv, sv = oq.quantize(v, fmt)
+        all_k.append(oq.dequantize(ck, sk))
+        all_v.append(oq.dequantize(cv, sv))
+    assert win.frames == sink + keep + 4 and win.valid_len == (sink + keep) * T

@@ -131,3 +131,28 @@ def test_ring_plan_visibility_skips_future_blocks():
     assert plan.visible(0, 3, 0)            # no causal rule: every block is computed
     zz = RingPlan(400, 4, "zigzag")
     assert all(zz.visible(r, s, 50) for r in range(4) for s in range(4))
+
+
+@pytest.mark.parametrize("sink,keep,appends", [(1, 3, [1, 1, 1, 1, 1, 2, 1, 3]), (0, 2, [1, 1, 1, 1]),
+                                               (2, 4, [3, 4, 1, 1, 5])])
+def test_window_ring_matches_reference_slide(sink, keep, appends):
+    """The frame ring read through history_rows equals the reference's memmove slide
+    (restated in oracle.window): sink frames then the last `keep` frames, in order."""
+    from hy_nomas_b200.window import SinkWindowKVCache
+    from oracle import window as ow
+    T, H = 4, 1
+    win = SinkWindowKVCache(1, H, T, sink, keep, storage_format="bf16", device="cpu")
+    full = []          # reference cache: every frame appended, slid like the pipeline
+    count = 0
+    for n in appends:
+        frames = torch.arange(count, count + n, dtype=torch.float32).repeat_interleave(T)
+        k = frames.view(1, n * T, 1, 1).expand(1, n * T, H, 128).to(torch.bfloat16).contiguous()
+        win.append(k, k)
+        full.append(k)
+        count += n
+        assert win.history_frames() == ow.visible_frames(count, sink, keep)
+        ref_k, ref_frames = ow.slide(torch.cat(full, 1), count, sink, keep, T)
+        rows = win.history_rows()
+        assert rows.dtype == torch.int32 and rows.numel() == win.valid_len == ref_frames * T
+        got = win.cache["k"][:, rows.long()]
+        assert torch.equal(got, ref_k[:, :ref_frames * T])
