@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time eager calls instead of replaying one captured CUDA graph of the call")
     ap.add_argument("--workload", default="config2", choices=["config2", "config4", "ring", "rollout"],
                     help="config2: 4-frame chunk vs 16-frame FP8 cache (Ulysses for N > 1); "
                          "config4: the same chunk vs a 48-frame cache; "
@@ -123,6 +125,24 @@ class ClockSampler:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+def capture_step(step_fn, device):
+    """CUDA graph of one call of ``step_fn`` (all kernels and NCCL collectives of one step on
+    the capture stream); its replay repeats exactly that work on the same buffers.  Warm-up
+    calls run first on a side stream, as graph capture requires."""
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step_fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step_fn()
+    torch.cuda.synchronize(device)
+    return graph
 
 
 def e2e_pipelined(step_fn, host_in, device, steps, warmup, world):
@@ -277,6 +297,11 @@ def run_b200(args):
     for _ in range(args.warmup):
         step(*img, *txt)
     torch.cuda.synchronize(device)
+    graph = None if args.no_graph else capture_step(lambda: step(*img, *txt), device)
+    run_step = (lambda: step(*img, *txt)) if graph is None else graph.replay
+    for _ in range(args.warmup):
+        run_step()
+    torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
     sampler = ClockSampler(local)
@@ -288,7 +313,7 @@ def run_b200(args):
     torch.cuda.synchronize(device)
     t0.record(stream)
     for _ in range(args.steps):
-        step(*img, *txt)
+        run_step()
     t1.record(stream)
     torch.cuda.synchronize(device)
     if world > 1:
@@ -320,6 +345,8 @@ def run_b200(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_heads, reps=2)
 
+    del graph, run_step   # a graph holding NCCL calls is released before the process group
+    torch.cuda.synchronize(device)
     if world > 1:
         from hy_nomas_b200 import parallel_states as ps2
         ps2.destroy_sequence_parallel_group()
@@ -337,6 +364,7 @@ def run_b200(args):
                    "text_tokens": TXT, "tokens_per_frame": T, "mask": "frame-level block-causal (G=1)",
                    "kv_cache": "fp8_e4m3 per-token-per-head scale", "append": "quantise-on-write of the chunk each step",
                    "parallelism": f"ulysses_sp{world}" if world > 1 else "single",
+                   "timed_call": "eager" if args.no_graph else "CUDA graph replay of one drop-in call",
                    "l2": f"inputs larger than L2 ({2 * Lh * H_TOTAL * D / 1e6:.0f} MB FP8 history + 115 MB bf16 chunk "
                          "per step)",
                    "tflop_per_step": round(flops_total / 1e12, 4)},
@@ -392,6 +420,11 @@ def run_ring(args):
     for _ in range(args.warmup):
         step(q, k, v)
     torch.cuda.synchronize(device)
+    graph = None if args.no_graph else capture_step(lambda: step(q, k, v), device)
+    run_step = (lambda: step(q, k, v)) if graph is None else graph.replay
+    for _ in range(args.warmup):
+        run_step()
+    torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
     sampler = ClockSampler(local)
@@ -403,7 +436,7 @@ def run_ring(args):
     torch.cuda.synchronize(device)
     t0.record(stream)
     for _ in range(args.steps):
-        step(q, k, v)
+        run_step()
     t1.record(stream)
     torch.cuda.synchronize(device)
     if world > 1:
@@ -438,6 +471,8 @@ def run_ring(args):
     peak_bf16, _, peak_src = load_peaks()
     local_flops = flops_total / world
     achieved = local_flops / (kern_ms * 1e-3) / 1e12
+    del graph, run_step   # a graph holding NCCL calls is released before the process group
+    torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -452,6 +487,7 @@ def run_ring(args):
         "config": {"workload": "config 3: ring SP, 21 frames x 1560 tokens, frame-causal", "heads": H_TOTAL,
                    "head_dim": D, "seq_len": L, "tokens_per_frame": T, "layout": "zig-zag (2N chunks)",
                    "parallelism": f"ring_sp{world}" if world > 1 else "single",
+                   "timed_call": "eager" if args.no_graph else "CUDA graph replay of one ring call",
                    "kv_block": "fp8_e4m3 codes + fp32 per-(token, head) scales, quantised each step",
                    "l2": "inputs larger than L2 (201 MB bf16 per tensor over the job)",
                    "tflop_per_step": round(flops_total / 1e12, 4)},

@@ -6,7 +6,7 @@
 // (hymm/models/dit/modules/int8_kv_cache.py:149-158):
 //   peak  = max |x|                       (fp32)
 //   s     = peak > 0 ? peak / R : 1       (IEEE fp32 division, R = 127 or 448)
-//   y     = x / s                         (IEEE fp32 division)
+//   y     = x / s                         (IEEE fp32 division, correctly rounded: div_rn_by)
 //   INT8: code = clamp(y >= 0 ? floor(y + 0.5) : ceil(y - 0.5), -127, 127)
 //   E4M3: code = e4m3_rn(clamp(y, -448, 448))
 #include "hyb_common.cuh"
@@ -41,78 +41,128 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
   }
 }
 
+// x / s rounded to nearest, from r = RN(1/s): q0 = RN(x r), then two residual steps
+// q' = RN(q + r (x - s q)) with the residual formed exactly by the fma.  The first step
+// leaves q1 within one ulp of x / s; correcting a quotient that close with a correctly
+// rounded reciprocal gives RN(x / s) (P. Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", IBM J. Res. Develop. 34(1), 1990; restated in Muller
+// et al., Handbook of Floating-Point Arithmetic, on FMA-based division).  The argument needs
+// x, s and the residuals in the normal range: callers use it for |x|, s >= 2^-90 only.
+__device__ __forceinline__ float div_rn_by(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float q1 = __fmaf_rn(__fmaf_rn(-s, q0, x), r, q0);
+  return __fmaf_rn(__fmaf_rn(-s, q1, x), r, q1);
+}
+
+__device__ __forceinline__ float quotient(float x, float s, float r, bool fast_row) {
+  if (fast_row && fabsf(x) >= 0x1p-90f) return div_rn_by(x, s, r);
+  return __fdiv_rn(x, s);
+}
+
+// Quantise one 128-value row held by a 16-lane group (8 values per lane): absmax over the
+// group, the row scale, and the 8 codes of this lane.  Returns the 8 code bytes.
+__device__ __forceinline__ uint2 quantise_row8(const float (&x)[8], int fmt, unsigned half_mask, float& s_out,
+                                               bool& nonfinite) {
+  float peak = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    peak = fmaxf(peak, fabsf(x[i]));
+    nonfinite |= !isfinite(x[i]);
+  }
+#pragma unroll
+  for (int off = kRowLanes / 2; off >= 1; off >>= 1)
+    peak = fmaxf(peak, __shfl_xor_sync(half_mask, peak, off, kRowLanes));
+  const float denom = (fmt == HYB_FMT_INT8) ? 127.0f : 448.0f;
+  const float s = peak > 0.f ? __fdiv_rn(peak, denom) : 1.0f;
+  s_out = s;
+  const bool fast_row = s >= 0x1p-90f;
+  const float r = __frcp_rn(s);
+  uint32_t w[2];
+  if (fmt == HYB_FMT_INT8) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t acc = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float y = quotient(x[half * 4 + i], s, r, fast_row);
+        float r = (y >= 0.f) ? floorf(__fadd_rn(y, 0.5f)) : ceilf(__fsub_rn(y, 0.5f));
+        r = fminf(fmaxf(r, -127.f), 127.f);
+        const int8_t c = static_cast<int8_t>(static_cast<int>(r));
+        acc |= static_cast<uint32_t>(static_cast<uint8_t>(c)) << (8 * i);
+      }
+      w[half] = acc;
+    }
+  } else {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t acc = 0;
+#pragma unroll
+      for (int i = 0; i < 4; i += 2) {
+        float2 y;
+        y.x = fminf(fmaxf(quotient(x[half * 4 + i], s, r, fast_row), -448.f), 448.f);
+        y.y = fminf(fmaxf(quotient(x[half * 4 + i + 1], s, r, fast_row), -448.f), 448.f);
+        const __nv_fp8x2_storage_t c2 = __nv_cvt_float2_to_fp8x2(y, __NV_SATFINITE, __NV_E4M3);
+        acc |= static_cast<uint32_t>(c2) << (8 * i);
+      }
+      w[half] = acc;
+    }
+  }
+  return make_uint2(w[0], w[1]);
+}
+
+// One 16-lane group per (batch, token, head) row, K and V of the row together, two rows per
+// iteration: four 16-byte loads in flight per lane before any arithmetic.  Row indices are
+// 32-bit (the launcher checks B * (L + L2) * H * 16 < 2^31).
+constexpr int kAppendRowsPerIter = 2;
+
+__device__ __forceinline__ const __nv_bfloat16* append_src(const AppendParams& p, int which, int b, int t, int h,
+                                                           int sub) {
+  return t < p.L ? p.src[which] + b * p.s_b[which] + t * p.s_t[which] + h * p.s_h[which] + sub * 8
+                 : p.src2[which] + b * p.s2_b[which] + (t - p.L) * p.s2_t[which] + h * p.s2_h[which] + sub * 8;
+}
+
 __global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams p) {
-  const int which = blockIdx.y;  // 0 = K, 1 = V
   const int Lt = p.L + p.L2;
-  const long long rows = static_cast<long long>(p.B) * Lt * p.H;
+  const int rows = p.B * Lt * p.H;
   const int sub = threadIdx.x & (kRowLanes - 1);
-  const long long row0 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / kRowLanes;
-  const long long row_step = static_cast<long long>(gridDim.x) * blockDim.x / kRowLanes;
+  // The two 16-lane halves of a warp own different rows and may leave the loop on different
+  // iterations, so each half shuffles under its own lane mask.
+  const unsigned half_mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
+  const int group = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) / kRowLanes);
+  const int groups = static_cast<int>(gridDim.x * blockDim.x / kRowLanes);
   bool nonfinite = false;
-  for (long long row = row0; row < rows; row += row_step) {
-    const int h = static_cast<int>(row % p.H);
-    const long long bt = row / p.H;
-    const int t = static_cast<int>(bt % Lt);
-    const int b = static_cast<int>(bt / Lt);
-    const __nv_bfloat16* src =
-        t < p.L ? p.src[which] + b * p.s_b[which] + t * p.s_t[which] + h * p.s_h[which] + sub * 8
-                : p.src2[which] + b * p.s2_b[which] + (t - p.L) * p.s2_t[which] + h * p.s2_h[which] +
-                      sub * 8;
-    uint4 raw = *reinterpret_cast<const uint4*>(src);
-    float x[8];
-    unpack8(raw, x);
-    float peak = 0.f;
+  for (int base = group; base < rows; base += groups * kAppendRowsPerIter) {
+    int bb[kAppendRowsPerIter], tt[kAppendRowsPerIter], hh[kAppendRowsPerIter];
+    bool live[kAppendRowsPerIter];
+    uint4 raw[kAppendRowsPerIter][2];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      peak = fmaxf(peak, fabsf(x[i]));
-      nonfinite |= !isfinite(x[i]);
+    for (int u = 0; u < kAppendRowsPerIter; ++u) {
+      const int row = base + u * groups;
+      live[u] = row < rows;
+      const int rr = live[u] ? row : base;
+      hh[u] = rr % p.H;
+      const int bt = rr / p.H;
+      tt[u] = bt % Lt;
+      bb[u] = bt / Lt;
+#pragma unroll
+      for (int which = 0; which < 2; ++which)
+        raw[u][which] = __ldg(reinterpret_cast<const uint4*>(append_src(p, which, bb[u], tt[u], hh[u], sub)));
     }
-    // The two 16-lane halves of a warp own different rows and may leave the loop on
-    // different iterations, so each half shuffles under its own lane mask.
-    const unsigned half_mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
 #pragma unroll
-    for (int off = kRowLanes / 2; off >= 1; off >>= 1)
-      peak = fmaxf(peak, __shfl_xor_sync(half_mask, peak, off, kRowLanes));
-    const float denom = (p.fmt == HYB_FMT_INT8) ? 127.0f : 448.0f;
-    const float s = peak > 0.f ? __fdiv_rn(peak, denom) : 1.0f;
-    const long long dst_off =
-        b * p.d_b + (t + p.start) * p.d_t + h * p.d_h + sub * 8;
-    if (p.fmt == HYB_FMT_INT8) {
-      uint32_t w[2];
+    for (int u = 0; u < kAppendRowsPerIter; ++u) {
+      if (!live[u]) continue;   // uniform over the 16-lane group that owns the row
+      const long long dst_off = bb[u] * p.d_b + (tt[u] + p.start) * p.d_t + hh[u] * p.d_h + sub * 8;
+      const long long sc_off = bb[u] * p.c_b + (tt[u] + p.start) * p.c_t + hh[u] * p.c_h;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t acc = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float y = __fdiv_rn(x[half * 4 + i], s);
-          float r = (y >= 0.f) ? floorf(__fadd_rn(y, 0.5f)) : ceilf(__fsub_rn(y, 0.5f));
-          r = fminf(fmaxf(r, -127.f), 127.f);
-          const int8_t c = static_cast<int8_t>(static_cast<int>(r));
-          acc |= static_cast<uint32_t>(static_cast<uint8_t>(c)) << (8 * i);
-        }
-        w[half] = acc;
+      for (int which = 0; which < 2; ++which) {
+        float x[8];
+        unpack8(raw[u][which], x);
+        float s;
+        const uint2 codes = quantise_row8(x, p.fmt, half_mask, s, nonfinite);
+        *reinterpret_cast<uint2*>(static_cast<uint8_t*>(p.dst[which]) + dst_off) = codes;
+        if (sub == 0) p.scale[which][sc_off] = s;
       }
-      *reinterpret_cast<uint2*>(static_cast<int8_t*>(p.dst[which]) + dst_off) =
-          make_uint2(w[0], w[1]);
-    } else {
-      uint32_t w[2];
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t acc = 0;
-#pragma unroll
-        for (int i = 0; i < 4; i += 2) {
-          float2 y;
-          y.x = fminf(fmaxf(__fdiv_rn(x[half * 4 + i], s), -448.f), 448.f);
-          y.y = fminf(fmaxf(__fdiv_rn(x[half * 4 + i + 1], s), -448.f), 448.f);
-          const __nv_fp8x2_storage_t c2 = __nv_cvt_float2_to_fp8x2(y, __NV_SATFINITE, __NV_E4M3);
-          acc |= static_cast<uint32_t>(c2) << (8 * i);
-        }
-        w[half] = acc;
-      }
-      *reinterpret_cast<uint2*>(static_cast<uint8_t*>(p.dst[which]) + dst_off) =
-          make_uint2(w[0], w[1]);
     }
-    if (sub == 0) p.scale[which][b * p.c_b + (t + p.start) * p.c_t + h * p.c_h] = s;
   }
   if (p.status != nullptr && __any_sync(0xffffffffu, nonfinite) && (threadIdx.x & 31) == 0)
     atomicOr(p.status, HYB_DEV_NONFINITE);
@@ -267,8 +317,12 @@ extern "C" int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, 
   p.c_h = s_sh;
   p.status = dev_status;
   const long long rows = static_cast<long long>(B) * (L + L2) * H;
-  dim3 grid(grid_for(rows * kRowLanes, 256), 2);
-  kv_append_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  if (rows * kRowLanes >= (1LL << 31))
+    return fail(HYB_ERR_UNSUPPORTED, "kv append: %lld rows in one call (split the call)", rows);
+  // about two iterations per group: enough loads in flight without a long grid-stride tail
+  long long blocks = (rows * kRowLanes + 256LL * 2 * kAppendRowsPerIter - 1) / (256LL * 2 * kAppendRowsPerIter);
+  blocks = blocks < 1 ? 1 : (blocks > 148LL * 64 ? 148LL * 64 : blocks);
+  kv_append_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }

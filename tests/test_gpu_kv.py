@@ -93,3 +93,34 @@ def test_capacity_and_shape_errors(cuda_lib):
         kvc.quantize_kv_pair_into(cache, k, k[:, :4], 0)
     with pytest.raises(ValueError):
         kvc.dequantize_kv(cache, "k", 17)
+
+
+@pytest.mark.parametrize("fmt", ["int8", "fp8_e4m3"])
+def test_append_bit_exact_on_adversarial_rows(cuda_lib, fmt):
+    """Rows whose quotients x / s sit on rounding ties of the code format, rows spanning 2^-133
+    .. 2^20 in magnitude, negative zeros, and rows whose absmax is a bf16 subnormal."""
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(4242)
+    L, H = 512, 4
+    x = torch.randn(1, L, H, 128, generator=g)
+    mags = torch.pow(2.0, torch.randint(-60, 21, (1, L, H, 1), generator=g).float())
+    x = x * mags
+    x[:, :32] *= torch.pow(2.0, torch.randint(-133, -100, (1, 32, H, 128), generator=g).float())  # tiny, mixed
+    x[:, 32:40] = 2.0 ** -130 * torch.randint(-3, 4, (1, 8, H, 128), generator=g).float()        # subnormal absmax
+    x[:, 40:48] = -0.0
+    x[:, 48:56, :, 5] = 1.0
+    # ties: absmax 448 (s = 1) or 127 (s = 1), values halfway between neighbouring codes
+    top = 448.0 if fmt == "fp8_e4m3" else 127.0
+    ties = torch.tensor([1.0625, -1.0625, 2.125, 0.5 + 2 ** -5, 3.5 * 2 ** -8, -0.5, 1.5, -2.5, 100.5, 13.0])
+    x[:, 56:64] = ties.repeat(13)[:128].view(1, 1, 1, 128)
+    x[:, 56:64, :, 0] = top
+    x[:, 64:72] = x[:, 56:64] * 2.0 ** -40   # the same ties at a power-of-two scale
+    x = x.to(torch.bfloat16)
+    k, v = x.to(dev), (-x).to(dev)
+    cache = _block(fmt, 1, L, H, dev)
+    kvc.quantize_kv_pair_into(cache, k, v, 0)
+    torch.cuda.synchronize()
+    for key, src in (("k", x), ("v", -x)):
+        codes, scale = oq.quantize(src, fmt)
+        assert np.array_equal(_codes_np(cache[key]), _codes_np(codes)), key
+        assert np.array_equal(cache[f"{key}_scale"].cpu().numpy().view(np.int32), scale.numpy().view(np.int32))
