@@ -337,7 +337,7 @@ def run_b200(args):
     peak_bf16, peak_hbm, peak_src = load_peaks()
     local_flops = attention_flops(Lh, Li, TXT, Hl, D, True, T)
     achieved = local_flops / (kern["ms"] * 1e-3) / 1e12
-    traffic = load_traffic().get("attn_fwd_config2_bytes_per_launch")
+    traffic = load_traffic().get("attn_fwd_config2_bytes_per_launch") if args.workload == "config2" else None
     if traffic is not None and world > 1:
         traffic = traffic * Hl / H_TOTAL
 
@@ -375,7 +375,7 @@ def run_b200(args):
                 "ms_per_step": round(ems, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_bf16, "unit": "TFLOP/s",
                      "frac": round(achieved / peak_bf16, 4), "traffic": traffic,
-                     "kernel": "attn_fwd_kernel (tcgen05 kind::f16, bf16 operands)",
+                     "kernel": "attn_fwd2_kernel (tcgen05 kind::f16, bf16 operands)",
                      "kernel_ms": round(kern["ms"], 4), "peak_source": f"{peak_src} bf16 dense (cuBLAS)",
                      "algorithmic_unit": "4*H*D FLOP per visible (query, key) pair"},
         "cpu_baseline": cpu,
