@@ -145,11 +145,13 @@ def capture_step(step_fn, device):
     return graph
 
 
-def e2e_pipelined(step_fn, host_in, device, steps, warmup, world):
+def e2e_pipelined(step_fn, host_in, device, steps, warmup, world, static_outputs=False):
     """Mean ms per step through the public call with host buffers: every step copies its
     inputs from pinned host memory (H2D stream) and reads its outputs back into pinned host
     memory (D2H stream); inputs are double-buffered so that step i+1's copies overlap step
-    i's compute.  Device-timed on the caller's stream, max over ranks."""
+    i's compute.  With ``static_outputs`` (a graphed call returns the same output tensors for
+    a buffer set) a step also waits until the read-back of step i-2 has finished.
+    Device-timed on the caller's stream, max over ranks."""
     import torch.distributed as dist
     compute = torch.cuda.current_stream(device)
     h2d = torch.cuda.Stream(device=device)
@@ -160,6 +162,7 @@ def e2e_pipelined(step_fn, host_in, device, steps, warmup, world):
 
     def run(n, start_event=None):
         free = [None, None]
+        read_back = [None, None]
         for i in range(n):
             j = i % 2
             with torch.cuda.stream(h2d):
@@ -172,6 +175,8 @@ def e2e_pipelined(step_fn, host_in, device, steps, warmup, world):
                 copied = torch.cuda.Event()
                 copied.record(h2d)
             compute.wait_event(copied)
+            if static_outputs and read_back[j] is not None:
+                compute.wait_event(read_back[j])
             outs = step_fn(*dev_in[j])
             done = torch.cuda.Event()
             done.record(compute)
@@ -184,10 +189,13 @@ def e2e_pipelined(step_fn, host_in, device, steps, warmup, world):
                 for h_, o in zip(host_out[j], outs):
                     h_.copy_(o, non_blocking=True)
                     o.record_stream(d2h)
+                ev = torch.cuda.Event()
+                ev.record(d2h)
+                read_back[j] = ev
         compute.wait_stream(h2d)
         compute.wait_stream(d2h)
 
-    run(max(2, warmup))
+    run(max(6 if static_outputs else 2, warmup))   # a graphed call captures both buffer sets here
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
@@ -328,8 +336,11 @@ def run_b200(args):
     value = flops_total / (ms * 1e-3) / 1e12
 
     # ---- end-to-end through the public API with pinned host buffers
+    from hy_nomas_b200.graphs import GraphedCall
     host_in = [t.cpu().pin_memory() for t in (*img, *txt)]
-    ems, h2d, d2h = e2e_pipelined(lambda *x: step(*x), host_in, device, args.steps, args.warmup, world)
+    call = step if args.no_graph else GraphedCall(step, device)
+    ems, h2d, d2h = e2e_pipelined(call, host_in, device, args.steps, args.warmup, world,
+                                  static_outputs=not args.no_graph)
 
     # ---- dominant kernel alone: the tcgen05 attention launch over the staged buffers
     kern = time_attention_kernel(prob, device, args.steps)
@@ -345,7 +356,9 @@ def run_b200(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_heads, reps=2)
 
-    del graph, run_step   # a graph holding NCCL calls is released before the process group
+    del graph, run_step   # graphs holding NCCL calls are released before the process group
+    if not args.no_graph:
+        call.release()
     torch.cuda.synchronize(device)
     if world > 1:
         from hy_nomas_b200 import parallel_states as ps2
@@ -464,14 +477,19 @@ def run_ring(args):
     # end to end: pinned host shards in, output shard back, every step
     host_in = [t.cpu().pin_memory() for t in (q, k, v)]
 
-    def ring_call(q_, k_, v_):   # a fresh output per call: its read-back overlaps the next call
+    def ring_call(q_, k_, v_):   # a fresh output per eager call: its read-back overlaps the next
         return (ring.ring_attention(q_, k_, v_, group, seq_len=L, tokens_per_frame=T),)
 
-    ems, h2d, d2h = e2e_pipelined(ring_call, host_in, device, args.steps, args.warmup, world)
+    from hy_nomas_b200.graphs import GraphedCall
+    rcall = ring_call if args.no_graph else GraphedCall(ring_call, device)
+    ems, h2d, d2h = e2e_pipelined(rcall, host_in, device, args.steps, args.warmup, world,
+                                  static_outputs=not args.no_graph)
     peak_bf16, _, peak_src = load_peaks()
     local_flops = flops_total / world
     achieved = local_flops / (kern_ms * 1e-3) / 1e12
-    del graph, run_step   # a graph holding NCCL calls is released before the process group
+    del graph, run_step   # graphs holding NCCL calls are released before the process group
+    if not args.no_graph:
+        rcall.release()
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()

@@ -376,3 +376,35 @@ def test_window_rollout_matches_oracle(cuda_lib, sink, keep, fmt, write_in_call)
         all_k.append(oq.dequantize(ck, sk))
         all_v.append(oq.dequantize(cv, sv))
     assert win.frames == sink + keep + 4 and win.valid_len == (sink + keep) * T
+
+
+def test_graphed_call_replays_the_drop_in(cuda_lib):
+    """GraphedCall: warm-up calls run eagerly, then one captured graph per input buffer set;
+    replayed outputs equal the eager call's bit for bit and the cache write is repeated."""
+    import os
+    from hy_nomas_b200.graphs import GraphedCall
+    os.environ["HYB_ASSUME_FINITE_KV"] = "1"
+    try:
+        dev = torch.device("cuda")
+        B, Lh, Li, Lt, H, G = 1, 512, 256, 1, 2, 128
+        cache, cur, _, _ = make_case(B, 1, Lh, Li, Lt, H, "fp8_e4m3", seed=812)
+        cache = to_dev(cache, dev)
+        bufs = [[t.to(dev) for t in cur] for _ in range(2)]
+
+        def step(qi, ki, vi, qt, kt, vt):
+            with torch.no_grad():
+                return hatt.causal_attention_with_cache_mp(
+                    (qi, qt), (ki, kt), (vi, vt), cache, cache_valid_len=Lh, update_cache=True,
+                    tokens_per_frame=G, chunk_causal_frames=1, seg_ar_attention_backend="b200")
+
+        ref = [t.clone() for t in step(*bufs[0])]
+        call = GraphedCall(step, dev, warmup=1)
+        for i in range(6):
+            out = call(*bufs[i % 2])
+            torch.cuda.synchronize()
+            for a, b in zip(out, ref):
+                assert torch.equal(a, b), i
+        assert len(call._graphs) == 2
+        call.release()
+    finally:
+        os.environ.pop("HYB_ASSUME_FINITE_KV", None)
