@@ -361,7 +361,9 @@ def run_b200(args):
         call.release()
     torch.cuda.synchronize(device)
     if world > 1:
+        from hy_nomas_b200 import communications as comm2
         from hy_nomas_b200 import parallel_states as ps2
+        comm2.release_peer_exchanges()
         ps2.destroy_sequence_parallel_group()
         dist.destroy_process_group()
     if rank != 0:
@@ -377,6 +379,9 @@ def run_b200(args):
                    "text_tokens": TXT, "tokens_per_frame": T, "mask": "frame-level block-causal (G=1)",
                    "kv_cache": "fp8_e4m3 per-token-per-head scale", "append": "quantise-on-write of the chunk each step",
                    "parallelism": f"ulysses_sp{world}" if world > 1 else "single",
+                   "exchange": ("peer memory (CUDA IPC push kernels + device barrier)"
+                                if world > 1 and os.environ.get("HYB_PEER_EXCHANGE", "1") != "0"
+                                else ("NCCL all_to_all_single" if world > 1 else None)),
                    "timed_call": "eager" if args.no_graph else "CUDA graph replay of one drop-in call",
                    "l2": f"inputs larger than L2 ({2 * Lh * H_TOTAL * D / 1e6:.0f} MB FP8 history + 115 MB bf16 chunk "
                          "per step)",
@@ -599,6 +604,9 @@ def run_rollout(args):
     host_in = [t.cpu().pin_memory() for t in (*img, *txt)]
     ems, h2d, d2h = e2e_pipelined(lambda *x: step(*x), host_in, device, args.steps, args.warmup, world)
     if world > 1:
+        from hy_nomas_b200 import communications as comm2
+        torch.cuda.synchronize(device)
+        comm2.release_peer_exchanges()
         ps.destroy_sequence_parallel_group()
         dist.destroy_process_group()
     if rank != 0:

@@ -91,6 +91,12 @@ class AttnArgs(ctypes.Structure):
     ]
 
 
+class PeerSync(ctypes.Structure):
+    """``hyb_peer_sync``."""
+
+    _fields_ = [("flags", c_ptr * 64), ("state", c_ptr), ("dev_status", c_ptr)]
+
+
 class WorkspaceLayout(ctypes.Structure):
     """``hyb_workspace_layout``."""
 
@@ -108,6 +114,15 @@ SIGNATURES = {
                                      ctypes.POINTER(Tensor4), c_ptr, c_ptr, c_ptr]),
     "hyb_fill_key_bits": (c_i32, [c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "hyb_attn_work_plan": (c_i32, [ctypes.POINTER(AttnArgs), c_i32, ctypes.POINTER(c_i32), c_i32]),
+    "hyb_peer_alloc": (c_i32, [c_i64, ctypes.POINTER(c_ptr), c_ptr]),
+    "hyb_peer_open": (c_i32, [c_ptr, ctypes.POINTER(c_ptr)]),
+    "hyb_peer_close": (c_i32, [c_ptr]),
+    "hyb_peer_free": (c_i32, [c_ptr]),
+    "hyb_ulysses_push_qkv": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(Tensor4),
+                                     ctypes.POINTER(Tensor4), ctypes.POINTER(Tensor4), ctypes.POINTER(c_ptr),
+                                     ctypes.POINTER(PeerSync), c_ptr]),
+    "hyb_ulysses_push_o": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_ptr, ctypes.POINTER(Tensor4),
+                                   ctypes.POINTER(c_ptr), ctypes.POINTER(c_ptr), ctypes.POINTER(PeerSync), c_ptr]),
     "hyb_version": (c_i32, []),
     "hyb_last_error": (c_i32, [ctypes.c_char_p, ctypes.c_size_t]),
     "hyb_device_supported": (c_i32, []),

@@ -267,11 +267,18 @@ def causal_attention_with_cache_mp(
     from . import communications as comm
 
     o_send = None
+    exchange = None
     if is_sp:
         if sp_metadata is None:
             sp_metadata = comm.prepare_sp_communication(img_q.shape[1], img_q.shape[2], img_q.device, sp_group)
-        img_q, img_k, img_v = comm.all_to_all_qkv(
-            img_q, img_k, img_v, group=sp_group, sequence_lengths=sp_metadata.sequence_lengths)
+        if (comm.peer_exchange_enabled(sp_metadata.sequence_lengths, img_q.shape[2])
+                and img_q.dtype == torch.bfloat16 and img_k.dtype == torch.bfloat16 and img_v.dtype == torch.bfloat16):
+            exchange = comm.peer_exchange(sp_group, img_q.shape[0], img_q.shape[1], img_q.shape[2], txt_q.shape[1],
+                                          img_q.device)
+            img_q, img_k, img_v = exchange.push_qkv(img_q, img_k, img_v)
+        else:
+            img_q, img_k, img_v = comm.all_to_all_qkv(
+                img_q, img_k, img_v, group=sp_group, sequence_lengths=sp_metadata.sequence_lengths)
         if txt_q.shape[2] != img_q.shape[2]:
             shard = img_q.shape[2]
             start_h = info.rank_within_spgroup * shard
@@ -367,7 +374,9 @@ def causal_attention_with_cache_mp(
         window.append(img_k.detach(), img_v.detach(), assume_finite=_assume_finite())
         stats["writes"] += 1
 
-    if is_sp:
+    if is_sp and exchange is not None:
+        img_attn, txt_attn = exchange.push_o(o_send, out_txt)
+    elif is_sp:
         img_attn = comm.all_to_all_o(o_send, group=sp_group, batch=B,
                                      sequence_lengths=sp_metadata.sequence_lengths, heads_local=H, dim=D)
         txt_attn = comm.all_gather(out_txt, dim=2, group=sp_group, sizes=sp_metadata.head_sizes)

@@ -217,3 +217,148 @@ def all_gather(input_: torch.Tensor, dim: int = 1, group=None, sizes=None):
     gathered = gathered.view(world, *x.shape)
     parts = [gathered[r, :sizes[r]] for r in range(world)]
     return torch.cat(parts, dim=0).movedim(0, dim).contiguous()
+
+
+# ------------------------------------------------------------------------------------------
+# Exchange over peer memory (CUDA IPC): replaces the three collectives of one Ulysses call.
+# ------------------------------------------------------------------------------------------
+class _DeviceArray:
+    """__cuda_array_interface__ view of a raw device allocation (for torch.as_tensor)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def _bf16_tensor(ptr: int, shape, device) -> torch.Tensor:
+    return torch.as_tensor(_DeviceArray(ptr, shape, "<i2"), device=device).view(torch.bfloat16)
+
+
+class PeerExchange:
+    """Ulysses exchange of one geometry (group, batch B, per-rank length Ls, heads H, text
+    length Lt) over buffers that every rank maps with CUDA IPC.  ``push_qkv`` writes this rank's
+    Q|K|V heads straight into every rank's receive buffer (the receive layout of
+    ``all_to_all_qkv``; two buffers used alternately, so a rank that runs ahead never
+    overwrites one a slower rank still reads) and ``push_o`` writes this rank's output heads
+    and text rows straight into every rank's output buffers; each is one kernel ending in a
+    device-side barrier.  Equal sequence lengths on every rank."""
+
+    def __init__(self, group, B: int, Ls: int, H: int, Lt: int, device):
+        self.group = group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.B, self.Ls, self.H, self.Lt = B, Ls, H, Lt
+        self.Hp = H // self.P
+        self.device = torch.device(device)
+        self.lib = lib = _lib.load()
+        P, Hp, D = self.P, self.Hp, 128
+        sizes = [P * Ls * 3 * B * Hp * D * 2, P * Ls * 3 * B * Hp * D * 2, B * Ls * H * D * 2,
+                 max(B * Lt * H * D * 2, 256), 256]
+        self._local = []
+        handles = bytearray()
+        with torch.cuda.device(self.device):
+            for nbytes in sizes:
+                ptr = ctypes.c_void_p()
+                h = (ctypes.c_uint8 * 64)()
+                _lib.check(lib.hyb_peer_alloc(max(int(nbytes), 256), ctypes.byref(ptr), h), "peer alloc")
+                self._local.append(ptr.value)
+                handles += bytes(h)
+            mine = torch.tensor(list(handles), dtype=torch.uint8, device=self.device)
+            every = torch.empty((P, mine.numel()), dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            every = every.cpu().numpy()
+            self._opened = []
+            ptrs = [[0] * P for _ in sizes]
+            for rr in range(P):
+                for i in range(len(sizes)):
+                    if rr == self.rank:
+                        ptrs[i][rr] = self._local[i]
+                        continue
+                    peer = ctypes.c_void_p()
+                    _lib.check(lib.hyb_peer_open(bytes(every[rr, 64 * i:64 * (i + 1)]), ctypes.byref(peer)),
+                               "peer open")
+                    ptrs[i][rr] = peer.value
+                    self._opened.append(peer.value)
+        recv_shape = (P, Ls, 3 * B, Hp, D)
+        self.recv = [_bf16_tensor(self._local[0], recv_shape, self.device),
+                     _bf16_tensor(self._local[1], recv_shape, self.device)]
+        self.out = _bf16_tensor(self._local[2], (B, Ls, H, D), self.device)
+        self.txt_out = _bf16_tensor(self._local[3], (B, Lt, H, D), self.device) if Lt else None
+        self.state = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.sync = _lib.PeerSync()
+        for rr in range(P):
+            self.sync.flags[rr] = ptrs[4][rr]
+        self.sync.state = self.state.data_ptr()
+        self.sync.dev_status = _lib.device_status(self.device).data_ptr()
+        vp = ctypes.c_void_p * P
+        self._recv_tab = [vp(*ptrs[0]), vp(*ptrs[1])]
+        self._out_tab = vp(*ptrs[2])
+        self._txt_tab = vp(*ptrs[3])
+        self.calls = 0
+        # every rank has mapped every buffer before anyone writes into them
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+
+    def push_qkv(self, q, k, v):
+        """Sequence-sharded q, k, v [B, Ls, H, D] -> head-sharded [B, P*Ls, H/P, D] views."""
+        cur = self.calls % 2
+        self.calls += 1
+        views = [_lib.bf16_view(t) for t in (q, k, v)]
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.hyb_ulysses_push_qkv(self.P, self.rank, self.B, self.Ls, self.H, 128,
+                                                     *(ctypes.byref(x) for x in views), self._recv_tab[cur],
+                                                     ctypes.byref(self.sync), _lib.stream_ptr(self.device)),
+                       "ulysses push qkv")
+        full = self.recv[cur].reshape(self.P * self.Ls, 3 * self.B, self.Hp, 128).permute(1, 0, 2, 3)
+        return tuple(full[i * self.B:(i + 1) * self.B] for i in range(3))
+
+    def push_o(self, o_send, out_txt):
+        """This rank's heads (o_send [P, H/P, Ls, B, D], out_txt [B, Lt, H/P, D]) -> fresh
+        [B, Ls, H, D] image and [B, Lt, H, D] text outputs of this rank."""
+        txt_view = _lib.bf16_view(out_txt) if self.Lt else None
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.hyb_ulysses_push_o(self.P, self.rank, self.B, self.Ls, self.Lt, self.H, 128,
+                                                   o_send.data_ptr(),
+                                                   ctypes.byref(txt_view) if txt_view is not None else None,
+                                                   self._out_tab, self._txt_tab, ctypes.byref(self.sync),
+                                                   _lib.stream_ptr(self.device)), "ulysses push o")
+        img = self.out.clone()
+        txt = self.txt_out.clone() if self.Lt else out_txt.new_empty((self.B, 0, self.H, 128))
+        return img, txt
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            self.lib.hyb_peer_close(p)
+        for p in self._local:
+            self.lib.hyb_peer_free(p)
+        self._opened, self._local = [], []
+
+
+_EXCHANGES: dict = {}
+
+
+def peer_exchange(group, B, Ls, H, Lt, device):
+    """The cached PeerExchange of this geometry (created collectively on first use)."""
+    key = (id(group), dist.get_world_size(group), B, Ls, H, Lt, str(device))
+    ex = _EXCHANGES.get(key)
+    if ex is None:
+        ex = PeerExchange(group, B, Ls, H, Lt, device)
+        _EXCHANGES[key] = ex
+    return ex
+
+
+def release_peer_exchanges() -> None:
+    """Unmap and free every exchange's buffers (before destroying the process group)."""
+    for ex in _EXCHANGES.values():
+        ex.close()
+    _EXCHANGES.clear()
+
+
+def peer_exchange_enabled(sequence_lengths, heads) -> bool:
+    """Peer-memory exchange for equal per-rank lengths unless HYB_PEER_EXCHANGE=0."""
+    import os
+    if os.environ.get("HYB_PEER_EXCHANGE", "1") == "0":
+        return False
+    P = len(sequence_lengths)
+    return 1 < P <= 64 and len(set(sequence_lengths)) == 1 and heads % P == 0

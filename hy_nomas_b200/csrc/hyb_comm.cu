@@ -8,6 +8,8 @@
 //    (communications.py:191-198 after the head->sequence all_to_all).
 //  * LSE merge of partial attentions (dynamic_ring_attention.py:86-105):
 //    lse = max + log1p(exp(min - max)); out = out_a*exp(lse_a - lse) + out_b*exp(lse_b - lse).
+#include <cstring>
+
 #include "hyb_common.cuh"
 
 namespace hyb {
@@ -175,6 +177,168 @@ int grid_for(long long items, int threads) {
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+
+// ---------------------------------------------------------------------------------------
+// Peer-memory exchange (one process per GPU, buffers mapped into every rank with CUDA IPC).
+//
+// A push kernel writes this rank's slices straight into the destination ranks' buffers over
+// NVLink, then the grid meets the other ranks at a flag barrier: every block fences its
+// writes at system scope and counts itself in; the last block stores the next epoch into
+// slot `rank` of every rank's flag array (release, system scope) and waits until every rank
+// has stored that epoch into its own array (acquire loads, bounded: after kSpinLimitCycles
+// it reports HYB_DEV_TIMEOUT in the status word and returns).  Epochs live in device memory,
+// so a captured CUDA graph replays correctly.  Each rank visits its destinations starting
+// from its own successor, so at any moment the ranks write to different peers.
+// ---------------------------------------------------------------------------------------
+struct PeerSync {
+  int P, rank;
+  int* flags[kMaxRanks];   // every rank's flag array int32[P], as mapped in this process
+  unsigned* state;         // this rank: [0] blocks arrived in the current launch, [1] epoch
+  int* status;
+};
+
+__device__ __forceinline__ void st_release_sys(int* ptr, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+__device__ void grid_signal_and_wait(const PeerSync& s) {
+  __shared__ int is_last;
+  __shared__ int epoch;
+  __threadfence_system();  // every thread's peer writes, before the block counts itself in
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&s.state[0], 1u);
+    is_last = prev == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    s.state[0] = 0u;  // the next launch on this stream counts from zero
+    s.state[1] += 1u;
+    epoch = static_cast<int>(s.state[1]);
+  }
+  __syncthreads();
+  const int e = epoch;
+  const int t = threadIdx.x;
+  if (t < s.P) {
+    st_release_sys(s.flags[t] + s.rank, e);
+    const int* mine = s.flags[s.rank] + t;
+    const long long t0 = clock64();
+    while (ld_acquire_sys(mine) < e) {
+      if (clock64() - t0 > kSpinLimitCycles) {
+        if (s.status != nullptr) atomicOr(s.status, HYB_DEV_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+struct PushQkvParams {
+  int P, rank, B, Ls, Hp;
+  const __nv_bfloat16* src[3];
+  long long s_b[3], s_t[3], s_h[3];
+  __nv_bfloat16* recv[kMaxRanks];  // each rank's receive buffer [P(src), Ls, 3B, H/P, D]
+  PeerSync sync;
+};
+
+// One thread per 16-byte chunk: head slice of destination d of token t of q, k or v.
+__global__ void __launch_bounds__(256) push_qkv_kernel(const PushQkvParams p) {
+  const int nb = 3 * p.B;
+  const long long per_dst = static_cast<long long>(p.Ls) * nb * p.Hp * 16;
+  const long long chunks = per_dst * p.P;
+  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < chunks;
+       c += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(c / per_dst);
+    long long r = c - k * per_dst;
+    const int sub = static_cast<int>(r & 15);
+    r >>= 4;
+    const int hl = static_cast<int>(r % p.Hp);
+    r /= p.Hp;
+    const int bb = static_cast<int>(r % nb);
+    const int t = static_cast<int>(r / nb);
+    const int d = (p.rank + 1 + k) % p.P;
+    const int which = bb / p.B;
+    const int b = bb - which * p.B;
+    const int h = d * p.Hp + hl;
+    const uint4 v = *reinterpret_cast<const uint4*>(p.src[which] + b * p.s_b[which] + t * p.s_t[which] +
+                                                    h * p.s_h[which] + sub * 8);
+    __nv_bfloat16* dst = p.recv[d] + ((((static_cast<long long>(p.rank) * p.Ls + t) * nb + bb) * p.Hp + hl) * 128 + sub * 8);
+    *reinterpret_cast<uint4*>(dst) = v;
+  }
+  grid_signal_and_wait(p.sync);
+}
+
+struct PushOParams {
+  int P, rank, B, Ls, Lt, Hp, H;
+  const __nv_bfloat16* o_send;  // this rank's heads, [P(dst), Hp, Ls, B, D]
+  const __nv_bfloat16* txt;     // this rank's heads of the text rows [B, Lt, Hp, D] (strided)
+  long long t_b, t_t, t_h;
+  __nv_bfloat16* out[kMaxRanks];      // each rank's image output [B, Ls, H, D]
+  __nv_bfloat16* txt_out[kMaxRanks];  // each rank's text output [B, Lt, H, D]
+  PeerSync sync;
+};
+
+__global__ void __launch_bounds__(256) push_o_kernel(const PushOParams p) {
+  const long long img_per_dst = static_cast<long long>(p.Hp) * p.Ls * p.B * 16;
+  const long long txt_per_dst = static_cast<long long>(p.B) * p.Lt * p.Hp * 16;
+  const long long chunks = (img_per_dst + txt_per_dst) * p.P;
+  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < chunks;
+       c += static_cast<long long>(gridDim.x) * blockDim.x) {
+    if (c < img_per_dst * p.P) {
+      const int k = static_cast<int>(c / img_per_dst);
+      long long r = c - k * img_per_dst;
+      const int sub = static_cast<int>(r & 15);
+      r >>= 4;
+      const int b = static_cast<int>(r % p.B);
+      r /= p.B;
+      const int t = static_cast<int>(r % p.Ls);
+      const int hl = static_cast<int>(r / p.Ls);
+      const int d = (p.rank + 1 + k) % p.P;
+      const uint4 v = *reinterpret_cast<const uint4*>(
+          p.o_send + ((((static_cast<long long>(d) * p.Hp + hl) * p.Ls + t) * p.B + b) * 128 + sub * 8));
+      *reinterpret_cast<uint4*>(p.out[d] + (((static_cast<long long>(b) * p.Ls + t) * p.H + p.rank * p.Hp + hl) * 128 +
+                                            sub * 8)) = v;
+    } else {
+      const long long cc = c - img_per_dst * p.P;
+      const int k = static_cast<int>(cc / txt_per_dst);
+      long long r = cc - k * txt_per_dst;
+      const int sub = static_cast<int>(r & 15);
+      r >>= 4;
+      const int hl = static_cast<int>(r % p.Hp);
+      r /= p.Hp;
+      const int t = static_cast<int>(r % p.Lt);
+      const int b = static_cast<int>(r / p.Lt);
+      const int d = (p.rank + 1 + k) % p.P;
+      const uint4 v = *reinterpret_cast<const uint4*>(p.txt + b * p.t_b + t * p.t_t + hl * p.t_h + sub * 8);
+      *reinterpret_cast<uint4*>(p.txt_out[d] + (((static_cast<long long>(b) * p.Lt + t) * p.H + p.rank * p.Hp + hl) * 128 +
+                                                sub * 8)) = v;
+    }
+  }
+  grid_signal_and_wait(p.sync);
+}
+
+int peer_sync_of(const hyb_peer_sync* ps, int P, int rank, PeerSync* out) {
+  if (ps == nullptr || ps->state == nullptr) return fail(HYB_ERR_INVALID_ARG, "peer sync: null state");
+  out->P = P;
+  out->rank = rank;
+  for (int r = 0; r < P; ++r) {
+    if (ps->flags[r] == nullptr || (reinterpret_cast<uintptr_t>(ps->flags[r]) & 3u))
+      return fail(HYB_ERR_INVALID_ARG, "peer sync: flag array of rank %d missing or misaligned", r);
+    out->flags[r] = ps->flags[r];
+  }
+  out->state = ps->state;
+  out->status = ps->dev_status;
+  return HYB_OK;
+}
+
 }  // namespace
 }  // namespace hyb
 
@@ -280,6 +444,113 @@ extern "C" int hyb_lse_merge(int32_t rows, int32_t H, int32_t D, float* out_acc,
   MergeParams p{rows, H, D, out_acc, lse_acc, out_b, out_b_fmt, lse_b};
   const long long threads = static_cast<long long>(rows) * H * 32;
   lse_merge_kernel<<<grid_for(threads, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
+
+extern "C" int hyb_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle) {
+  if (ptr == nullptr || ipc_handle == nullptr || bytes <= 0) return fail(HYB_ERR_INVALID_ARG, "peer alloc: bad arguments");
+  *ptr = nullptr;
+  HYB_CUDA_TRY(cudaMalloc(ptr, static_cast<size_t>(bytes)));
+  HYB_CUDA_TRY(cudaMemset(*ptr, 0, static_cast<size_t>(bytes)));
+  cudaIpcMemHandle_t h;
+  HYB_CUDA_TRY(cudaIpcGetMemHandle(&h, *ptr));
+  memcpy(ipc_handle, &h, sizeof(h));
+  return HYB_OK;
+}
+
+extern "C" int hyb_peer_open(const void* ipc_handle, void** peer_ptr) {
+  if (ipc_handle == nullptr || peer_ptr == nullptr) return fail(HYB_ERR_INVALID_ARG, "peer open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  *peer_ptr = nullptr;
+  HYB_CUDA_TRY(cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return HYB_OK;
+}
+
+extern "C" int hyb_peer_close(void* peer_ptr) {
+  if (peer_ptr == nullptr) return HYB_OK;
+  HYB_CUDA_TRY(cudaIpcCloseMemHandle(peer_ptr));
+  return HYB_OK;
+}
+
+extern "C" int hyb_peer_free(void* ptr) {
+  if (ptr == nullptr) return HYB_OK;
+  HYB_CUDA_TRY(cudaFree(ptr));
+  return HYB_OK;
+}
+
+extern "C" int hyb_ulysses_push_qkv(int32_t P, int32_t rank, int32_t B, int32_t Ls, int32_t H, int32_t D,
+                                    const hyb_tensor4* q, const hyb_tensor4* k, const hyb_tensor4* v,
+                                    void* const* recv, const hyb_peer_sync* sync, void* stream) {
+  if (D != 128) return fail(HYB_ERR_UNSUPPORTED, "ulysses push: head_dim %d != 128", D);
+  if (P <= 1 || P > kMaxRanks || rank < 0 || rank >= P || B <= 0 || Ls < 0 || H <= 0 || H % P != 0 ||
+      q == nullptr || k == nullptr || v == nullptr || recv == nullptr)
+    return fail(HYB_ERR_INVALID_ARG, "ulysses push: bad sizes (2..%d ranks, heads divisible by ranks)", kMaxRanks);
+  PushQkvParams p;
+  p.P = P;
+  p.rank = rank;
+  p.B = B;
+  p.Ls = Ls;
+  p.Hp = H / P;
+  const hyb_tensor4* srcs[3] = {q, k, v};
+  for (int i = 0; i < 3; ++i) {
+    if (srcs[i]->fmt != HYB_FMT_BF16 || !al16(srcs[i]->data) || (srcs[i]->s_b % 8) || (srcs[i]->s_t % 8) ||
+        (srcs[i]->s_h % 8))
+      return fail(HYB_ERR_INVALID_ARG, "ulysses push: bf16 16-byte aligned q/k/v required");
+    p.src[i] = static_cast<const __nv_bfloat16*>(srcs[i]->data);
+    p.s_b[i] = srcs[i]->s_b;
+    p.s_t[i] = srcs[i]->s_t;
+    p.s_h[i] = srcs[i]->s_h;
+  }
+  for (int r = 0; r < P; ++r) {
+    if (recv[r] == nullptr || !al16(recv[r])) return fail(HYB_ERR_INVALID_ARG, "ulysses push: receive buffer %d", r);
+    p.recv[r] = static_cast<__nv_bfloat16*>(recv[r]);
+  }
+  int rc = peer_sync_of(sync, P, rank, &p.sync);
+  if (rc != HYB_OK) return rc;
+  const long long chunks = static_cast<long long>(P) * Ls * 3 * B * p.Hp * 16;
+  push_qkv_kernel<<<grid_for(chunks > 0 ? chunks : 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
+
+extern "C" int hyb_ulysses_push_o(int32_t P, int32_t rank, int32_t B, int32_t Ls, int32_t Lt, int32_t H, int32_t D,
+                                  const void* o_send, const hyb_tensor4* txt, void* const* out, void* const* txt_out,
+                                  const hyb_peer_sync* sync, void* stream) {
+  if (D != 128) return fail(HYB_ERR_UNSUPPORTED, "ulysses push o: head_dim %d != 128", D);
+  if (P <= 1 || P > kMaxRanks || rank < 0 || rank >= P || B <= 0 || Ls < 0 || Lt < 0 || H <= 0 || H % P != 0 ||
+      out == nullptr || (Lt > 0 && (txt == nullptr || txt_out == nullptr)) || (Ls > 0 && !al16(o_send)))
+    return fail(HYB_ERR_INVALID_ARG, "ulysses push o: bad sizes or buffers");
+  PushOParams p;
+  p.P = P;
+  p.rank = rank;
+  p.B = B;
+  p.Ls = Ls;
+  p.Lt = Lt;
+  p.Hp = H / P;
+  p.H = H;
+  p.o_send = static_cast<const __nv_bfloat16*>(o_send);
+  p.txt = nullptr;
+  p.t_b = p.t_t = p.t_h = 0;
+  if (Lt > 0) {
+    if (txt->fmt != HYB_FMT_BF16 || !al16(txt->data) || (txt->s_b % 8) || (txt->s_t % 8) || (txt->s_h % 8))
+      return fail(HYB_ERR_INVALID_ARG, "ulysses push o: bf16 16-byte aligned text rows required");
+    p.txt = static_cast<const __nv_bfloat16*>(txt->data);
+    p.t_b = txt->s_b;
+    p.t_t = txt->s_t;
+    p.t_h = txt->s_h;
+  }
+  for (int r = 0; r < P; ++r) {
+    if (out[r] == nullptr || !al16(out[r]) || (Lt > 0 && (txt_out[r] == nullptr || !al16(txt_out[r]))))
+      return fail(HYB_ERR_INVALID_ARG, "ulysses push o: output buffer %d", r);
+    p.out[r] = static_cast<__nv_bfloat16*>(out[r]);
+    p.txt_out[r] = Lt > 0 ? static_cast<__nv_bfloat16*>(txt_out[r]) : nullptr;
+  }
+  int rc = peer_sync_of(sync, P, rank, &p.sync);
+  if (rc != HYB_OK) return rc;
+  const long long chunks = static_cast<long long>(P) * (static_cast<long long>(p.Hp) * Ls * B + static_cast<long long>(B) * Lt * p.Hp) * 16;
+  push_o_kernel<<<grid_for(chunks > 0 ? chunks : 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }

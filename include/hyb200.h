@@ -225,6 +225,45 @@ int hyb_lse_merge(int32_t rows, int32_t H, int32_t D,
                   float* out_acc, float* lse_acc, const void* out_b, int32_t out_b_fmt,
                   const float* lse_b, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Peer-memory exchange for Ulysses sequence parallelism (one process per GPU).  Buffers are
+ * device allocations shared with CUDA IPC; every rank maps every other rank's buffers.  The
+ * push calls write this rank's slices straight into the destination ranks' buffers over
+ * NVLink and end with a device-side flag barrier (bounded: a rank that never arrives makes
+ * the others report HYB_DEV_TIMEOUT in dev_status after ~2 s instead of hanging).  They
+ * replace the all_to_all_single / all_gather collectives of all_to_all_qkv, all_to_all_4D
+ * and all_gather (hymm/distributed/communications.py:66-200, :270-280, :410-421) with one
+ * kernel each; the bytes land in the same layouts.
+ * ------------------------------------------------------------------------------------- */
+typedef struct hyb_peer_sync {
+  int32_t* flags[64];      /* every rank's flag array int32[P] (peer-shared), as mapped here */
+  uint32_t* state;         /* this rank's uint32[2] (blocks arrived, epoch), zero-initialised */
+  int32_t* dev_status;     /* int32 status word, OR-ed with HYB_DEV_TIMEOUT, or NULL */
+} hyb_peer_sync;
+
+/* cudaMalloc(bytes) zero-filled, and its IPC handle (64 bytes) for the other ranks. */
+int hyb_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+/* Map another rank's buffer (IPC handle from hyb_peer_alloc) into this process. */
+int hyb_peer_open(const void* ipc_handle, void** peer_ptr);
+int hyb_peer_close(void* peer_ptr);
+int hyb_peer_free(void* ptr);
+
+/* q, k, v bf16 [B, Ls, H, D] -> rank d's receive buffer recv[d] [P(src), Ls, 3B, H/P, D] at
+ * slot src = rank (heads [d*H/P, (d+1)*H/P)), then the barrier.  Same bytes as the receive
+ * side of all_to_all_qkv (communications.py:270-280) with equal sequence lengths. */
+int hyb_ulysses_push_qkv(int32_t P, int32_t rank, int32_t B, int32_t Ls, int32_t H, int32_t D,
+                         const hyb_tensor4* q, const hyb_tensor4* k, const hyb_tensor4* v,
+                         void* const* recv, const hyb_peer_sync* sync, void* stream);
+
+/* This rank's attention output for its H/P heads -> every rank's final layout: o_send
+ * [P(dst), H/P, Ls, B, D] (the layout the attention epilogue writes) to out[d] [B, Ls, H, D]
+ * at heads [rank*H/P, ...); text rows txt [B, Lt, H/P, D] to every txt_out[d] [B, Lt, H, D];
+ * then the barrier.  Replaces all_to_all_4D(scatter 1, gather 2) of the image rows and the
+ * head all_gather of the text rows (communications.py:260-267, :410-421; nomas_cpt.py:864-872). */
+int hyb_ulysses_push_o(int32_t P, int32_t rank, int32_t B, int32_t Ls, int32_t Lt, int32_t H, int32_t D,
+                       const void* o_send, const hyb_tensor4* txt, void* const* out, void* const* txt_out,
+                       const hyb_peer_sync* sync, void* stream);
+
 /* Ulysses send-side pack (sequence -> heads): q, k, v bf16 [B, Ls, H, D] -> send buffer
  * [P, Ls_max, nsrc*B, H/P, D] (the all_to_all_qkv layout, padding rows zeroed).
  * k == v == NULL packs q alone (nsrc = 1, the all_to_all_4D(scatter 2, gather 1) layout). */

@@ -58,11 +58,25 @@ def main():
             (img[2][:, sl].to(dev), txt[2].to(dev)), cache, cache_valid_len=Lh, attn_mode="flash3",
             text_mask=tmask, update_cache=True, cache_txt=True, cache_mask=mask, tokens_per_frame=T,
             seg_ar_attention_backend="b200", chunk_causal_frames=1)
+    # the same call over NCCL collectives (HYB_PEER_EXCHANGE=0) gives the same bytes; the cache
+    # write is repeated with identical values
+    from hy_nomas_b200 import communications as comm
+    os.environ["HYB_PEER_EXCHANGE"] = "0"
+    with torch.no_grad():
+        nccl_img, nccl_txt = hatt.causal_attention_with_cache_mp(
+            (img[0][:, sl].to(dev), txt[0].to(dev)), (img[1][:, sl].to(dev), txt[1].to(dev)),
+            (img[2][:, sl].to(dev), txt[2].to(dev)), cache, cache_valid_len=Lh, attn_mode="flash3",
+            text_mask=tmask, update_cache=True, cache_txt=True, cache_mask=mask, tokens_per_frame=T,
+            seg_ar_attention_backend="b200", chunk_causal_frames=1)
+    os.environ.pop("HYB_PEER_EXCHANGE", None)
+    peer_ok = torch.equal(nccl_img, out_img) and torch.equal(nccl_txt, out_txt)
+    if not peer_ok:
+        print("peer exchange differs from NCCL on rank", rank)
     gathered = [torch.empty_like(out_img) for _ in range(world)]
     dist.all_gather(gathered, out_img.contiguous())
     codes = [torch.empty_like(cache["k"]) for _ in range(world)]
     dist.all_gather(codes, cache["k"].contiguous())
-    ok = True
+    ok = peer_ok
     if rank == 0:
         ps.set_sequence_parallel_state(False)
         full_cache, full_mask = make_cache(list(range(H)))
@@ -109,6 +123,7 @@ def main():
     ok = bool(ok_t.item())
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.broadcast(flag, 0)
+    comm.release_peer_exchanges()
     ps.destroy_sequence_parallel_group()
     dist.destroy_process_group()
     if rank == 0 and flag.item() == 1:

@@ -50,6 +50,8 @@ int main(void) {
   F(hyb_attn_args, q) F(hyb_attn_args, kwords) F(hyb_attn_args, qbits) F(hyb_attn_args, oi_sseg)
   F(hyb_attn_args, lse) F(hyb_attn_args, dev_status) F(hyb_attn_args, kv_splits) F(hyb_attn_args, part_lse)
   F(hyb_attn_args, img_k_len) F(hyb_attn_args, k_pos1) F(hyb_attn_args, acc_o) F(hyb_attn_args, acc_mode)
+  printf("hyb_peer_sync %zu\n", sizeof(hyb_peer_sync));
+  F(hyb_peer_sync, state) F(hyb_peer_sync, dev_status)
   printf("hyb_workspace_layout %zu\n", sizeof(hyb_workspace_layout));
   F(hyb_workspace_layout, total) F(hyb_workspace_layout, kv_splits)
   return 0;
@@ -66,7 +68,8 @@ def test_ctypes_layouts_match_c(tmp_path):
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
     c = dict(line.rsplit(" ", 1) for line in out.strip().splitlines())
     types = {"hyb_tensor4": _lib.Tensor4, "hyb_cached_attn_args": _lib.CachedAttnArgs,
-             "hyb_attn_args": _lib.AttnArgs, "hyb_workspace_layout": _lib.WorkspaceLayout}
+             "hyb_attn_args": _lib.AttnArgs, "hyb_workspace_layout": _lib.WorkspaceLayout,
+             "hyb_peer_sync": _lib.PeerSync}
     for key, val in c.items():
         if "." in key:
             t, m = key.split(".")
