@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ring-schedule", default="allgather", choices=["allgather", "ring"],
+                    help="ring workload: every block to every rank over peer memory, or neighbour passing")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager calls instead of replaying one captured CUDA graph of the call")
     ap.add_argument("--workload", default="config2", choices=["config2", "config4", "ring", "rollout"],
@@ -428,12 +430,14 @@ def run_ring(args):
     torch.cuda.empty_cache()
     flops_total = attention_flops(0, L, 0, H_TOTAL, D, False, T)
     group = None
-    state = ring.ring_plan_state(q, seq_len=L, world=world, rank=rank, tokens_per_frame=T)
+    sched = args.ring_schedule
+    state = ring.ring_plan_state(q, seq_len=L, world=world, rank=rank, tokens_per_frame=T, schedule=sched,
+                                 group=group)
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream(device)
 
     def step(q_, k_, v_):
-        return ring.ring_attention(q_, k_, v_, group, seq_len=L, tokens_per_frame=T, out=out)
+        return ring.ring_attention(q_, k_, v_, group, seq_len=L, tokens_per_frame=T, out=out, schedule=sched)
 
     for _ in range(args.warmup):
         step(q, k, v)
@@ -483,7 +487,7 @@ def run_ring(args):
     host_in = [t.cpu().pin_memory() for t in (q, k, v)]
 
     def ring_call(q_, k_, v_):   # a fresh output per eager call: its read-back overlaps the next
-        return (ring.ring_attention(q_, k_, v_, group, seq_len=L, tokens_per_frame=T),)
+        return (ring.ring_attention(q_, k_, v_, group, seq_len=L, tokens_per_frame=T, schedule=sched),)
 
     from hy_nomas_b200.graphs import GraphedCall
     rcall = ring_call if args.no_graph else GraphedCall(ring_call, device)
@@ -496,6 +500,7 @@ def run_ring(args):
     if not args.no_graph:
         rcall.release()
     torch.cuda.synchronize(device)
+    ring.release_ring_states()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -510,6 +515,9 @@ def run_ring(args):
         "config": {"workload": "config 3: ring SP, 21 frames x 1560 tokens, frame-causal", "heads": H_TOTAL,
                    "head_dim": D, "seq_len": L, "tokens_per_frame": T, "layout": "zig-zag (2N chunks)",
                    "parallelism": f"ring_sp{world}" if world > 1 else "single",
+                   "schedule": (f"{sched}: " + ("every e4m3 block pushed to every rank over peer memory, one "
+                                                "attention launch" if sched == "allgather" else
+                                                "neighbour passing over NCCL send/recv, one launch per step")),
                    "timed_call": "eager" if args.no_graph else "CUDA graph replay of one ring call",
                    "kv_block": "fp8_e4m3 codes + fp32 per-(token, head) scales, quantised each step",
                    "l2": "inputs larger than L2 (201 MB bf16 per tensor over the job)",
@@ -519,7 +527,7 @@ def run_ring(args):
                 "ms_per_step": round(ems, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_bf16, "unit": "TFLOP/s",
                      "frac": round(achieved / peak_bf16, 4), "traffic": None,
-                     "kernel": "attn_fwd2_kernel ring steps (tcgen05 kind::f16, bf16 operands)",
+                     "kernel": "attn_fwd2_kernel (tcgen05 kind::f16, bf16 operands)",
                      "kernel_ms_per_step": round(kern_ms, 4), "kernel_ms_max_rank": round(kern_ms_max, 4),
                      "peak_source": f"{peak_src} bf16 dense (cuBLAS)",
                      "algorithmic_unit": "4*H*D FLOP per visible (query, key) pair"},

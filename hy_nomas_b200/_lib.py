@@ -115,6 +115,11 @@ SIGNATURES = {
     "hyb_fill_key_bits": (c_i32, [c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "hyb_attn_work_plan": (c_i32, [ctypes.POINTER(AttnArgs), c_i32, ctypes.POINTER(c_i32), c_i32]),
     "hyb_peer_alloc": (c_i32, [c_i64, ctypes.POINTER(c_ptr), c_ptr]),
+    "hyb_peer_push_bytes": (c_i32, [c_i32, c_i32, c_ptr, c_i64, ctypes.POINTER(c_ptr), ctypes.POINTER(PeerSync),
+                                    c_ptr]),
+    "hyb_ring_gather_stage": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(c_ptr), c_i32,
+                                      ctypes.POINTER(c_i32), ctypes.POINTER(c_i32), ctypes.POINTER(c_i32),
+                                      c_ptr, c_ptr, c_ptr]),
     "hyb_peer_open": (c_i32, [c_ptr, ctypes.POINTER(c_ptr)]),
     "hyb_peer_close": (c_i32, [c_ptr]),
     "hyb_peer_free": (c_i32, [c_ptr]),

@@ -234,6 +234,67 @@ def _bf16_tensor(ptr: int, shape, device) -> torch.Tensor:
     return torch.as_tensor(_DeviceArray(ptr, shape, "<i2"), device=device).view(torch.bfloat16)
 
 
+class PeerBuffers:
+    """Device buffers every rank of ``group`` maps with CUDA IPC, plus the flag arrays of the
+    device barrier that ends each push kernel.  ``ptrs[i][r]`` is buffer i of rank r as mapped
+    in this process; ``local[i]`` is this rank's own."""
+
+    def __init__(self, group, sizes, device):
+        self.group = group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        self.lib = lib = _lib.load()
+        sizes = [max(int(n), 256) for n in sizes] + [256]   # last: the barrier flags int32[<= 64]
+        self.sizes = sizes
+        self.local = []
+        self._opened = []
+        handles = bytearray()
+        with torch.cuda.device(self.device):
+            for nbytes in sizes:
+                ptr = ctypes.c_void_p()
+                h = (ctypes.c_uint8 * 64)()
+                _lib.check(lib.hyb_peer_alloc(nbytes, ctypes.byref(ptr), h), "peer alloc")
+                self.local.append(ptr.value)
+                handles += bytes(h)
+            mine = torch.tensor(list(handles), dtype=torch.uint8, device=self.device)
+            every = torch.empty((self.P, mine.numel()), dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            every = every.cpu().numpy()
+            self.ptrs = [[0] * self.P for _ in sizes]
+            for rr in range(self.P):
+                for i in range(len(sizes)):
+                    if rr == self.rank:
+                        self.ptrs[i][rr] = self.local[i]
+                        continue
+                    peer = ctypes.c_void_p()
+                    _lib.check(lib.hyb_peer_open(bytes(every[rr, 64 * i:64 * (i + 1)]), ctypes.byref(peer)),
+                               "peer open")
+                    self.ptrs[i][rr] = peer.value
+                    self._opened.append(peer.value)
+        self.state = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.sync = _lib.PeerSync()
+        for rr in range(self.P):
+            self.sync.flags[rr] = self.ptrs[-1][rr]
+        self.sync.state = self.state.data_ptr()
+        self.sync.dev_status = _lib.device_status(self.device).data_ptr()
+        # every rank has mapped every buffer before anyone writes into them
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+
+    def table(self, i, offset: int = 0):
+        """ctypes array of buffer i of every rank (+ a byte offset)."""
+        return (ctypes.c_void_p * self.P)(*[p + offset for p in self.ptrs[i]])
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            self.lib.hyb_peer_close(p)
+        for p in self.local:
+            self.lib.hyb_peer_free(p)
+        self._opened, self.local = [], []
+
+
 class PeerExchange:
     """Ulysses exchange of one geometry (group, batch B, per-rank length Ls, heads H, text
     length Lt) over buffers that every rank maps with CUDA IPC.  ``push_qkv`` writes this rank's
@@ -244,60 +305,25 @@ class PeerExchange:
     device-side barrier.  Equal sequence lengths on every rank."""
 
     def __init__(self, group, B: int, Ls: int, H: int, Lt: int, device):
-        self.group = group
-        self.P = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        P = dist.get_world_size(group)
+        self.P, self.rank = P, dist.get_rank(group)
         self.B, self.Ls, self.H, self.Lt = B, Ls, H, Lt
-        self.Hp = H // self.P
+        self.Hp = H // P
         self.device = torch.device(device)
-        self.lib = lib = _lib.load()
-        P, Hp, D = self.P, self.Hp, 128
-        sizes = [P * Ls * 3 * B * Hp * D * 2, P * Ls * 3 * B * Hp * D * 2, B * Ls * H * D * 2,
-                 max(B * Lt * H * D * 2, 256), 256]
-        self._local = []
-        handles = bytearray()
-        with torch.cuda.device(self.device):
-            for nbytes in sizes:
-                ptr = ctypes.c_void_p()
-                h = (ctypes.c_uint8 * 64)()
-                _lib.check(lib.hyb_peer_alloc(max(int(nbytes), 256), ctypes.byref(ptr), h), "peer alloc")
-                self._local.append(ptr.value)
-                handles += bytes(h)
-            mine = torch.tensor(list(handles), dtype=torch.uint8, device=self.device)
-            every = torch.empty((P, mine.numel()), dtype=torch.uint8, device=self.device)
-            dist.all_gather_into_tensor(every, mine, group=group)
-            every = every.cpu().numpy()
-            self._opened = []
-            ptrs = [[0] * P for _ in sizes]
-            for rr in range(P):
-                for i in range(len(sizes)):
-                    if rr == self.rank:
-                        ptrs[i][rr] = self._local[i]
-                        continue
-                    peer = ctypes.c_void_p()
-                    _lib.check(lib.hyb_peer_open(bytes(every[rr, 64 * i:64 * (i + 1)]), ctypes.byref(peer)),
-                               "peer open")
-                    ptrs[i][rr] = peer.value
-                    self._opened.append(peer.value)
+        self.lib = _lib.load()
+        Hp, D = self.Hp, 128
+        recv_bytes = P * Ls * 3 * B * Hp * D * 2
+        self.buf = PeerBuffers(group, [recv_bytes, recv_bytes, B * Ls * H * D * 2, B * Lt * H * D * 2], device)
         recv_shape = (P, Ls, 3 * B, Hp, D)
-        self.recv = [_bf16_tensor(self._local[0], recv_shape, self.device),
-                     _bf16_tensor(self._local[1], recv_shape, self.device)]
-        self.out = _bf16_tensor(self._local[2], (B, Ls, H, D), self.device)
-        self.txt_out = _bf16_tensor(self._local[3], (B, Lt, H, D), self.device) if Lt else None
-        self.state = torch.zeros(2, dtype=torch.int32, device=self.device)
-        self.sync = _lib.PeerSync()
-        for rr in range(P):
-            self.sync.flags[rr] = ptrs[4][rr]
-        self.sync.state = self.state.data_ptr()
-        self.sync.dev_status = _lib.device_status(self.device).data_ptr()
-        vp = ctypes.c_void_p * P
-        self._recv_tab = [vp(*ptrs[0]), vp(*ptrs[1])]
-        self._out_tab = vp(*ptrs[2])
-        self._txt_tab = vp(*ptrs[3])
+        self.recv = [_bf16_tensor(self.buf.local[0], recv_shape, self.device),
+                     _bf16_tensor(self.buf.local[1], recv_shape, self.device)]
+        self.out = _bf16_tensor(self.buf.local[2], (B, Ls, H, D), self.device)
+        self.txt_out = _bf16_tensor(self.buf.local[3], (B, Lt, H, D), self.device) if Lt else None
+        self.sync = self.buf.sync
+        self._recv_tab = [self.buf.table(0), self.buf.table(1)]
+        self._out_tab = self.buf.table(2)
+        self._txt_tab = self.buf.table(3)
         self.calls = 0
-        # every rank has mapped every buffer before anyone writes into them
-        torch.cuda.synchronize(self.device)
-        dist.barrier(group=group)
 
     def push_qkv(self, q, k, v):
         """Sequence-sharded q, k, v [B, Ls, H, D] -> head-sharded [B, P*Ls, H/P, D] views."""
@@ -327,12 +353,7 @@ class PeerExchange:
         return img, txt
 
     def close(self) -> None:
-        torch.cuda.synchronize(self.device)
-        for p in self._opened:
-            self.lib.hyb_peer_close(p)
-        for p in self._local:
-            self.lib.hyb_peer_free(p)
-        self._opened, self._local = [], []
+        self.buf.close()
 
 
 _EXCHANGES: dict = {}

@@ -818,7 +818,69 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
   }
 }
 
-// Visibility bitmap with the first Lk keys of every batch row set (ring blocks: every key
+// Sequence-parallel K/V blocks -> one head-major bf16 K/V of the whole sequence.  Position
+// `pos` lies in chunk c ([bounds[c], bounds[c+1])), held by rank owner[c] at block row
+// row0[c] + (pos - bounds[c]).  A block is [K codes | V codes | K scales | V scales] for Lmax
+// rows of H heads (the ring message layout); decode as load_row8.
+constexpr int kMaxGatherChunks = 128;
+struct GatherParams {
+  int L, H, Lmax, fmt, nchunks;
+  const uint8_t* blocks[64];
+  int bounds[kMaxGatherChunks + 1];
+  int owner[kMaxGatherChunks];
+  int row0[kMaxGatherChunks];
+  __nv_bfloat16* out_k;
+  __nv_bfloat16* out_v;
+};
+
+__global__ void __launch_bounds__(256) gather_stage_kernel(const GatherParams p) {
+  const long long chunks = static_cast<long long>(p.H) * p.L * 16;
+  const long long codes = static_cast<long long>(p.Lmax) * p.H * kHD;
+  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < chunks;
+       c += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int sub = static_cast<int>(c & 15);
+    const long long r = c >> 4;
+    const int pos = static_cast<int>(r % p.L);
+    const int h = static_cast<int>(r / p.L);
+    int lo = 0, hi = p.nchunks - 1;  // chunk containing pos
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.bounds[mid] <= pos) {
+        lo = mid;
+      } else {
+        hi = mid - 1;
+      }
+    }
+    const uint8_t* blk = p.blocks[p.owner[lo]];
+    const int row = p.row0[lo] + (pos - p.bounds[lo]);
+    const long long out_off = (static_cast<long long>(h) * p.L + pos) * kHD + sub * 8;
+#pragma unroll
+    for (int o = 0; o < 2; ++o) {
+      StageSeg sg;
+      sg.rows = nullptr;
+      sg.data = blk + o * codes;
+      sg.scale = reinterpret_cast<const float*>(blk + 2 * codes) + o * static_cast<long long>(p.Lmax) * p.H;
+      sg.s_b = 0;
+      sg.s_t = static_cast<long long>(p.H) * kHD;
+      sg.s_h = kHD;
+      sg.c_b = 0;
+      sg.c_t = p.H;
+      sg.c_h = 1;
+      sg.fmt = p.fmt;
+      sg.len = p.Lmax;
+      sg.bcast = 0;
+      float v[8];
+      load_row8(sg, 0, row, h, sub, v);
+      uint4 packed;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&packed);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      *reinterpret_cast<uint4*>((o == 0 ? p.out_k : p.out_v) + out_off) = packed;
+    }
+  }
+}
+
+// Visibility bitmap with the first Lk keys of every batch row set// Visibility bitmap with the first Lk keys of every batch row set (ring blocks: every key
 // of the block is valid; the block-causal rule is applied by the attention kernel).
 __global__ void __launch_bounds__(256) key_bits_kernel(int B, int Lk, int kwords, uint32_t* bits) {
   const long long n = static_cast<long long>(B) * kwords;
@@ -1373,6 +1435,43 @@ extern "C" int hyb_stage_head_major(int32_t B, int32_t L, int32_t H, int32_t D, 
   sp.out[1] = dst_v;
   stage_kernel<<<grid_for(static_cast<long long>(B) * H * L * 16, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       sp);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
+
+extern "C" int hyb_ring_gather_stage(int32_t P, int32_t fmt, int32_t L, int32_t H, int32_t D, int32_t Lmax,
+                                     const void* const* blocks, int32_t nchunks, const int32_t* bounds,
+                                     const int32_t* owner, const int32_t* row0, void* out_k, void* out_v,
+                                     void* stream) {
+  if (D != kHD) return fail(HYB_ERR_UNSUPPORTED, "gather stage: head_dim %d != 128", D);
+  if (fmt != HYB_FMT_E4M3 && fmt != HYB_FMT_INT8) return fail(HYB_ERR_UNSUPPORTED, "gather stage: format %d", fmt);
+  if (P <= 0 || P > 64 || L < 0 || H <= 0 || Lmax <= 0 || nchunks <= 0 || nchunks > kMaxGatherChunks ||
+      blocks == nullptr || bounds == nullptr || owner == nullptr || row0 == nullptr || !al16(out_k) || !al16(out_v))
+    return fail(HYB_ERR_INVALID_ARG, "gather stage: bad arguments (at most %d chunks)", kMaxGatherChunks);
+  GatherParams p;
+  p.L = L;
+  p.H = H;
+  p.Lmax = Lmax;
+  p.fmt = fmt;
+  p.nchunks = nchunks;
+  for (int r = 0; r < P; ++r) {
+    if (blocks[r] == nullptr || (reinterpret_cast<uintptr_t>(blocks[r]) & 15u))
+      return fail(HYB_ERR_INVALID_ARG, "gather stage: block %d", r);
+    p.blocks[r] = static_cast<const uint8_t*>(blocks[r]);
+  }
+  if (bounds[0] != 0 || bounds[nchunks] != L) return fail(HYB_ERR_INVALID_ARG, "gather stage: chunks must cover [0, L)");
+  for (int c = 0; c < nchunks; ++c) {
+    if (bounds[c + 1] < bounds[c] || owner[c] < 0 || owner[c] >= P || row0[c] < 0 ||
+        row0[c] + (bounds[c + 1] - bounds[c]) > Lmax)
+      return fail(HYB_ERR_INVALID_ARG, "gather stage: chunk %d out of range", c);
+    p.owner[c] = owner[c];
+    p.row0[c] = row0[c];
+  }
+  for (int c = 0; c <= nchunks; ++c) p.bounds[c] = bounds[c];
+  p.out_k = static_cast<__nv_bfloat16*>(out_k);
+  p.out_v = static_cast<__nv_bfloat16*>(out_v);
+  if (L == 0) return HYB_OK;
+  gather_stage_kernel<<<grid_for(static_cast<long long>(H) * L * 16, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }

@@ -325,6 +325,29 @@ __global__ void __launch_bounds__(256) push_o_kernel(const PushOParams p) {
   grid_signal_and_wait(p.sync);
 }
 
+struct PushBytesParams {
+  int P, rank;
+  long long chunks16;           // 16-byte chunks per destination
+  const uint4* src;
+  uint4* dst[kMaxRanks];        // where this rank's bytes go in each rank's buffer
+  PeerSync sync;
+};
+
+// The same bytes to every rank (an all-gather contribution); destinations whose pointer is the
+// source itself are skipped.
+__global__ void __launch_bounds__(256) push_bytes_kernel(const PushBytesParams p) {
+  const long long total = p.chunks16 * p.P;
+  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < total;
+       c += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(c / p.chunks16);
+    const long long i = c - k * p.chunks16;
+    const int d = (p.rank + 1 + k) % p.P;
+    if (p.dst[d] == p.src) continue;
+    p.dst[d][i] = p.src[i];
+  }
+  grid_signal_and_wait(p.sync);
+}
+
 int peer_sync_of(const hyb_peer_sync* ps, int P, int rank, PeerSync* out) {
   if (ps == nullptr || ps->state == nullptr) return fail(HYB_ERR_INVALID_ARG, "peer sync: null state");
   out->P = P;
@@ -551,6 +574,28 @@ extern "C" int hyb_ulysses_push_o(int32_t P, int32_t rank, int32_t B, int32_t Ls
   if (rc != HYB_OK) return rc;
   const long long chunks = static_cast<long long>(P) * (static_cast<long long>(p.Hp) * Ls * B + static_cast<long long>(B) * Lt * p.Hp) * 16;
   push_o_kernel<<<grid_for(chunks > 0 ? chunks : 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
+
+extern "C" int hyb_peer_push_bytes(int32_t P, int32_t rank, const void* src, int64_t bytes, void* const* dst,
+                                   const hyb_peer_sync* sync, void* stream) {
+  if (P <= 1 || P > kMaxRanks || rank < 0 || rank >= P || bytes < 0 || (bytes % 16) != 0 || dst == nullptr ||
+      (bytes > 0 && !al16(src)))
+    return fail(HYB_ERR_INVALID_ARG, "peer push: bad arguments (16-byte multiples, 2..%d ranks)", kMaxRanks);
+  PushBytesParams p;
+  p.P = P;
+  p.rank = rank;
+  p.chunks16 = bytes / 16;
+  p.src = static_cast<const uint4*>(src);
+  for (int r = 0; r < P; ++r) {
+    if (dst[r] == nullptr || !al16(dst[r])) return fail(HYB_ERR_INVALID_ARG, "peer push: destination %d", r);
+    p.dst[r] = static_cast<uint4*>(dst[r]);
+  }
+  int rc = peer_sync_of(sync, P, rank, &p.sync);
+  if (rc != HYB_OK) return rc;
+  const long long total = p.chunks16 * P;
+  push_bytes_kernel<<<grid_for(total > 0 ? total : 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }

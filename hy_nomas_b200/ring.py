@@ -84,6 +84,18 @@ class RingPlan:
         pieces.sort(key=lambda t: t[0])
         return torch.cat([t for _, t in pieces], dim)
 
+    def gather_chunks(self):
+        """(position, length, owner rank, row in the owner's block) of every chunk, in position
+        order: the table that lays the ranks' blocks out as the whole sequence."""
+        chunks = []
+        for r in range(self.world):
+            off = 0
+            for pos, n in self.segments[r]:
+                if n > 0:
+                    chunks.append((pos, n, r, off))
+                off += n
+        return sorted(chunks)
+
     def visible(self, q_rank: int, k_rank: int, group_tokens: int) -> bool:
         """False when every key of k_rank's shard is in a later causal group than every query of
         q_rank's shard (the step is skipped)."""
@@ -100,12 +112,14 @@ class KVBlock:
     """Quantised K/V of one shard in a single contiguous byte buffer (one P2P message), sized
     for ``L`` tokens; a shard of fewer tokens uses the leading rows."""
 
-    def __init__(self, L: int, H: int, device, fmt: str = "fp8_e4m3"):
+    def __init__(self, L: int, H: int, device, fmt: str = "fp8_e4m3", buf: torch.Tensor | None = None):
         self.L, self.H, self.fmt = L, H, fmt
         self.code_fmt, dtype = _FMT[fmt]
         n_codes = L * H * _D
         n_scale = L * H * 4
-        self.buf = torch.empty(2 * (n_codes + n_scale), dtype=torch.uint8, device=device)
+        if buf is not None and buf.numel() < 2 * (n_codes + n_scale):
+            raise ValueError("KV block buffer too small")
+        self.buf = buf if buf is not None else torch.empty(2 * (n_codes + n_scale), dtype=torch.uint8, device=device)
         b = self.buf
         self.k = b[:n_codes].view(dtype).view(1, L, H, _D)
         self.v = b[n_codes:2 * n_codes].view(dtype).view(1, L, H, _D)
@@ -272,42 +286,208 @@ class RingAttention:
         return out
 
 
+def _u8_tensor(ptr: int, nbytes: int, device) -> torch.Tensor:
+    from .communications import _DeviceArray
+    return torch.as_tensor(_DeviceArray(ptr, (nbytes,), "|u1"), device=device)
+
+
+class GatherAttention:
+    """The all-gather schedule of ring attention for a switched fabric.  Every rank quantises
+    its K/V into its slot of a block buffer that every rank maps (CUDA IPC), pushes the block
+    to every other rank in one kernel (each rank starting from a different peer, so the
+    NVSwitch ports carry P - 1 streams at once) and meets them at a device barrier; one
+    kernel then decodes all P blocks into a head-major bf16 K/V of the whole sequence in
+    position order, and one attention launch covers this rank's query chunks against it.
+    Moves the same bytes per rank as the neighbour ring (P - 1 blocks in, P - 1 out) without
+    P attention launches and partial merges.  ``emulate=True`` runs every rank in one process
+    over a shared local buffer (tests on one GPU)."""
+
+    def __init__(self, plan: RingPlan, rank: int, heads: int, device, *, tokens_per_frame: int,
+                 causal_frames: int = 1, kv_format: str = "fp8_e4m3", softmax_scale: float | None = None,
+                 group=None, shared=None):
+        self.plan, self.rank, self.H, self.device = plan, rank, heads, torch.device(device)
+        self.G = int(causal_frames) * int(tokens_per_frame)
+        self.scale = float(softmax_scale) if softmax_scale else 0.0
+        self.lib = lib = _lib.load()
+        P, H, dev, L = plan.world, heads, self.device, plan.seq_len
+        Lmax = plan.max_length()
+        self.Lmax = Lmax
+        self.code_fmt = _FMT[kv_format][0]
+        self.block_bytes = ((2 * (Lmax * H * _D + Lmax * H * 4)) + 15) // 16 * 16
+        self.peers = None
+        if shared is not None:                   # emulation: one buffer holds every rank's block
+            base = shared.data_ptr()
+            self._keep = shared
+        elif P > 1:
+            from .communications import PeerBuffers
+            self.peers = PeerBuffers(group, [P * self.block_bytes], dev)
+            base = self.peers.local[0]
+            self._push_dst = self.peers.table(0, offset=rank * self.block_bytes)
+        else:
+            self._keep = torch.empty(self.block_bytes, dtype=torch.uint8, device=dev)
+            base = self._keep.data_ptr()
+        self.base = base
+        self.slots = [KVBlock(Lmax, H, dev, kv_format, buf=_u8_tensor(base + r * self.block_bytes, self.block_bytes, dev))
+                      for r in range(P)]
+        chunks = plan.gather_chunks()
+        self.nchunks = len(chunks)
+        self.bounds = (ctypes.c_int32 * (self.nchunks + 1))(*([c[0] for c in chunks] + [L]))
+        self.owner = (ctypes.c_int32 * self.nchunks)(*[c[2] for c in chunks])
+        self.row0 = (ctypes.c_int32 * self.nchunks)(*[c[3] for c in chunks])
+        self.block_tab = (ctypes.c_void_p * P)(*[base + r * self.block_bytes for r in range(P)])
+        self.kv = torch.empty((2, H * max(L, 1) * _D), dtype=torch.bfloat16, device=dev)
+        Ls = plan.length(rank)
+        self.Ls = Ls
+        self.qh = torch.empty((H * max(Ls, 1) * _D,), dtype=torch.bfloat16, device=dev)
+        self.kwords = ((L + 127) // 128) * 4
+        self.bits = torch.empty(max(self.kwords, 4), dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(lib.hyb_fill_key_bits(1, L, self.kwords, self.bits.data_ptr(), _lib.stream_ptr(dev)), "key bits")
+            lay = _lib.WorkspaceLayout()
+            _lib.check(lib.hyb_cached_attention_workspace_layout(1, H, _D, L - Ls, max(Ls, 1), 0, 0, ctypes.byref(lay)),
+                       "gather layout")
+        self.kv_splits = max(1, lay.kv_splits)
+        self.part_o = torch.empty((self.kv_splits * H * max(Ls, 1) * _D,), dtype=torch.float32, device=dev) \
+            if self.kv_splits > 1 else None
+        self.part_lse = torch.empty((self.kv_splits * H * max(Ls, 1),), dtype=torch.float32, device=dev) \
+            if self.kv_splits > 1 else None
+        self.status = _lib.device_status(dev)
+        self.launches = 0
+        self.event_log = None
+
+    def fill_own(self, k, v) -> None:
+        self.slots[self.rank].fill(k, v)
+
+    def exchange(self, stream: int) -> None:
+        if self.peers is not None:
+            _lib.check(self.lib.hyb_peer_push_bytes(self.plan.world, self.rank, self.slots[self.rank].buf.data_ptr(),
+                                                    self.block_bytes, self._push_dst, ctypes.byref(self.peers.sync),
+                                                    stream), "ring block push")
+            self.launches += 1
+
+    def attend(self, q, out, lse, stream: int) -> None:
+        plan, H, Ls, L = self.plan, self.H, self.Ls, self.plan.seq_len
+        qv = _lib.bf16_view(q)
+        _lib.check(self.lib.hyb_stage_head_major(1, Ls, H, _D, ctypes.byref(qv), None, self.qh.data_ptr(), None,
+                                                 stream), "ring stage q")
+        kv_k, kv_v = self.kv[0].data_ptr(), self.kv[1].data_ptr()
+        _lib.check(self.lib.hyb_ring_gather_stage(plan.world, self.code_fmt, L, H, _D, self.Lmax, self.block_tab,
+                                                  self.nchunks, self.bounds, self.owner, self.row0, kv_k, kv_v,
+                                                  stream), "ring gather stage")
+        a = _lib.AttnArgs()
+        a.abi_version = _lib.HYB_ABI_VERSION
+        a.B, a.H, a.D, a.Lq, a.Lk = 1, H, _D, Ls, L
+        a.hist_len, a.img_len, a.img_k_len = 0, Ls, L
+        a.group_tokens = self.G
+        a.softmax_scale = self.scale
+        a.q_seg, a.q_pos0, a.q_pos1 = plan.positions(self.rank)
+        a.k_seg, a.k_pos0, a.k_pos1 = 0, 0, 0
+        a.q, a.k, a.v = self.qh.data_ptr(), kv_k, kv_v
+        a.kbits, a.kwords = self.bits.data_ptr(), self.kwords
+        a.qbits, a.qwords = None, 0
+        a.out_img = out.data_ptr()
+        a.oi_sb, a.oi_st, a.oi_sh = out.stride(0), out.stride(1), out.stride(2)
+        a.oi_seg, a.oi_sseg = Ls, 0
+        a.lse = lse.data_ptr() if lse is not None else None
+        a.dev_status = self.status.data_ptr()
+        a.kv_splits = self.kv_splits
+        if self.kv_splits > 1:
+            a.part_o, a.part_lse = self.part_o.data_ptr(), self.part_lse.data_ptr()
+        if self.event_log is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record(torch.cuda.current_stream(self.device))
+        _lib.check(self.lib.hyb_attn_fwd(ctypes.byref(a), stream), "ring attention")
+        if self.event_log is not None:
+            ev[1].record(torch.cuda.current_stream(self.device))
+            self.event_log.append(ev)
+        self.launches += 3
+
+    def __call__(self, q, k, v, group=None, *, out=None, lse=None):
+        H, Ls, dev = self.H, self.Ls, self.device
+        if q.shape != (1, Ls, H, _D) or k.shape != q.shape or v.shape != q.shape:
+            raise ValueError(f"ring shard must be [1, {Ls}, {H}, {_D}] on rank {self.rank}")
+        if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+            raise ValueError("ring attention takes bf16 q/k/v")
+        out = out if out is not None else torch.empty_like(q)
+        self.launches = 0
+        if Ls == 0:
+            return out
+        with torch.cuda.device(dev):
+            cs = _lib.stream_ptr(dev)
+            self.fill_own(k, v)
+            self.launches += 1
+            self.exchange(cs)
+            self.attend(q, out, lse, cs)
+        return out
+
+    def close(self) -> None:
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
+
+
 _PLANS: dict = {}
+
+
+SCHEDULES = ("allgather", "ring")
 
 
 def ring_attention(q, k, v, group=None, *, seq_len: int, tokens_per_frame: int, causal_frames: int = 1,
                    kv_format: str = "fp8_e4m3", layout: str = "zigzag", softmax_scale: float | None = None,
-                   out=None, lse=None):
+                   schedule: str = "allgather", out=None, lse=None):
     """Frame-causal self-attention of a sequence of ``seq_len`` tokens sharded over the ranks
     of ``group`` by ``RingPlan(seq_len, P, layout)``.  q/k/v: this rank's shard bf16
-    [1, Ls, H, 128].  Returns this rank's output [1, Ls, H, 128] bf16."""
+    [1, Ls, H, 128].  Returns this rank's output [1, Ls, H, 128] bf16.  ``schedule``:
+    "allgather" (every block to every rank over peer memory, one attention launch) or "ring"
+    (neighbour passing with NCCL send/recv, one launch per step)."""
     P = dist.get_world_size(group) if dist.is_initialized() else 1
     r = dist.get_rank(group) if dist.is_initialized() else 0
     ra = ring_plan_state(q, seq_len=seq_len, world=P, rank=r, tokens_per_frame=tokens_per_frame,
                          causal_frames=causal_frames, kv_format=kv_format, layout=layout,
-                         softmax_scale=softmax_scale)
+                         softmax_scale=softmax_scale, schedule=schedule, group=group)
     return ra(q, k, v, group, out=out, lse=lse)
 
 
 def ring_plan_state(q, *, seq_len, world, rank, tokens_per_frame, causal_frames=1, kv_format="fp8_e4m3",
-                    layout="zigzag", softmax_scale=None) -> RingAttention:
-    """The cached ``RingAttention`` of this geometry (buffers are reused across calls)."""
+                    layout="zigzag", softmax_scale=None, schedule="allgather", group=None):
+    """The cached ``GatherAttention`` / ``RingAttention`` of this geometry (buffers are reused
+    across calls; creating a gather schedule is collective over ``group``)."""
+    if schedule not in SCHEDULES:
+        raise ValueError(f"unknown ring schedule {schedule!r}")
     P, r = world, rank
-    key = (seq_len, P, layout, r, q.shape[2], q.device, tokens_per_frame, causal_frames, kv_format, softmax_scale)
+    key = (seq_len, P, layout, r, q.shape[2], q.device, tokens_per_frame, causal_frames, kv_format, softmax_scale,
+           schedule)
     ra = _PLANS.get(key)
     if ra is None:
-        ra = RingAttention(RingPlan(seq_len, P, layout), r, q.shape[2], q.device, tokens_per_frame=tokens_per_frame,
-                           causal_frames=causal_frames, kv_format=kv_format, softmax_scale=softmax_scale)
-        _PLANS.clear()
+        release_ring_states()
+        plan = RingPlan(seq_len, P, layout)
+        kw = dict(tokens_per_frame=tokens_per_frame, causal_frames=causal_frames, kv_format=kv_format,
+                  softmax_scale=softmax_scale)
+        if schedule == "allgather":
+            ra = GatherAttention(plan, r, q.shape[2], q.device, group=group, **kw)
+        else:
+            ra = RingAttention(plan, r, q.shape[2], q.device, **kw)
         _PLANS[key] = ra
     return ra
 
 
+def release_ring_states() -> None:
+    """Free the cached ring states (peer buffers are unmapped: call before destroying the group)."""
+    for ra in _PLANS.values():
+        if hasattr(ra, "close"):
+            ra.close()
+    _PLANS.clear()
+
+
 def ring_attention_emulated(q, k, v, world: int, *, tokens_per_frame: int, causal_frames: int = 1,
-                            kv_format: str = "fp8_e4m3", layout: str = "zigzag", softmax_scale=None):
-    """The ring schedule for ``world`` emulated ranks in one process on one GPU: q/k/v are the
-    full sequence [1, L, H, 128]; every rank's queries meet every block in ring order with the
-    same kernels and accumulator modes as ``ring_attention``.  Returns the full output."""
+                            kv_format: str = "fp8_e4m3", layout: str = "zigzag", softmax_scale=None,
+                            schedule: str = "ring"):
+    """``world`` emulated ranks in one process on one GPU: q/k/v are the full sequence
+    [1, L, H, 128]; the same kernels, in the same order, as ``ring_attention`` with the given
+    schedule.  Returns the full output."""
+    if schedule == "allgather":
+        return _gather_emulated(q, k, v, world, tokens_per_frame=tokens_per_frame, causal_frames=causal_frames,
+                                kv_format=kv_format, layout=layout, softmax_scale=softmax_scale)
     plan = RingPlan(q.shape[1], world, layout)
     H, dev = q.shape[2], q.device
     rings = [RingAttention(plan, r, H, dev, tokens_per_frame=tokens_per_frame, causal_frames=causal_frames,
@@ -336,4 +516,27 @@ def ring_attention_emulated(q, k, v, world: int, *, tokens_per_frame: int, causa
                         ra._stage_block(blocks[src], plan.length(src), ra.kvh[0], cs)
                         ra._attend(src, ra.kvh[0], out, None, modes[s], cs)
             outs.append(out)
+    return plan.unshard(outs)
+
+
+def _gather_emulated(q, k, v, world, *, tokens_per_frame, causal_frames, kv_format, layout, softmax_scale):
+    plan = RingPlan(q.shape[1], world, layout)
+    H, dev = q.shape[2], q.device
+    kw = dict(tokens_per_frame=tokens_per_frame, causal_frames=causal_frames, kv_format=kv_format,
+              softmax_scale=softmax_scale)
+    block_bytes = ((2 * (plan.max_length() * H * _D + plan.max_length() * H * 4)) + 15) // 16 * 16
+    shared = torch.empty(world * block_bytes, dtype=torch.uint8, device=dev)
+    states = [GatherAttention(plan, r, H, dev, shared=shared, **kw) for r in range(world)]
+    for r, st in enumerate(states):
+        if plan.length(r):
+            st.fill_own(plan.shard(k, r).contiguous(), plan.shard(v, r).contiguous())
+    outs = []
+    cs = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        for r, st in enumerate(states):
+            o = torch.empty((1, plan.length(r), H, _D), dtype=torch.bfloat16, device=dev)
+            if plan.length(r):
+                qs = plan.shard(q, r).contiguous()
+                st.attend(qs, o, None, cs)
+            outs.append(o)
     return plan.unshard(outs)

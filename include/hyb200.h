@@ -213,6 +213,16 @@ int hyb_attn_work_plan(const hyb_attn_args* args, int32_t sms, int32_t* splits, 
 int hyb_stage_head_major(int32_t B, int32_t L, int32_t H, int32_t D, const hyb_tensor4* src_k,
                          const hyb_tensor4* src_v, void* dst_k, void* dst_v, void* stream);
 
+/* Sequence-parallel K/V blocks of P ranks -> head-major bf16 K and V [H, L, 128] of the whole
+ * sequence.  Block r (blocks[r], as mapped here) is [K codes | V codes | K scales | V scales]
+ * for Lmax rows of H heads; position pos in chunk c ([bounds[c], bounds[c+1])) is row
+ * row0[c] + pos - bounds[c] of block owner[c].  Decode as hyb_kv_dequant.  Replaces the
+ * per-step kv buffers of the reference ring (dynamic_ring_attention.py:115-286). */
+int hyb_ring_gather_stage(int32_t P, int32_t fmt, int32_t L, int32_t H, int32_t D, int32_t Lmax,
+                          const void* const* blocks, int32_t nchunks, const int32_t* bounds,
+                          const int32_t* owner, const int32_t* row0, void* out_k, void* out_v,
+                          void* stream);
+
 /* Key-visibility bitmap for hyb_attn_fwd with keys [0, Lk) of every batch row visible:
  * bits [B, kwords] uint32.  No reference counterpart (the reference ring attends every key of
  * a block; flash_attn_func takes no key mask). */
@@ -263,6 +273,14 @@ int hyb_ulysses_push_qkv(int32_t P, int32_t rank, int32_t B, int32_t Ls, int32_t
 int hyb_ulysses_push_o(int32_t P, int32_t rank, int32_t B, int32_t Ls, int32_t Lt, int32_t H, int32_t D,
                        const void* o_send, const hyb_tensor4* txt, void* const* out, void* const* txt_out,
                        const hyb_peer_sync* sync, void* stream);
+
+/* All-gather contribution over peer memory: `bytes` (a multiple of 16) from src to dst[d] on
+ * every rank d (skipping dst[d] == src), then the barrier.  The ring schedule of
+ * ring_attention passes its e4m3 K/V blocks this way (every block to every rank at once over
+ * NVSwitch instead of one neighbour hop per step: flash_attn_p2p_communicate,
+ * dynamic_ring_attention.py:45-83). */
+int hyb_peer_push_bytes(int32_t P, int32_t rank, const void* src, int64_t bytes, void* const* dst,
+                        const hyb_peer_sync* sync, void* stream);
 
 /* Ulysses send-side pack (sequence -> heads): q, k, v bf16 [B, Ls, H, D] -> send buffer
  * [P, Ls_max, nsrc*B, H/P, D] (the all_to_all_qkv layout, padding rows zeroed).

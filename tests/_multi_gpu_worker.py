@@ -107,17 +107,19 @@ def main():
     Lr, Tr = 8 * 96 + 5, 96
     rq, rk, rv = (seeded_kv((1, Lr, 4, D), make_generator(77 + i)).to(dev) for i in range(3))
     emu = ring.ring_attention_emulated(rq, rk, rv, world, tokens_per_frame=Tr)
-    for layout in ("zigzag", "contiguous"):
+    for schedule, layout in (("ring", "zigzag"), ("ring", "contiguous"), ("allgather", "zigzag"),
+                             ("allgather", "contiguous")):
         plan = ring.RingPlan(Lr, world, layout)
-        emu = ring.ring_attention_emulated(rq, rk, rv, world, tokens_per_frame=Tr, layout=layout)
+        emu = ring.ring_attention_emulated(rq, rk, rv, world, tokens_per_frame=Tr, layout=layout, schedule=schedule)
         for _ in range(2):   # second pass reuses the cached plan and buffers
             out_ring = ring.ring_attention(plan.shard(rq, rank).contiguous(), plan.shard(rk, rank).contiguous(),
                                            plan.shard(rv, rank).contiguous(), None, seq_len=Lr,
-                                           tokens_per_frame=Tr, layout=layout)
+                                           tokens_per_frame=Tr, layout=layout, schedule=schedule)
         if not torch.equal(out_ring, plan.shard(emu, rank)):
-            print("ring mismatch on rank", rank, layout,
+            print("ring mismatch on rank", rank, schedule, layout,
                   (out_ring.float() - plan.shard(emu, rank).float()).abs().max().item())
             ok = False
+    ring.release_ring_states()
     ok_t = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
     ok = bool(ok_t.item())

@@ -109,10 +109,11 @@ def test_lse_merge_kernel_matches_oracle(cuda_lib):
     torch.testing.assert_close(acc.cpu().double(), torch.from_numpy(g["out"])[0], rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("schedule", ["ring", "allgather"])
 @pytest.mark.parametrize("P,frames,T,layout", [(1, 5, 64, "zigzag"), (4, 21, 48, "zigzag"),
                                                (3, 7, 100, "zigzag"), (3, 7, 100, "contiguous"),
                                                (8, 21, 39, "zigzag")])
-def test_ring_schedule_matches_frame_causal_oracle(cuda_lib, P, frames, T, layout):
+def test_ring_schedule_matches_frame_causal_oracle(cuda_lib, P, frames, T, layout, schedule):
     """The ring's per-step attention launches with the accumulating epilogue, over P emulated
     ranks, equal frame-causal attention over the whole sequence (shards not aligned to frames,
     ragged zig-zag chunks when L is not a multiple of 2P)."""
@@ -123,7 +124,8 @@ def test_ring_schedule_matches_frame_causal_oracle(cuda_lib, P, frames, T, layou
     H, L = 2, frames * T - 1
     gen = make_generator(900 + P)
     q, k, v = (seeded_kv((1, L, H, 128), gen) for _ in range(3))
-    got = ring.ring_attention_emulated(q.to(dev), k.to(dev), v.to(dev), P, tokens_per_frame=T, layout=layout)
+    got = ring.ring_attention_emulated(q.to(dev), k.to(dev), v.to(dev), P, tokens_per_frame=T, layout=layout,
+                                       schedule=schedule)
     # keys and values as the blocks carry them: e4m3 per (token, head), decoded
     kd = oq.dequantize(*oq.quantize_e4m3(k))
     vd = oq.dequantize(*oq.quantize_e4m3(v))

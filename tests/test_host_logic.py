@@ -156,3 +156,20 @@ def test_window_ring_matches_reference_slide(sink, keep, appends):
         assert rows.dtype == torch.int32 and rows.numel() == win.valid_len == ref_frames * T
         got = win.cache["k"][:, rows.long()]
         assert torch.equal(got, ref_k[:, :ref_frames * T])
+
+
+@pytest.mark.parametrize("L,P,layout", [(32760, 8, "zigzag"), (1001, 3, "zigzag"), (1001, 3, "contiguous"),
+                                        (7, 4, "zigzag")])
+def test_gather_chunks_lay_out_the_sequence(L, P, layout):
+    """The all-gather schedule's chunk table: chunks tile [0, L) in order, and chunk rows index
+    each owner's block in the order the owner holds its tokens."""
+    from hy_nomas_b200.ring import RingPlan
+    plan = RingPlan(L, P, layout)
+    chunks = plan.gather_chunks()
+    pos = 0
+    for start, n, owner, row0 in chunks:
+        assert start == pos and n > 0
+        shard = plan.shard(torch.arange(L).view(1, L), owner)
+        assert torch.equal(shard[0, row0:row0 + n], torch.arange(start, start + n))
+        pos += n
+    assert pos == L
