@@ -1083,7 +1083,8 @@ int choose_kv_splits(int B, int H, int Lq, int Lk, int sms) {
 // Capacity of the partial buffers: the most key slices any query pair may be cut into (the
 // per-pair counts are chosen at launch by plan_units).  The dense estimate above, raised to 4
 // when the launch has fewer than 8 waves of pair-CTAs (its tail is then a large share), and
-// bounded to 1 GiB of partial rows.
+// bounded to 1 GiB of partial rows.  (Room for more slices was measured slower at 3 heads:
+// the planner then cut pairs into 7-8 slices, whose partial rows cost more than it models.)
 int split_capacity(int B, int H, int Lq, int Lk, int sms) {
   const char* e = getenv("HYB_KV_SPLITS");
   if (e != nullptr) {
