@@ -1667,11 +1667,11 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
 // process whose framework has already reserved (nearly) all of HBM in its own pool for the
 // KV cache and activations, a latency-critical decode loop that must not call cudaMalloc
 // because it can synchronise the whole device, or a plugin host whose FFI passes tensors but
-// no allocator.  For them the staging scratch (head-major Q/K/V and the visibility bitmaps)
-// lives in one fixed device array owned by this library.  The array is static device memory:
+// no allocator.  For them the staging scratch (head-major Q/K/V, the visibility bitmaps and the
+// fp32 partial rows of split query pairs) lives in one fixed device array owned by this library.  The array is static device memory:
 // every GPU on which this library's kernels are loaded holds it until the process exits.
-// Nothing in it has to start at zero: within one call every byte the attention kernel reads
-// is first written by that call's mask and staging kernels.
+// Nothing in it has to start at zero: within one call every byte the attention and merge
+// kernels read is first written by that call's mask, staging and attention kernels.
 // =========================================================================================
 static constexpr long long kNoAllocScratchBytes = 64LL << 20;  // 64 MiB per device
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];

@@ -39,3 +39,14 @@ def cuda_lib():
     lib = _lib.load()
     assert lib.hyb_device_supported() == 1, "libhyb200 needs an sm_100 device"
     return lib
+
+
+def config1_inputs():
+    """The seeded BASELINE config-1 inputs (hist_k, hist_v, [img_q, img_k, img_v, txt_q,
+    txt_k, txt_v]) exactly as tests/golden/make_golden.py generated them for attn_config1.npz."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("make_golden", GOLDEN / "make_golden.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    hk, hv, cur = mod.config1_inputs()
+    return hk, hv, cur, mod.input_checksums([hk, hv, *cur])

@@ -22,6 +22,9 @@ its inputs and the reference's outputs (bf16 as int16 bit patterns, e4m3 as uint
                         (attention/dynamic_ring_attention.py:86-105), eager bodies
   window_slide.npz      SelfForcingTrainingPipeline._slide_kv_cache sink + window eviction
                         (hymm/models/self_forcing/causal_training_pipeline.py:203-236)
+  attn_config1.npz      BASELINE config 1 (8 heads, 256-token frame vs 4 cached E4M3 frames):
+                        the reference's outputs only; the inputs are regenerated from the seed
+                        (``config1_inputs``) and checked against the stored checksums
 """
 from __future__ import annotations
 
@@ -282,6 +285,43 @@ def make_window():
                         v_after=ns.kv_cache1[0]["v"].numpy())
 
 
+def config1_inputs():
+    """BASELINE config 1 inputs, regenerated identically by the tests: B=1, 8 heads x 128, a
+    256-token frame (16 x 16) against 4 cached frames (1,024 tokens) and 1 text token, seeded
+    N(0, 1) with 4 outlier channels per head x8 (config seed 1235)."""
+    from hy_nomas_b200.synthetic import config_seed, make_generator
+    gen = make_generator(config_seed(1))
+    H = 8
+    hk, hv = seeded((1, 1024, H, 128), gen), seeded((1, 1024, H, 128), gen)
+    cur = [seeded((1, L, H, 128), gen) for L in (256, 1) for _ in range(3)]
+    return hk, hv, cur
+
+
+def input_checksums(tensors):
+    return np.array([t.double().sum().item() for t in tensors], dtype=np.float64)
+
+
+def make_config1():
+    """Config 1 through the reference: e4m3 codes of the history (restated quantiser; the
+    reference has no FP8 cache) decoded into a bf16 cache, one torch-mode call.  Stores only
+    the outputs and input checksums (the inputs are regenerated from the seed)."""
+    native = importlib.import_module("hymm.models.dit.nomas_cpt")
+    from oracle.quant import dequantize, quantize_e4m3
+    hk, hv, cur = config1_inputs()
+    ck, sk = quantize_e4m3(hk)
+    cv, sv = quantize_e4m3(hv)
+    Lh, Li, Lt, H = 1024, 256, 1, 8
+    cache = {"k": torch.zeros(1, Lh + Li + Lt, H, 128, dtype=torch.bfloat16),
+             "v": torch.zeros(1, Lh + Li + Lt, H, 128, dtype=torch.bfloat16)}
+    cache["k"][:, :Lh] = dequantize(ck, sk)
+    cache["v"][:, :Lh] = dequantize(cv, sv)
+    out = _call_ref(native, q=(cur[0], cur[3]), k=(cur[1], cur[4]), v=(cur[2], cur[5]), kv_cache=cache,
+                    cache_valid_len=Lh, text_mask=None, update_cache=False, cache_txt=True, cache_mask=None)
+    np.savez_compressed(HERE / "attn_config1.npz", out_img=bf(out[0].reshape(1, Li, H, 128)),
+                        out_txt=bf(out[1].reshape(1, Lt, H, 128)),
+                        checksums=input_checksums([hk, hv, *cur]))
+
+
 def main():
     _install_stub()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
@@ -291,6 +331,7 @@ def main():
     make_ring_merge()
     make_window()
     make_sp()
+    make_config1()
     print("fixtures written to", HERE)
 
 

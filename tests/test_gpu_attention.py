@@ -408,3 +408,25 @@ def test_graphed_call_replays_the_drop_in(cuda_lib):
         call.release()
     finally:
         os.environ.pop("HYB_ASSUME_FINITE_KV", None)
+
+
+def test_config1_drop_in_matches_reference(cuda_lib):
+    """BASELINE config 1 through the drop-in (history quantised on the GPU into an E4M3 cache,
+    one frame of 256 tokens, frame-causal) against the reference's own outputs."""
+    from conftest import config1_inputs
+    g = load_golden("attn_config1.npz")
+    dev = torch.device("cuda")
+    hk, hv, cur, _ = config1_inputs()
+    Lh, Li, Lt, H = 1024, 256, 1, 8
+    cache = kvc.make_fp8_kv_block(1, Lh + Li + Lt, H, 128, device=dev)
+    kvc.quantize_kv_pair_into(cache, hk.to(dev), hv.to(dev), 0)
+    c = [t.to(dev) for t in cur]
+    with torch.no_grad():
+        out_img, out_txt = hatt.causal_attention_with_cache_mp(
+            (c[0], c[3]), (c[1], c[4]), (c[2], c[5]), cache, cache_valid_len=Lh, attn_mode="flash3",
+            tokens_per_frame=256, chunk_causal_frames=1)
+    for got, key in ((out_img, "out_img"), (out_txt, "out_txt")):
+        ref = bf16(g[key]).float()
+        o = got.reshape(ref.shape).float().cpu()
+        assert ((o - ref).abs() <= ATOL + 1e-2 * ref.abs()).all(), key
+        assert torch.nn.functional.cosine_similarity(o.flatten()[None], ref.flatten()[None]).item() >= COS

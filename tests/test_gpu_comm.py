@@ -152,3 +152,28 @@ def test_stage_head_major_matches_dequant(cuda_lib):
                                              _stream()), "stage")
     ref = oq.dequantize(codes, scale)[0].permute(1, 0, 2).contiguous()
     assert torch.equal(out.cpu().view(torch.int16), ref.view(torch.int16))
+
+
+def test_peer_barrier_times_out_into_the_status_word(cuda_lib):
+    """The device barrier that ends every peer push waits for a flag that nothing sets here
+    (the second "rank" is a local buffer no one signals from): after its bounded spin it
+    records HYB_DEV_TIMEOUT in the status word and returns, and the context stays usable."""
+    dev = torch.device("cuda")
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    src = torch.arange(64, dtype=torch.int32, device=dev)
+    dst = [torch.zeros(64, dtype=torch.int32, device=dev) for _ in range(2)]
+    flags = [torch.zeros(64, dtype=torch.int32, device=dev) for _ in range(2)]
+    state = torch.zeros(2, dtype=torch.int32, device=dev)
+    sync = _lib.PeerSync()
+    sync.flags[0], sync.flags[1] = flags[0].data_ptr(), flags[1].data_ptr()
+    sync.state = state.data_ptr()
+    sync.dev_status = status.data_ptr()
+    table = (ctypes.c_void_p * 2)(dst[0].data_ptr(), dst[1].data_ptr())
+    _lib.check(cuda_lib.hyb_peer_push_bytes(2, 0, src.data_ptr(), src.numel() * 4, table, ctypes.byref(sync),
+                                            _stream()), "push")
+    torch.cuda.synchronize()
+    assert status.item() & _lib.HYB_DEV_TIMEOUT
+    assert torch.equal(dst[1], src) and torch.equal(dst[0], src)   # both destinations differ from the source
+    assert flags[1][0].item() == 1 and flags[0][0].item() == 1 and flags[0][1].item() == 0
+    assert int(state[0].item()) == 0 and int(state[1].item()) == 1
+    assert torch.equal(src + 1, torch.arange(1, 65, dtype=torch.int32, device=dev))   # context still usable

@@ -173,3 +173,17 @@ def test_oracle_window_slide_matches_reference():
     vis = owin.visible_frames(frames, sink, keep)
     rows = torch.cat([torch.arange(f * T, (f + 1) * T) for f in vis])
     assert torch.equal(k[:, rows], k_after[:, :len(vis) * T])
+
+
+def test_oracle_config1_matches_reference():
+    """BASELINE config 1 (8 heads, a 256-token frame against 4 cached E4M3 frames + 1 text
+    token): the regenerated inputs are the fixture's, and the oracle equals the reference."""
+    from conftest import config1_inputs
+    g = load_golden("attn_config1.npz")
+    hk, hv, cur, sums = config1_inputs()
+    assert np.array_equal(sums, g["checksums"])
+    dk = oq.dequantize(*oq.quantize_e4m3(hk))
+    dv = oq.dequantize(*oq.quantize_e4m3(hv))
+    out_img, out_txt = oatt.cached_attention(*cur, dk, dv, group_tokens=256)
+    torch.testing.assert_close(out_img, bf16(g["out_img"]).float(), atol=ORACLE_ATOL, rtol=ORACLE_RTOL)
+    torch.testing.assert_close(out_txt, bf16(g["out_txt"]).float(), atol=ORACLE_ATOL, rtol=ORACLE_RTOL)
