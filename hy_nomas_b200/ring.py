@@ -48,7 +48,11 @@ class RingPlan:
             raise ValueError(f"unknown ring layout {layout!r}")
         self.seq_len, self.world, self.layout = seq_len, world, layout
         n = 2 * world if layout == "zigzag" else world
-        bounds = [(i * seq_len) // n for i in range(n + 1)]
+        # Chunks of at least 4 query pairs start on a 256-token boundary (one query pair of the
+        # attention kernel), so that no pair holds rows of both of a rank's chunks: such a pair
+        # would load the key range of its later rows for all of its rows.
+        align = 256 if seq_len >= n * 1024 else 1
+        bounds = [min(seq_len, ((i * seq_len) // n + align // 2) // align * align) for i in range(n)] + [seq_len]
         chunk = [(bounds[i], bounds[i + 1] - bounds[i]) for i in range(n)]
         if layout == "zigzag":
             self.segments = [(chunk[r], chunk[n - 1 - r]) for r in range(world)]

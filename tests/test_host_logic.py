@@ -108,7 +108,9 @@ def test_ring_plan_partitions_the_sequence(L, P, layout):
         for p, n in segs:
             owned.extend(range(p, p + n))
     assert sorted(owned) == list(range(L))
-    assert max(plan.length(r) for r in range(P)) - min(plan.length(r) for r in range(P)) <= 2
+    n = 2 * P if layout == "zigzag" else P
+    align = 256 if L >= n * 1024 else 1     # large chunks start on query-pair boundaries
+    assert max(plan.length(r) for r in range(P)) - min(plan.length(r) for r in range(P)) <= 2 * align
     if L:
         x = torch.arange(L).view(1, L, 1, 1)
         assert torch.equal(plan.unshard([plan.shard(x, r) for r in range(P)]), x)
