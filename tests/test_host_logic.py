@@ -175,3 +175,43 @@ def test_gather_chunks_lay_out_the_sequence(L, P, layout):
         assert torch.equal(shard[0, row0:row0 + n], torch.arange(start, start + n))
         pos += n
     assert pos == L
+
+
+def test_bench_reference_arm_prints_the_contract_line():
+    """bench.py --impl reference (the reference's CPU path on the host cores) prints one JSON
+    line with the metric, unit, impl and the e2e / cpu_baseline objects the driver reads."""
+    import json
+    import subprocess
+    import sys
+    from conftest import REPO
+    res = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "0", "--cpu-heads", "1"], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stderr[-2000:]
+    lines = [ln for ln in res.stdout.strip().splitlines() if ln.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["unit"] == "TFLOP/s" and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+
+
+@pytest.mark.parametrize("P", [2, 4, 8])
+def test_large_zigzag_chunks_start_on_query_pair_boundaries(P):
+    """Config 3: every chunk but the last starts and ends on a 256-token boundary, so no query
+    pair of the attention kernel holds rows of both of a rank's chunks."""
+    from hy_nomas_b200.ring import RingPlan
+    plan = RingPlan(21 * 1560, P, "zigzag")
+    for r in range(P):
+        (p0, n0), (p1, n1) = plan.segments[r]
+        assert p0 % 256 == 0 and n0 % 256 == 0 and p1 % 256 == 0
+
+
+def test_peer_exchange_needs_equal_lengths_and_divisible_heads(monkeypatch):
+    from hy_nomas_b200 import communications as comm
+    monkeypatch.delenv("HYB_PEER_EXCHANGE", raising=False)
+    assert comm.peer_exchange_enabled((780,) * 8, 24)
+    assert not comm.peer_exchange_enabled((780, 779), 24)       # uneven: NCCL path
+    assert not comm.peer_exchange_enabled((780,) * 5, 24)       # heads not divisible
+    assert not comm.peer_exchange_enabled((780,), 24)           # one rank: no exchange
+    monkeypatch.setenv("HYB_PEER_EXCHANGE", "0")
+    assert not comm.peer_exchange_enabled((780,) * 8, 24)
