@@ -209,17 +209,18 @@ def bf16_view(t: torch.Tensor) -> Tensor4:
     """[B, L, H, D] bf16 tensor -> Tensor4."""
     if t.dtype != torch.bfloat16 or t.ndim != 4:
         raise TypeError("expected a [B, L, H, D] bfloat16 tensor")
-    if t.stride(3) != 1:
+    st = t.stride()
+    if st[3] != 1:
         raise ValueError("head_dim must be the contiguous dimension")
-    return Tensor4(t.data_ptr(), HYB_FMT_BF16, 0, t.stride(0), t.stride(1), t.stride(2), None, 0, 0, 0)
+    return Tensor4(t.data_ptr(), HYB_FMT_BF16, 0, st[0], st[1], st[2], None, 0, 0, 0)
 
 
 def coded_view(codes: torch.Tensor, scale: torch.Tensor, fmt: int) -> Tensor4:
     """Quantised cache (codes [B, L, H, D], fp32 scale [B, L, H, 1]) -> Tensor4."""
-    if codes.stride(3) != 1:
+    st, ss = codes.stride(), scale.stride()
+    if st[3] != 1:
         raise ValueError("head_dim must be the contiguous dimension")
-    return Tensor4(codes.data_ptr(), fmt, 0, codes.stride(0), codes.stride(1), codes.stride(2),
-                   scale.data_ptr(), scale.stride(0), scale.stride(1), scale.stride(2))
+    return Tensor4(codes.data_ptr(), fmt, 0, st[0], st[1], st[2], scale.data_ptr(), ss[0], ss[1], ss[2])
 
 
 _STATUS: dict[int, torch.Tensor] = {}

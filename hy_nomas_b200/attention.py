@@ -297,10 +297,9 @@ def causal_attention_with_cache_mp(
     img_len = img_k.shape[1]
     txt_len = txt_k.shape[1]
     H, D = img_q.shape[2], img_q.shape[3]
-    if text_mask is not None:
-        cur_txt_mask = text_mask.bool()
-    else:
-        cur_txt_mask = torch.ones(B, txt_len, device=img_k.device, dtype=torch.bool)
+    # No text mask means every text token is valid: the kernels read a NULL mask that way, so
+    # no all-true mask is built per call.
+    cur_txt_mask = text_mask.bool() if text_mask is not None else None
 
     history_batch = kv_cache["k"].shape[0]
     if history_batch != B:
@@ -342,7 +341,7 @@ def causal_attention_with_cache_mp(
                 kv_cache["v"][:, off:off + tv.shape[1]] = tv.detach()
                 off += tk.shape[1]
         if cache_mask is not None:
-            if cache_txt:
+            if cache_txt and cur_txt_mask is not None:
                 cache_mask[:, cache_valid_len:cache_valid_len + img_len] = True
                 cache_mask[:, cache_valid_len + img_len:new_end] = cur_txt_mask
             else:
