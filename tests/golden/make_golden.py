@@ -25,6 +25,13 @@ its inputs and the reference's outputs (bf16 as int16 bit patterns, e4m3 as uint
   attn_config1.npz      BASELINE config 1 (8 heads, 256-token frame vs 4 cached E4M3 frames):
                         the reference's outputs only; the inputs are regenerated from the seed
                         (``config1_inputs``) and checked against the stored checksums
+  intra_<case>.npz      causal_attention_with_cache_mp(attn_mode="flash3") with intra-segment
+                        action masks (nomas_cpt.py:691-770 -> _intra_seg_cache_forward, :198-332,
+                        ranges from _build_intra_seg_cache_ranges, :107-193).  The range kernel
+                        it calls (MagiAttention / flex) runs on CUDA only; a dense stand-in with
+                        the kernels' rectangle-union semantics (overlaps refused, rows without
+                        ranges zero, fp32 softmax, bf16 output) takes its place, and the ranges
+                        the reference built are stored as a dense visibility per sample
 """
 from __future__ import annotations
 
@@ -322,9 +329,101 @@ def make_config1():
                         checksums=input_checksums([hk, hv, *cur]))
 
 
+
+def _dense_range_kernel(calls):
+    """Stand-in for the range attention kernel (CUDA-only in the reference): the union of the
+    (q_range, k_range) rectangles is the visibility, as both backends define it (flex refuses
+    overlapping rectangles, range_attention.py:97-100); softmax in fp32, rows without keys
+    zero, output in the input dtype.  Every call's rectangles are appended to ``calls``."""
+    def kernel(q, k, v, q_ranges, k_ranges, attn_type_map=None, backend="magi", softmax_scale=None,
+               deterministic=False, **kwargs):
+        nq, nk, D = q.shape[0], k.shape[0], q.shape[-1]
+        cover = torch.zeros(nq, nk, dtype=torch.int32)
+        for (qs, qe), (ks, ke) in zip(q_ranges.tolist(), k_ranges.tolist()):
+            cover[qs:qe, ks:ke] += 1
+        if nq and nk and int(cover.max()) > 1:
+            raise ValueError("overlapping QK rectangles")
+        vis = cover.bool()
+        calls.append(vis.clone())
+        qf, kf, vf = (x.float().transpose(0, 1) for x in (q, k, v))
+        s = (qf @ kf.transpose(1, 2)) * (softmax_scale or 1.0 / D ** 0.5)
+        s = s.masked_fill(~vis[None], float("-inf"))
+        m = s.amax(-1, keepdim=True)
+        m = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+        p = torch.exp(s - m)
+        l = p.sum(-1, keepdim=True)
+        o = (p @ vf) / torch.where(l > 0, l, torch.ones_like(l))
+        return o.transpose(0, 1).to(q.dtype), None
+    return kernel
+
+
+def make_intra_seg():
+    """Intra-segment action masks through the reference's flash3 cached path (INT8 cache)."""
+    native = importlib.import_module("hymm.models.dit.nomas_cpt")
+    i8 = importlib.import_module("hymm.models.dit.modules.int8_kv_cache")
+    H, D = 2, 128
+    calls = []
+    native.range_attention = _dense_range_kernel(calls)
+    native._flex_flash_attn_func = object()      # the magi branch only checks that it exists
+
+    def run_case(name, B, Lh, holes, T, frames, text_mask, offsets, windows, update_cache, seed):
+        gen = torch.Generator().manual_seed(seed)
+        Li, Lt = T * frames, len(text_mask[0])
+        cap = Lh + Li + Lt + 8
+        cache = i8.make_int8_kv_block(B, cap, H, D, device="cpu")
+        if Lh:
+            i8.quantize_kv_pair_into(cache, seeded((B, Lh, H, D), gen), seeded((B, Lh, H, D), gen), 0)
+        args = [seeded((B, L, H, D), gen) for L in (Li, Lt) for _ in range(3)]
+        cmask = torch.zeros(B, cap, dtype=torch.bool)
+        cmask[:, :Lh] = True
+        for b, (a, e) in holes:
+            cmask[b, a:e] = False
+        tmask = torch.tensor(text_mask, dtype=torch.bool)
+        before = {k: v.clone() for k, v in cache.items()}
+        mask_before = cmask.clone()
+        calls.clear()
+        with torch.no_grad():
+            out = native.causal_attention_with_cache_mp(
+                (args[0], args[3]), (args[1], args[4]), (args[2], args[5]), cache, cache_valid_len=Lh,
+                attn_mode="flash3", text_mask=tmask, update_cache=update_cache, cache_txt=True,
+                cache_mask=cmask, intra_seg_txt_offsets=offsets, intra_seg_vid_windows=windows,
+                tokens_per_frame=T, seg_ar_attention_backend="magi")
+        assert len(calls) == B
+        # the reference's rectangles (compact per sample) as dense [Lq, Lk] visibility
+        dense = torch.zeros(B, Li + Lt, Lh + Li + Lt, dtype=torch.bool)
+        for b in range(B):
+            hist_idx = mask_before[b, :Lh].nonzero().flatten()
+            txt_idx = tmask[b].nonzero().flatten()
+            qpos = torch.cat([torch.arange(Li), Li + txt_idx])
+            kpos = torch.cat([hist_idx, Lh + torch.arange(Li), Lh + Li + txt_idx])
+            dense[b][qpos[:, None], kpos[None, :]] = calls[b]
+        np.savez_compressed(
+            HERE / f"intra_{name}.npz", Lh=Lh, T=T, frames=frames, update_cache=update_cache,
+            hist_k=before["k"].numpy(), hist_v=before["v"].numpy(), hist_k_scale=before["k_scale"].numpy(),
+            hist_v_scale=before["v_scale"].numpy(), cache_mask=mask_before.numpy(), text_mask=tmask.numpy(),
+            offsets=np.array([-1 if o is None else len(o) for o in offsets], dtype=np.int64),
+            offsets_flat=np.array([x for o in offsets if o is not None for x in o], dtype=np.int64),
+            windows=np.array(windows, dtype=np.int64).reshape(-1, 3), ref_visibility=dense.numpy(),
+            img_q=bf(args[0]), img_k=bf(args[1]), img_v=bf(args[2]), txt_q=bf(args[3]), txt_k=bf(args[4]),
+            txt_v=bf(args[5]), out_img=bf(out[0].reshape(B, Li, H, D)), out_txt=bf(out[1].reshape(B, Lt, H, D)))
+
+    # head text, two actions, a gap window; padded text tokens; history holes
+    run_case("basic", 1, 64, [(0, (5, 9))], 16, 3, [[1, 1, 1, 0, 1, 1, 1, 0]], [[2, 4, 6]],
+             [[0, 1, 0], [1, 2, -1], [2, 3, 1]], False, 41)
+    # two samples: offsets past the valid text (clamped), an uncovered frame; the second sample
+    # has no offsets and keeps full attention
+    run_case("batch", 2, 48, [(0, (0, 4)), (1, (20, 30))], 16, 3, [[1, 1, 1, 1, 1, 0], [1, 0, 1, 1, 0, 0]],
+             [[1, 3, 7], None], [[0, 1, 1], [2, 3, 0]], False, 42)
+    # empty history, empty head, cache write of the chunk
+    run_case("nohist_update", 1, 0, [], 16, 3, [[1, 1, 1, 1]], [[0, 2, 3]], [[0, 2, 1], [2, 3, 0]], True, 43)
+
+
 def main():
     _install_stub()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
+    if "--only-intra" in sys.argv:
+        make_intra_seg()
+        return
     if "--only-late" not in sys.argv:
         make_quant()
         make_attention()
@@ -332,6 +431,7 @@ def main():
     make_window()
     make_sp()
     make_config1()
+    make_intra_seg()
     print("fixtures written to", HERE)
 
 

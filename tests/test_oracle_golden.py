@@ -187,3 +187,56 @@ def test_oracle_config1_matches_reference():
     out_img, out_txt = oatt.cached_attention(*cur, dk, dv, group_tokens=256)
     torch.testing.assert_close(out_img, bf16(g["out_img"]).float(), atol=ORACLE_ATOL, rtol=ORACLE_RTOL)
     torch.testing.assert_close(out_txt, bf16(g["out_txt"]).float(), atol=ORACLE_ATOL, rtol=ORACLE_RTOL)
+
+
+INTRA_CASES = ["basic", "batch", "nohist_update"]
+
+
+def intra_case(name):
+    """Inputs of an intra-segment fixture: decoded history, the chunk, masks, per-sample
+    offsets (None where the reference got None) and the windows in tokens."""
+    g = load_golden(f"intra_{name}.npz")
+    Lh, T = int(g["Lh"]), int(g["T"])
+    counts, flat = g["offsets"].tolist(), g["offsets_flat"].tolist()
+    offsets, pos = [], 0
+    for c in counts:
+        offsets.append(None if c < 0 else flat[pos:pos + c])
+        pos += max(c, 0)
+    windows = [[int(a) * T, int(b) * T, int(c)] for a, b, c in g["windows"].tolist()]
+    hk = oq.dequantize(torch.from_numpy(g["hist_k"][:, :Lh]), torch.from_numpy(g["hist_k_scale"][:, :Lh]))
+    hv = oq.dequantize(torch.from_numpy(g["hist_v"][:, :Lh]), torch.from_numpy(g["hist_v_scale"][:, :Lh]))
+    cur = [bf16(g[n]) for n in ("img_q", "img_k", "img_v", "txt_q", "txt_k", "txt_v")]
+    return g, Lh, T, offsets, windows, hk, hv, cur
+
+
+@pytest.mark.parametrize("name", INTRA_CASES)
+def test_oracle_intra_segment_visibility_is_the_reference_ranges(name):
+    """Row by row, the restated mask equals the rectangles the reference's range builder made
+    (exact: a single key too many or too few could hide inside the output tolerance)."""
+    g, Lh, T, offsets, windows, hk, hv, cur = intra_case(name)
+    B, Li = cur[0].shape[:2]
+    Lt = cur[3].shape[1]
+    vis, qvalid = oatt.intra_segment_visibility(
+        Lh, Li, Lt, offsets, windows, history_mask=torch.from_numpy(g["cache_mask"]),
+        text_mask=torch.from_numpy(g["text_mask"]), batch=B)
+    assert torch.equal(vis & qvalid[:, :, None], torch.from_numpy(g["ref_visibility"]))
+
+
+@pytest.mark.parametrize("name", INTRA_CASES)
+def test_oracle_intra_segment_matches_reference(name):
+    g, Lh, T, offsets, windows, hk, hv, cur = intra_case(name)
+    out_img, out_txt = oatt.intra_segment_attention(
+        *cur, hk, hv, offsets, windows, history_mask=torch.from_numpy(g["cache_mask"]),
+        text_mask=torch.from_numpy(g["text_mask"]))
+    torch.testing.assert_close(out_img, bf16(g["out_img"]).float(), atol=ORACLE_ATOL, rtol=ORACLE_RTOL)
+    torch.testing.assert_close(out_txt, bf16(g["out_txt"]).float(), atol=ORACLE_ATOL, rtol=ORACLE_RTOL)
+    # rows without ranges are exactly zero in both
+    ref_zero = bf16(g["out_img"]).float().abs().amax(dim=(2, 3)) == 0
+    assert torch.equal(out_img.abs().amax(dim=(2, 3)) == 0, ref_zero)
+
+
+def test_oracle_intra_segment_rejects_overlaps_and_unordered_offsets():
+    with pytest.raises(ValueError, match="overlap"):
+        oatt.intra_segment_rows(32, 2, [1, 2], [[0, 20, 0], [16, 32, -1]])
+    with pytest.raises(ValueError, match="nondecreasing"):
+        oatt.intra_segment_rows(32, 4, [3, 1, 4], [[0, 32, 0]])
