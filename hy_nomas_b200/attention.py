@@ -18,8 +18,10 @@ order (``reactor/hy_nomas_cache.py:192-209``, which lacks ``sp_metadata`` and
 4. SP out: O head->seq all-to-all, text all-gather over heads (:864-872); cast to the
    input dtypes and reshape to [B, L, H*D] (:874-884).
 
-Modes the reference routes elsewhere and this build does not implement raise:
-``qvg`` storage, ``sparse_context``, intra-segment action masks and SWA commits.
+Intra-segment action masks (``intra_seg_txt_offsets`` / ``intra_seg_vid_windows`` with
+``cache_txt``, :691-770) run in ``intra_seg.py`` on the same kernels.  Modes the reference
+routes elsewhere and this build does not implement raise: ``qvg`` storage,
+``sparse_context`` and SWA commits.
 """
 from __future__ import annotations
 
@@ -231,9 +233,12 @@ def causal_attention_with_cache_mp(
         raise RuntimeError("Flex cached attention requires no-grad inference")
     if sparse_context is not None:
         raise NotImplementedError("b200 cached attention: sparse_context routing is not implemented")
-    if (cache_txt and intra_seg_vid_windows is not None and len(intra_seg_vid_windows) > 0
-            and intra_seg_txt_offsets is not None and any(o is not None for o in intra_seg_txt_offsets)):
-        raise NotImplementedError("b200 cached attention: intra-segment action masks are not implemented")
+    intra = bool(cache_txt and intra_seg_vid_windows is not None and len(intra_seg_vid_windows) > 0
+                 and intra_seg_txt_offsets is not None and any(o is not None for o in intra_seg_txt_offsets))
+    if intra and attn_mode != "flash3":
+        raise RuntimeError(
+            "intra_segment_action_mask cache payload requires attn_mode='flash3', "
+            f"got {attn_mode!r}")
     if "swa_capacity" in kv_cache and update_cache:
         raise NotImplementedError("b200 cached attention: SWA commit is not implemented; use window.py")
 
@@ -364,10 +369,23 @@ def causal_attention_with_cache_mp(
     if is_sp:
         o_send, out_img_strides = comm.o_send_buffer(
             B, sp_metadata.sequence_lengths, H, D, img_q.device)
-    out_img, out_txt = cached_attention_local(
-        img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, cache_valid_len,
-        history_mask=history_mask, text_mask=cur_txt_mask, attend_txt=attend_txt,
-        group_tokens=group_tokens, out_img=o_send, out_img_strides=out_img_strides, hist_rows=hist_rows)
+    if intra:
+        from .intra_seg import intra_segment_attention
+        plain = o_send if (o_send is not None and out_img_strides is None) else _new_out(B, img_len, H, D, img_q.device)
+        out_txt = _new_out(B, txt_len, H, D, img_q.device)
+        intra_segment_attention(
+            img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, cache_valid_len,
+            offsets_per_sample=intra_seg_txt_offsets, windows=intra_seg_vid_windows,
+            tokens_per_frame=tokens_per_frame, history_mask=history_mask, text_mask=cur_txt_mask,
+            hist_rows=hist_rows, group_tokens=group_tokens, out_img=plain, out_txt=out_txt)
+        if o_send is not None and out_img_strides is not None:
+            comm.fill_o_send(o_send, plain)
+        out_img = o_send if o_send is not None else plain
+    else:
+        out_img, out_txt = cached_attention_local(
+            img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, cache_valid_len,
+            history_mask=history_mask, text_mask=cur_txt_mask, attend_txt=attend_txt,
+            group_tokens=group_tokens, out_img=o_send, out_img_strides=out_img_strides, hist_rows=hist_rows)
     stats["calls"] += 1
     if update_cache and window is not None:
         window.append(img_k.detach(), img_v.detach(), assume_finite=_assume_finite())

@@ -145,6 +145,14 @@ def o_send_buffer(B, sequence_lengths, Hp, D, device):
     return buf, None
 
 
+
+def fill_o_send(send, plain):
+    """Copy a head-sharded output held plainly, [B, L, Hp, D], into the packed send buffer
+    [P, Hp, Ls, B, D] of ``o_send_buffer`` (equal per-rank lengths, L = P * Ls)."""
+    P, Hp, Ls, B, D = send.shape
+    send.copy_(plain.view(B, P, Ls, Hp, D).permute(1, 3, 2, 0, 4))
+
+
 def all_to_all_o(send, group, batch, sequence_lengths, heads_local, dim):
     """Head-sharded attention output -> sequence-sharded [B, Ls, H, D]."""
     world = dist.get_world_size(group)

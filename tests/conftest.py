@@ -50,3 +50,21 @@ def config1_inputs():
     spec.loader.exec_module(mod)
     hk, hv, cur = mod.config1_inputs()
     return hk, hv, cur, mod.input_checksums([hk, hv, *cur])
+
+
+def intra_case(name):
+    """Inputs of an intra-segment fixture: decoded history, the chunk, masks, per-sample
+    offsets (None where the reference got None) and the windows in tokens."""
+    g = load_golden(f"intra_{name}.npz")
+    Lh, T = int(g["Lh"]), int(g["T"])
+    counts, flat = g["offsets"].tolist(), g["offsets_flat"].tolist()
+    offsets, pos = [], 0
+    for c in counts:
+        offsets.append(None if c < 0 else flat[pos:pos + c])
+        pos += max(c, 0)
+    windows = [[int(a) * T, int(b) * T, int(c)] for a, b, c in g["windows"].tolist()]
+    from oracle import quant as oq
+    hk = oq.dequantize(torch.from_numpy(g["hist_k"][:, :Lh]), torch.from_numpy(g["hist_k_scale"][:, :Lh]))
+    hv = oq.dequantize(torch.from_numpy(g["hist_v"][:, :Lh]), torch.from_numpy(g["hist_v_scale"][:, :Lh]))
+    cur = [bf16(g[n]) for n in ("img_q", "img_k", "img_v", "txt_q", "txt_k", "txt_v")]
+    return g, Lh, T, offsets, windows, hk, hv, cur

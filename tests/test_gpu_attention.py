@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import bf16, e4m3, load_golden
+from conftest import bf16, e4m3, intra_case, load_golden
 from hy_nomas_b200 import attention as hatt
 from hy_nomas_b200 import kv_cache as kvc
 from hy_nomas_b200.synthetic import make_generator, seeded_kv
@@ -430,3 +430,70 @@ def test_config1_drop_in_matches_reference(cuda_lib):
         o = got.reshape(ref.shape).float().cpu()
         assert ((o - ref).abs() <= ATOL + 1e-2 * ref.abs()).all(), key
         assert torch.nn.functional.cosine_similarity(o.flatten()[None], ref.flatten()[None]).item() >= COS
+
+
+@pytest.mark.parametrize("name", ["basic", "batch", "nohist_update"])
+def test_intra_segment_drop_in_matches_reference(cuda_lib, name):
+    """Intra-segment action masks through the drop-in (head text, per-action text slices, a
+    gap window, an uncovered frame, offsets past the valid text, a sample without offsets, a
+    cache write) against the reference's own outputs and against the fp32 oracle."""
+    g, Lh, T, offsets, windows_tok, hk, hv, cur = intra_case(name)
+    dev = torch.device("cuda")
+    cache = {n: torch.from_numpy(g[f"hist_{n}"]).to(dev) for n in ("k", "v")}
+    cache.update({f"{n}_scale": torch.from_numpy(g[f"hist_{n}_scale"]).to(dev) for n in ("k", "v")})
+    cmask = torch.from_numpy(g["cache_mask"]).to(dev)
+    tmask = torch.from_numpy(g["text_mask"])
+    d = [t.to(dev) for t in cur]
+    with torch.no_grad():
+        out_img, out_txt = hatt.causal_attention_with_cache_mp(
+            (d[0], d[3]), (d[1], d[4]), (d[2], d[5]), cache, cache_valid_len=Lh, attn_mode="flash3",
+            text_mask=tmask.to(dev), update_cache=bool(g["update_cache"]), cache_txt=True, cache_mask=cmask,
+            intra_seg_txt_offsets=offsets, intra_seg_vid_windows=g["windows"].tolist(), tokens_per_frame=T,
+            seg_ar_attention_backend="magi")
+    torch.cuda.synchronize()
+    B, Li, H, D = cur[0].shape
+    Lt = cur[3].shape[1]
+    out_img = out_img.reshape(B, Li, H, D).float().cpu()
+    out_txt = out_txt.reshape(B, Lt, H, D).float().cpu()
+    ref_img, ref_txt = bf16(g["out_img"]).float(), bf16(g["out_txt"]).float()
+    assert ((out_img - ref_img).abs() <= ATOL + 1e-2 * ref_img.abs()).all()
+    assert ((out_txt - ref_txt).abs() <= ATOL + 1e-2 * ref_txt.abs()).all()
+    # rows without ranges are exactly zero, and only those
+    assert torch.equal(out_img.abs().amax(dim=(2, 3)) == 0, ref_img.abs().amax(dim=(2, 3)) == 0)
+    assert torch.equal(out_txt.abs().amax(dim=(2, 3)) == 0, ref_txt.abs().amax(dim=(2, 3)) == 0)
+    o_img, o_txt, (m_img, m_txt) = oatt.intra_segment_attention(
+        *cur, hk, hv, offsets, windows_tok, history_mask=torch.from_numpy(g["cache_mask"]), text_mask=tmask,
+        return_magnitude=True)
+    assert_close(out_img, o_img, f"intra {name} image", m_img)
+    assert_close(out_txt, o_txt, f"intra {name} text", m_txt)
+
+
+def test_intra_segment_long_history_block_causal(cuda_lib):
+    """Three actions over an FP8 history of 5,000 tokens (the text rows' pass over the staged
+    keys runs in key slices) with the block-causal extension, against the fp32 oracle."""
+    T, frames, Lt = 160, 3, 40
+    cache, cur, dk, dv = make_case(1, 1, 5000, T * frames, Lt, 2, "fp8_e4m3", seed=77)
+    dev = torch.device("cuda")
+    cmask = torch.zeros(1, cache["k"].shape[1], dtype=torch.bool)
+    cmask[:, :5000] = True
+    cmask[:, 1200:1333] = False
+    tmask = torch.ones(1, Lt, dtype=torch.bool)
+    tmask[:, 30:] = False
+    tmask[:, 7] = False
+    offsets = [[5, 12, 20, 33]]
+    windows = [[0, 1, 2], [1, 2, 0], [2, 3, 1]]
+    d = [t.to(dev) for t in cur]
+    with torch.no_grad():
+        out_img, out_txt = hatt.causal_attention_with_cache_mp(
+            (d[0], d[3]), (d[1], d[4]), (d[2], d[5]), to_dev(cache, dev), cache_valid_len=5000,
+            attn_mode="flash3", text_mask=tmask.to(dev), cache_txt=True, cache_mask=cmask.to(dev),
+            intra_seg_txt_offsets=offsets, intra_seg_vid_windows=windows, tokens_per_frame=T,
+            chunk_causal_frames=1)
+    torch.cuda.synchronize()
+    o_img, o_txt, (m_img, m_txt) = oatt.intra_segment_attention(
+        *cur, dk, dv, offsets, [[a * T, b * T, c] for a, b, c in windows], history_mask=cmask, text_mask=tmask,
+        group_tokens=T, return_magnitude=True)
+    assert_close(out_img.reshape(o_img.shape), o_img, "long intra image", m_img)
+    assert_close(out_txt.reshape(o_txt.shape), o_txt, "long intra text", m_txt)
+    assert torch.all(out_txt.reshape(o_txt.shape).cpu()[0, 30:] == 0)
+

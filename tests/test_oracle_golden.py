@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import bf16, e4m3, load_golden
+from conftest import bf16, e4m3, intra_case, load_golden
 from oracle import attention as oatt
 from oracle import quant as oq
 from oracle import sp as osp
@@ -190,23 +190,6 @@ def test_oracle_config1_matches_reference():
 
 
 INTRA_CASES = ["basic", "batch", "nohist_update"]
-
-
-def intra_case(name):
-    """Inputs of an intra-segment fixture: decoded history, the chunk, masks, per-sample
-    offsets (None where the reference got None) and the windows in tokens."""
-    g = load_golden(f"intra_{name}.npz")
-    Lh, T = int(g["Lh"]), int(g["T"])
-    counts, flat = g["offsets"].tolist(), g["offsets_flat"].tolist()
-    offsets, pos = [], 0
-    for c in counts:
-        offsets.append(None if c < 0 else flat[pos:pos + c])
-        pos += max(c, 0)
-    windows = [[int(a) * T, int(b) * T, int(c)] for a, b, c in g["windows"].tolist()]
-    hk = oq.dequantize(torch.from_numpy(g["hist_k"][:, :Lh]), torch.from_numpy(g["hist_k_scale"][:, :Lh]))
-    hv = oq.dequantize(torch.from_numpy(g["hist_v"][:, :Lh]), torch.from_numpy(g["hist_v_scale"][:, :Lh]))
-    cur = [bf16(g[n]) for n in ("img_q", "img_k", "img_v", "txt_q", "txt_k", "txt_v")]
-    return g, Lh, T, offsets, windows, hk, hv, cur
 
 
 @pytest.mark.parametrize("name", INTRA_CASES)
