@@ -6,8 +6,8 @@ attribute ``hymm.models.dit.nomas_cpt.causal_attention_with_cache_mp`` is replac
 ``MMDoubleStreamBlock.forward_with_cache`` (nomas_cpt.py:1398-1416) and the TP block
 (modules/tensor_parallel.py:180) call the B200 path.  The replacement reads the reference's
 own sequence-parallel state (``hymm.distributed.parallel_states``) and keeps the native
-function for the modes this build does not implement (QVG storage, sparse routing,
-intra-segment action masks, SWA commits, non-bf16 caches).
+function for the modes this build does not implement (QVG storage, sparse routing, SWA
+commits, non-bf16 caches).  Intra-segment action masks run on the B200 path.
 """
 from __future__ import annotations
 
@@ -21,7 +21,7 @@ from . import kv_cache as _kvc
 _INSTALLED = {}
 
 
-def _eligible(kv_cache, update_cache, sparse_context, intra_seg_txt_offsets, intra_seg_vid_windows, cache_txt):
+def _eligible(kv_cache, update_cache, sparse_context):
     fmt = _kvc.cache_format(kv_cache)
     if fmt not in ("none", "int8", _kvc.FP8_FORMAT):
         return False
@@ -30,9 +30,6 @@ def _eligible(kv_cache, update_cache, sparse_context, intra_seg_txt_offsets, int
     if sparse_context is not None:
         return False
     if "swa_capacity" in kv_cache and update_cache:
-        return False
-    if (cache_txt and intra_seg_vid_windows and intra_seg_txt_offsets is not None
-            and any(o is not None for o in intra_seg_txt_offsets)):
         return False
     if not kv_cache["k"].is_cuda:
         return False
@@ -56,8 +53,7 @@ def install(native_module=None):
                 update_cache=False, cache_txt=True, cache_mask=None, intra_seg_txt_offsets=None,
                 intra_seg_vid_windows=None, tokens_per_frame=0, seg_ar_attention_backend="magi",
                 sparse_context=None, sp_metadata=None, attention_metadata=None, **extra):
-        if not _eligible(kv_cache, update_cache, sparse_context, intra_seg_txt_offsets,
-                         intra_seg_vid_windows, cache_txt) or attn_mode == "torch":
+        if not _eligible(kv_cache, update_cache, sparse_context) or attn_mode == "torch":
             patched.stats["fallbacks"] += 1
             return original(q, k, v, kv_cache, cache_valid_len, attn_mode, text_mask, update_cache,
                             cache_txt, cache_mask, intra_seg_txt_offsets, intra_seg_vid_windows,
