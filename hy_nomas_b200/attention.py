@@ -19,9 +19,10 @@ order (``reactor/hy_nomas_cache.py:192-209``, which lacks ``sp_metadata`` and
    input dtypes and reshape to [B, L, H*D] (:874-884).
 
 Intra-segment action masks (``intra_seg_txt_offsets`` / ``intra_seg_vid_windows`` with
-``cache_txt``, :691-770) run in ``intra_seg.py`` on the same kernels.  Modes the reference
-routes elsewhere and this build does not implement raise: ``qvg`` storage,
-``sparse_context`` and SWA commits.
+``cache_txt``, :691-770) run in ``intra_seg.py`` on the same kernels; a cache dict with
+``swa_capacity`` is committed after the attention by ``swa.py`` (bounded history, :593-597,
+:845-852).  Modes the reference routes elsewhere and this build does not implement raise:
+``qvg`` storage, ``sparse_context`` and the archived history samplings of the SWA cache.
 """
 from __future__ import annotations
 
@@ -33,6 +34,7 @@ import torch
 from . import _lib
 from . import kv_cache as kvc
 from . import parallel_states as _ps
+from . import swa as _swa
 
 _BACKENDS = ("magi", "flex", "b200")
 
@@ -239,8 +241,9 @@ def causal_attention_with_cache_mp(
         raise RuntimeError(
             "intra_segment_action_mask cache payload requires attn_mode='flash3', "
             f"got {attn_mode!r}")
-    if "swa_capacity" in kv_cache and update_cache:
-        raise NotImplementedError("b200 cached attention: SWA commit is not implemented; use window.py")
+    swa_commit = bool(update_cache and "swa_capacity" in kv_cache)
+    if swa_commit and kv_cache.get("swa_sampling", "recent") in _swa.ARCHIVED_SAMPLINGS:
+        raise NotImplementedError("b200 cached attention: archived SWA history sampling is not implemented")
 
     get_state, info = _STATE["get_state"], _STATE["info"]
     is_sp = bool(get_state())
@@ -321,6 +324,11 @@ def causal_attention_with_cache_mp(
     if cache_valid_len < 0 or cache_valid_len > cache_shape[1]:
         raise ValueError("Invalid KV valid length")
 
+    if swa_commit:
+        if not cache_txt or cache_mask is None:
+            raise ValueError("SWA requires a masked segment-AR cache write")
+        _swa.check_dense_record(kv_cache, cache_valid_len, img_len, tokens_per_frame)
+
     # ---- cache write (validated before either payload is touched)
     # A window ring cache is written after the attention has staged its history (the slot a new
     # frame takes may hold the oldest frame this call still attends).
@@ -329,7 +337,7 @@ def causal_attention_with_cache_mp(
         raise NotImplementedError("a ring cache without its SinkWindowKVCache cannot be written")
     if update_cache and window is not None and cache_txt and txt_k.shape[1] > 0:
         raise NotImplementedError("window caches hold whole image frames; pass cache_txt=False")
-    if update_cache and window is None:
+    if update_cache and window is None and not swa_commit:
         seg_k = [img_k, txt_k] if cache_txt else [img_k]
         seg_v = [img_v, txt_v] if cache_txt else [img_v]
         write_tokens = sum(t.shape[1] for t in seg_k)
@@ -387,6 +395,15 @@ def causal_attention_with_cache_mp(
             history_mask=history_mask, text_mask=cur_txt_mask, attend_txt=attend_txt,
             group_tokens=group_tokens, out_img=o_send, out_img_strides=out_img_strides, hist_rows=hist_rows)
     stats["calls"] += 1
+    if swa_commit:
+        # the bounded history is committed after the attention has read the old rows
+        write_mask = torch.ones(B, img_len + txt_len, dtype=torch.bool, device=img_q.device)
+        if cur_txt_mask is not None:
+            write_mask[:, img_len:] = cur_txt_mask
+        _swa.append_dense_record(kv_cache, cache_valid_len, img_len, txt_len, tokens_per_frame)
+        _swa.commit_window(kv_cache, cache_mask, [img_k.detach(), txt_k.detach()], [img_v.detach(), txt_v.detach()],
+                           write_mask, cache_valid_len, assume_finite=_assume_finite())
+        stats["writes"] += 1
     if update_cache and window is not None:
         window.append(img_k.detach(), img_v.detach(), assume_finite=_assume_finite())
         stats["writes"] += 1

@@ -6,8 +6,9 @@ attribute ``hymm.models.dit.nomas_cpt.causal_attention_with_cache_mp`` is replac
 ``MMDoubleStreamBlock.forward_with_cache`` (nomas_cpt.py:1398-1416) and the TP block
 (modules/tensor_parallel.py:180) call the B200 path.  The replacement reads the reference's
 own sequence-parallel state (``hymm.distributed.parallel_states``) and keeps the native
-function for the modes this build does not implement (QVG storage, sparse routing, SWA
-commits, non-bf16 caches).  Intra-segment action masks run on the B200 path.
+function for the modes this build does not implement (QVG storage, sparse routing, the
+archived history samplings of the SWA cache, non-bf16 caches).  Intra-segment action masks
+and the bounded ("recent") SWA history run on the B200 path.
 """
 from __future__ import annotations
 
@@ -17,6 +18,7 @@ import torch
 
 from . import attention as _att
 from . import kv_cache as _kvc
+from . import swa as _swa
 
 _INSTALLED = {}
 
@@ -29,7 +31,8 @@ def _eligible(kv_cache, update_cache, sparse_context):
         return False
     if sparse_context is not None:
         return False
-    if "swa_capacity" in kv_cache and update_cache:
+    if ("swa_capacity" in kv_cache and update_cache
+            and kv_cache.get("swa_sampling", "recent") in _swa.ARCHIVED_SAMPLINGS):
         return False
     if not kv_cache["k"].is_cuda:
         return False

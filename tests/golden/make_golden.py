@@ -32,6 +32,11 @@ its inputs and the reference's outputs (bf16 as int16 bit patterns, e4m3 as uint
                         the kernels' rectangle-union semantics (overlaps refused, rows without
                         ranges zero, fp32 softmax, bf16 output) takes its place, and the ranges
                         the reference built are stored as a dense visibility per sample
+  swa_<fmt>_<case>.npz  bounded segment-AR history (sliding-window cache): a sequence of
+                        causal_attention_with_cache_mp(attn_mode="torch", update_cache=True)
+                        calls on a cache dict with ``swa_capacity`` (nomas_cpt.py:593-597,
+                        :845-852 -> swa_cache.append_dense_record / commit_window), with the
+                        outputs, cache rows, mask, records and lengths after every call
 """
 from __future__ import annotations
 
@@ -418,11 +423,69 @@ def make_intra_seg():
     run_case("nohist_update", 1, 0, [], 16, 3, [[1, 1, 1, 1]], [[0, 2, 3]], [[0, 2, 1], [2, 3, 0]], True, 43)
 
 
+
+def make_swa():
+    """Sliding-window (bounded) history through the reference: one call per segment with
+    ``update_cache=True``; every call's inputs, outputs and the cache state it leaves."""
+    native = importlib.import_module("hymm.models.dit.nomas_cpt")
+    i8 = importlib.import_module("hymm.models.dit.modules.int8_kv_cache")
+    H, D, T, Lt = 2, 128, 16, 3
+
+    def run(name, fmt, capacity, frames_per_call, text_masks, seed):
+        gen = torch.Generator().manual_seed(seed)
+        cap = capacity + 8
+        if fmt == "int8":
+            cache = i8.make_int8_kv_block(1, cap, H, D, device="cpu")
+        else:
+            cache = {"k": torch.zeros(1, cap, H, D, dtype=torch.bfloat16),
+                     "v": torch.zeros(1, cap, H, D, dtype=torch.bfloat16)}
+        cache["swa_capacity"] = capacity
+        mask = torch.zeros(1, cap, dtype=torch.bool)
+        valid = 0
+        d = {"capacity": capacity, "steps": len(frames_per_call), "cap": cap}
+        for i, (nf, tm) in enumerate(zip(frames_per_call, text_masks)):
+            args = [seeded((1, L, H, D), gen) for L in (nf * T, Lt) for _ in range(3)]
+            tmask = torch.tensor([tm], dtype=torch.bool)
+            with torch.no_grad():
+                out = native.causal_attention_with_cache_mp(
+                    (args[0], args[3]), (args[1], args[4]), (args[2], args[5]), cache, cache_valid_len=valid,
+                    attn_mode="torch", text_mask=tmask, update_cache=True, cache_txt=True, cache_mask=mask,
+                    tokens_per_frame=T)
+            valid_before, valid = valid, int(cache["swa_valid_len"])
+            recs = [[r.start, r.image_tokens, r.end, r.time_start, r.height, r.width] for r in cache["swa_video"]]
+            for j, n in enumerate(("img_q", "img_k", "img_v", "txt_q", "txt_k", "txt_v")):
+                d[f"{i}_{n}"] = bf(args[j])
+            d[f"{i}_text_mask"] = tmask.numpy()
+            d[f"{i}_valid_before"] = valid_before
+            d[f"{i}_out_img"] = bf(out[0].reshape(1, nf * T, H, D))
+            d[f"{i}_out_txt"] = bf(out[1].reshape(1, Lt, H, D))
+            d[f"{i}_valid_after"] = valid
+            d[f"{i}_evicted"] = int(cache["swa_evicted"])
+            d[f"{i}_records"] = np.array(recs, dtype=np.int64).reshape(-1, 6)
+            d[f"{i}_next_frame"] = int(cache["swa_next_frame"])
+            d[f"{i}_mask"] = mask.numpy().copy()
+            for key in ("k", "v", "k_scale", "v_scale"):
+                if key in cache:
+                    t = cache[key][:, :valid]
+                    d[f"{i}_{key}"] = bf(t.clone()) if t.dtype == torch.bfloat16 else t.numpy().copy()
+        np.savez_compressed(HERE / f"swa_{fmt}_{name}.npz", **d)
+
+    # whole records, then one frame of a record (its text kept), then a record and a frame
+    frames, masks = [2, 2, 3, 1, 2], [[1, 1, 1], [1, 1, 0], [1, 0, 1], [1, 1, 1], [0, 1, 1]]
+    run("evict", "int8", 90, frames, masks, 51)
+    run("evict", "bf16", 90, frames, masks, 52)
+    # a chunk larger than the budget: the cut reaches into the current chunk
+    run("overflow", "int8", 40, [2, 3, 1], [[1, 1, 1], [1, 1, 0], [1, 1, 1]], 53)
+
+
 def main():
     _install_stub()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     if "--only-intra" in sys.argv:
         make_intra_seg()
+        return
+    if "--only-swa" in sys.argv:
+        make_swa()
         return
     if "--only-late" not in sys.argv:
         make_quant()
@@ -432,6 +495,7 @@ def main():
     make_sp()
     make_config1()
     make_intra_seg()
+    make_swa()
     print("fixtures written to", HERE)
 
 

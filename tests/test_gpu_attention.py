@@ -497,3 +497,48 @@ def test_intra_segment_long_history_block_causal(cuda_lib):
     assert_close(out_txt.reshape(o_txt.shape), o_txt, "long intra text", m_txt)
     assert torch.all(out_txt.reshape(o_txt.shape).cpu()[0, 30:] == 0)
 
+
+
+@pytest.mark.parametrize("name", ["swa_int8_evict", "swa_bf16_evict", "swa_int8_overflow"])
+def test_swa_history_sequence_matches_reference(cuda_lib, name):
+    """A sequence of cache-writing calls on a bounded (``swa_capacity``) history: after every
+    call the outputs match the reference's, and the cache rows (bit for bit), the mask, the
+    records, ``swa_valid_len`` and ``swa_evicted`` are the ones the reference's commit left."""
+    g = load_golden(f"{name}.npz")
+    dev = torch.device("cuda")
+    cap = int(g["cap"])
+    H, D = g["0_img_k"].shape[2:]
+    if "int8" in name:
+        cache = kvc.make_int8_kv_block(1, cap, H, D, device=dev)
+    else:
+        cache = {"k": torch.zeros(1, cap, H, D, dtype=torch.bfloat16, device=dev),
+                 "v": torch.zeros(1, cap, H, D, dtype=torch.bfloat16, device=dev)}
+    cache["swa_capacity"] = int(g["capacity"])
+    mask = torch.zeros(1, cap, dtype=torch.bool, device=dev)
+    valid = 0
+    for i in range(int(g["steps"])):
+        x = {n: bf16(g[f"{i}_{n}"]).to(dev) for n in ("img_q", "img_k", "img_v", "txt_q", "txt_k", "txt_v")}
+        with torch.no_grad():
+            out_img, out_txt = hatt.causal_attention_with_cache_mp(
+                (x["img_q"], x["txt_q"]), (x["img_k"], x["txt_k"]), (x["img_v"], x["txt_v"]), cache,
+                cache_valid_len=valid, attn_mode="flash3", text_mask=torch.from_numpy(g[f"{i}_text_mask"]).to(dev),
+                update_cache=True, cache_txt=True, cache_mask=mask, tokens_per_frame=16)
+        torch.cuda.synchronize()
+        ref_img, ref_txt = bf16(g[f"{i}_out_img"]).float(), bf16(g[f"{i}_out_txt"]).float()
+        out_img = out_img.reshape(ref_img.shape).float().cpu()
+        out_txt = out_txt.reshape(ref_txt.shape).float().cpu()
+        assert ((out_img - ref_img).abs() <= ATOL + 1e-2 * ref_img.abs()).all(), f"step {i} image"
+        valid_t = torch.from_numpy(g[f"{i}_text_mask"])[0]
+        assert ((out_txt[0, valid_t] - ref_txt[0, valid_t]).abs() <= ATOL + 1e-2 * ref_txt[0, valid_t].abs()).all()
+        assert torch.all(out_txt[0, ~valid_t] == 0)
+        valid = cache["swa_valid_len"]
+        assert valid == int(g[f"{i}_valid_after"]) and cache["swa_evicted"] == int(g[f"{i}_evicted"])
+        for key in ("k", "v", "k_scale", "v_scale"):
+            if f"{i}_{key}" not in g:
+                continue
+            got = cache[key][:, :valid].cpu()
+            got = got.view(torch.int16) if got.dtype == torch.bfloat16 else got
+            assert np.array_equal(got.numpy().view(np.uint8), g[f"{i}_{key}"].view(np.uint8)), f"step {i} {key}"
+        assert np.array_equal(mask.cpu().numpy(), g[f"{i}_mask"])
+        recs = [[r.start, r.image_tokens, r.end, r.time_start, r.height, r.width] for r in cache["swa_video"]]
+        assert recs == g[f"{i}_records"].tolist()
