@@ -7,8 +7,9 @@ time per call on one GPU and ~0.5 ms with sequence parallelism, more than the de
 loop has two) and replays it afterwards: the same kernels, collectives and cache writes on the
 same buffers, with one launch from the host.  Calls must be graph-capturable: no host sync
 inside (set ``HYB_ASSUME_FINITE_KV=1`` so the finite check of cache writes stays on the
-device), static shapes, and the same Python-side state on every call (a window cache, which
-advances its ring on every call, cannot be replayed this way).
+device), static shapes, and the same Python-side state on every call: a window cache, which
+advances its ring on every call, and a cache write to a bounded (``swa_capacity``) history,
+whose records and valid length move on every commit, cannot be replayed this way.
 """
 from __future__ import annotations
 
