@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-timeline", action="store_true",
+                    help="after the measurement, one more pass of the end-to-end loop with CUDA events around "
+                         "each upload / compute / read-back, and the host link alone; printed to stderr")
     ap.add_argument("--ring-schedule", default="allgather", choices=["allgather", "ring"],
                     help="ring workload: every block to every rank over peer memory, or neighbour passing")
     ap.add_argument("--no-graph", action="store_true",
@@ -147,13 +150,15 @@ def capture_step(step_fn, device):
     return graph
 
 
-def e2e_pipelined(step_fn, host_in, device, steps, warmup, world, static_outputs=False):
+def e2e_pipelined(step_fn, host_in, device, steps, warmup, world, static_outputs=False, log=None):
     """Mean ms per step through the public call with host buffers: every step copies its
     inputs from pinned host memory (H2D stream) and reads its outputs back into pinned host
     memory (D2H stream); inputs are double-buffered so that step i+1's copies overlap step
     i's compute.  With ``static_outputs`` (a graphed call returns the same output tensors for
     a buffer set) a step also waits until the read-back of step i-2 has finished.
-    Device-timed on the caller's stream, max over ranks."""
+    Device-timed on the caller's stream, max over ranks.  With ``log`` (a list), every timed
+    step appends a dict of timing events around its upload, compute and read-back, and the
+    region's start event is appended first."""
     import torch.distributed as dist
     compute = torch.cuda.current_stream(device)
     h2d = torch.cuda.Stream(device=device)
@@ -162,38 +167,53 @@ def e2e_pipelined(step_fn, host_in, device, steps, warmup, world, static_outputs
     host_out = [None, None]
     out_bytes = [0]
 
-    def run(n, start_event=None):
+    def ev(rec, name, stream):
+        if rec is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            rec[name] = e
+
+    def run(n, start_event=None, timeline=None):
         free = [None, None]
         read_back = [None, None]
         for i in range(n):
             j = i % 2
+            rec = {} if timeline is not None else None
             with torch.cuda.stream(h2d):
                 if i == 0 and start_event is not None:
                     h2d.wait_event(start_event)
                 if free[j] is not None:
                     h2d.wait_event(free[j])
+                ev(rec, "up0", h2d)
                 for d_, h_ in zip(dev_in[j], host_in):
                     d_.copy_(h_, non_blocking=True)
                 copied = torch.cuda.Event()
                 copied.record(h2d)
+                ev(rec, "up1", h2d)
             compute.wait_event(copied)
             if static_outputs and read_back[j] is not None:
                 compute.wait_event(read_back[j])
+            ev(rec, "c0", compute)
             outs = step_fn(*dev_in[j])
             done = torch.cuda.Event()
             done.record(compute)
+            ev(rec, "c1", compute)
             free[j] = done
             if host_out[j] is None:
                 host_out[j] = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
                 out_bytes[0] = sum(o.numel() * o.element_size() for o in outs)
             with torch.cuda.stream(d2h):
                 d2h.wait_event(done)
+                ev(rec, "down0", d2h)
                 for h_, o in zip(host_out[j], outs):
                     h_.copy_(o, non_blocking=True)
                     o.record_stream(d2h)
-                ev = torch.cuda.Event()
-                ev.record(d2h)
-                read_back[j] = ev
+                back = torch.cuda.Event()
+                back.record(d2h)
+                ev(rec, "down1", d2h)
+                read_back[j] = back
+            if timeline is not None:
+                timeline.append(rec)
         compute.wait_stream(h2d)
         compute.wait_stream(d2h)
 
@@ -204,7 +224,9 @@ def e2e_pipelined(step_fn, host_in, device, steps, warmup, world, static_outputs
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(compute)
-    run(steps, start_event=e0)
+    if log is not None:
+        log.append(e0)
+    run(steps, start_event=e0, timeline=log)
     e1.record(compute)
     torch.cuda.synchronize(device)
     ems = e0.elapsed_time(e1) / steps
@@ -267,6 +289,47 @@ def build_problem(rank, world, device, hist_frames=HIST_FRAMES):
     cache_mask = torch.zeros(1, cap, dtype=torch.bool, device=device)
     cache_mask[:, :Lh] = True
     return dict(cache=cache, img=img, txt=txt, cache_mask=cache_mask, Lh=Lh, Li=Li, Ls=Ls, Hl=Hl)
+
+
+
+def print_e2e_timeline(step_fn, host_in, device, steps, world, rank, static_outputs):
+    """One more pass of the end-to-end loop with CUDA events around every upload, compute and
+    read-back, then the host link alone (the step's uploads with nothing else running);
+    printed to stderr.  Every rank runs it (the loop holds collectives)."""
+    log = []
+    ems, _, _ = e2e_pipelined(step_fn, host_in, device, steps, 0, world, static_outputs, log=log)
+    dev_in = [torch.empty_like(t, device=device) for t in host_in]
+    stream = torch.cuda.current_stream(device)
+
+    def upload():
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+
+    for _ in range(3):
+        upload()
+    torch.cuda.synchronize(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(5):
+        upload()
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    up_ms = a.elapsed_time(b) / 5
+    if rank != 0:
+        return
+    t0 = log[0]
+    out = sys.stderr
+    nbytes = sum(t.numel() * t.element_size() for t in host_in)
+    print(f"e2e timeline: {ems:.3f} ms per step over {steps} steps; times in ms from the region's start", file=out)
+    for i, r in enumerate(log[1:]):
+        def at(k, r=r):
+            return t0.elapsed_time(r[k])
+        print(f"  step {i:3d}  upload {at('up0'):8.3f}-{at('up1'):8.3f} ({at('up1') - at('up0'):6.3f})  "
+              f"compute {at('c0'):8.3f}-{at('c1'):8.3f} ({at('c1') - at('c0'):6.3f})  "
+              f"read-back {at('down0'):8.3f}-{at('down1'):8.3f} ({at('down1') - at('down0'):6.3f})", file=out)
+    print(f"  the step's uploads alone: {up_ms:.3f} ms for {nbytes / 1e6:.1f} MB = {nbytes / up_ms / 1e6:.1f} GB/s",
+          file=out)
 
 
 def run_b200(args):
@@ -343,6 +406,8 @@ def run_b200(args):
     call = step if args.no_graph else GraphedCall(step, device)
     ems, h2d, d2h = e2e_pipelined(call, host_in, device, args.steps, args.warmup, world,
                                   static_outputs=not args.no_graph)
+    if args.e2e_timeline:
+        print_e2e_timeline(call, host_in, device, args.steps, world, rank, static_outputs=not args.no_graph)
 
     # ---- dominant kernel alone: the tcgen05 attention launch over the staged buffers
     kern = time_attention_kernel(prob, device, args.steps)
