@@ -215,3 +215,14 @@ def test_peer_exchange_needs_equal_lengths_and_divisible_heads(monkeypatch):
     assert not comm.peer_exchange_enabled((780,), 24)           # one rank: no exchange
     monkeypatch.setenv("HYB_PEER_EXCHANGE", "0")
     assert not comm.peer_exchange_enabled((780,) * 8, 24)
+
+
+def test_installer_keeps_swa_writes_on_the_b200_path_except_archived_sampling():
+    fake = types.SimpleNamespace(dtype=torch.bfloat16, is_cuda=True)   # a device tensor's two attributes
+    recent = {"k": fake, "v": fake, "swa_capacity": 64}
+    assert hinst._eligible(recent, True, None)
+    for sampling in ("uniform", "recent_mix_uniform", "temporal_context"):
+        archived = dict(recent, swa_sampling=sampling)
+        assert not hinst._eligible(archived, True, None)
+        assert hinst._eligible(archived, False, None)     # reads of an archived history stay here
+    assert not hinst._eligible(recent, True, {"config": {}})   # sparse routing goes to the native path
