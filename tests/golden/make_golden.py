@@ -1,10 +1,9 @@
 #!/usr/bin/env python
 """Generate the golden fixtures of tests/golden/ by running the Hy-Nomas reference.
 
-Run in a container that has the reference checkout (default ``/root/reference``,
-override with ``HY_NOMAS_REF``):
+Run where the reference checkout is available, with ``HY_NOMAS_REF`` naming it:
 
-    python tests/golden/make_golden.py
+    HY_NOMAS_REF=<reference checkout> python tests/golden/make_golden.py
 
 The reference's DiT module imports ``diffusers`` only for two base classes; a 10-line
 stub package written to a temporary directory stands in for it.  Every fixture stores
@@ -52,10 +51,12 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("HY_NOMAS_REF", "/root/reference"))
 
 
 def _install_stub() -> None:
+    ref = os.environ.get("HY_NOMAS_REF")
+    if not ref or not (Path(ref) / "hymm").is_dir():
+        raise SystemExit("set HY_NOMAS_REF to the Hy-Nomas reference checkout (the directory holding hymm/)")
     stub = Path(tempfile.mkdtemp(prefix="hyb_stub_"))
     (stub / "diffusers" / "models").mkdir(parents=True)
     (stub / "diffusers" / "__init__.py").write_text("")
@@ -64,7 +65,7 @@ def _install_stub() -> None:
     (stub / "diffusers" / "configuration_utils.py").write_text(
         "class ConfigMixin:\n    pass\ndef register_to_config(fn):\n    return fn\n")
     sys.path.insert(0, str(stub))
-    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(Path(ref)))
     sys.path.insert(0, str(REPO))
 
 
