@@ -57,11 +57,21 @@ def install(native_module=None):
                 intra_seg_vid_windows=None, tokens_per_frame=0, seg_ar_attention_backend="magi",
                 sparse_context=None, sp_metadata=None, attention_metadata=None, **extra):
         if not _eligible(kv_cache, update_cache, sparse_context) or attn_mode == "torch":
+            if extra.get("chunk_causal_frames"):
+                raise NotImplementedError(
+                    "chunk_causal_frames (frame-level block-causal chunks) runs on the b200 path only; "
+                    "this call would fall back to the reference, which has no such mask")
             patched.stats["fallbacks"] += 1
+            # The reactor's CacheStaging (reactor/hy_nomas_cache.py:192-209), which may sit behind
+            # this patch, takes the older signature without the last two arguments.
+            newer = {}
+            if sp_metadata is not None:
+                newer["sp_metadata"] = sp_metadata
+            if attention_metadata is not None:
+                newer["attention_metadata"] = attention_metadata
             return original(q, k, v, kv_cache, cache_valid_len, attn_mode, text_mask, update_cache,
                             cache_txt, cache_mask, intra_seg_txt_offsets, intra_seg_vid_windows,
-                            tokens_per_frame, seg_ar_attention_backend, sparse_context,
-                            sp_metadata, attention_metadata)
+                            tokens_per_frame, seg_ar_attention_backend, sparse_context, **newer)
         patched.stats["calls"] += 1
         return _att.causal_attention_with_cache_mp(
             q, k, v, kv_cache, cache_valid_len, attn_mode, text_mask, update_cache, cache_txt,

@@ -226,3 +226,33 @@ def test_installer_keeps_swa_writes_on_the_b200_path_except_archived_sampling():
         assert not hinst._eligible(archived, True, None)
         assert hinst._eligible(archived, False, None)     # reads of an archived history stay here
     assert not hinst._eligible(recent, True, {"config": {}})   # sparse routing goes to the native path
+
+
+def test_fallback_reaches_an_original_with_the_older_signature():
+    """The reactor's CacheStaging (15 parameters, no sp_metadata / attention_metadata) may be the
+    function this patch wraps; fallbacks must reach it, and the frame-causal extension must not
+    be dropped silently on the way."""
+    calls = []
+
+    def staging(q, k, v, kv_cache, cache_valid_len=0, attn_mode=None, text_mask=None, update_cache=False,
+                cache_txt=True, cache_mask=None, intra_seg_txt_offsets=None, intra_seg_vid_windows=None,
+                tokens_per_frame=0, seg_ar_attention_backend="magi", sparse_context=None):
+        calls.append((cache_valid_len, attn_mode, tokens_per_frame))
+        return "staging"
+
+    mod = types.SimpleNamespace(causal_attention_with_cache_mp=staging,
+                                get_sequence_parallel_state=lambda: False,
+                                nccl_info=types.SimpleNamespace(sp_group=None, rank_within_spgroup=0))
+    hinst.install(mod)
+    try:
+        patched = mod.causal_attention_with_cache_mp
+        x = torch.zeros(1, 2, 2, 128, dtype=torch.bfloat16)
+        cache = {"k": torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16), "v": torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)}
+        assert patched((x, x), (x, x), (x, x), cache, 0, "flash3", tokens_per_frame=16,
+                       sp_metadata=None, attention_metadata=None) == "staging"
+        assert calls == [(0, "flash3", 16)]
+        with pytest.raises(NotImplementedError, match="chunk_causal_frames"):
+            patched((x, x), (x, x), (x, x), cache, 0, "flash3", tokens_per_frame=16, chunk_causal_frames=1)
+    finally:
+        hinst.uninstall(mod)
+    hatt.set_parallel_state_provider(hatt._ps.get_sequence_parallel_state, hatt._ps.nccl_info)
