@@ -231,6 +231,11 @@ def causal_attention_with_cache_mp(
     """Multi-prompt causal attention with KV cache on B200 (see module docstring)."""
     if seg_ar_attention_backend not in _BACKENDS:
         raise ValueError("Invalid seg_ar_attention_backend")
+    # "flash3" and "torch" are the reference's cached-path modes (nomas_cpt.py:771-838); both run
+    # with flash3's semantics here (padded text queries give zero rows, the cache mask always
+    # applies), and None selects them too.
+    if attn_mode not in (None, "flash3", "torch"):
+        raise ValueError(f"Unsupported attn_mode for KV cache: {attn_mode}")
     if seg_ar_attention_backend == "flex" and torch.is_grad_enabled():
         raise RuntimeError("Flex cached attention requires no-grad inference")
     if sparse_context is not None:

@@ -49,6 +49,8 @@ def test_drop_in_validates_before_touching_the_device():
     cache = {"k": torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16), "v": torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)}
     with pytest.raises(ValueError, match="seg_ar_attention_backend"):
         hatt.causal_attention_with_cache_mp((x, x), (x, x), (x, x), cache, seg_ar_attention_backend="bogus")
+    with pytest.raises(ValueError, match="Unsupported attn_mode for KV cache: sdpa"):
+        hatt.causal_attention_with_cache_mp((x, x), (x, x), (x, x), cache, attn_mode="sdpa")
     with pytest.raises(NotImplementedError):
         hatt.causal_attention_with_cache_mp((x, x), (x, x), (x, x), cache, sparse_context={"config": {}})
     i8 = kvc.make_int8_kv_block(1, 4, 2, 128, device="cpu")
