@@ -258,3 +258,34 @@ def test_fallback_reaches_an_original_with_the_older_signature():
     finally:
         hinst.uninstall(mod)
     hatt.set_parallel_state_provider(hatt._ps.get_sequence_parallel_state, hatt._ps.nccl_info)
+
+
+def test_kv_cache_errors_are_the_reference_ones_and_write_nothing():
+    """Exception types and messages of the reference's INT8 cache API
+    (hymm/models/dit/modules/int8_kv_cache.py:114-181), raised before anything is written."""
+    cache = kvc.make_int8_kv_block(1, 8, 2, 128, device="cpu")
+    before = {k: v.clone() for k, v in cache.items() if torch.is_tensor(v)}
+    x = torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="^K/V shapes, dtypes, and devices must match$"):
+        kvc.quantize_kv_pair_into(cache, x, x[:, :3], 0)
+    for bad, start in ((torch.zeros(2, 4, 2, 128, dtype=torch.bfloat16), 0),   # batch
+                       (x, 5),                                                   # capacity
+                       (x, -1),
+                       (x.float(), 0)):                                          # dtype
+        with pytest.raises(ValueError, match="^KV pair shape, capacity, dtype, or device mismatch$"):
+            kvc.quantize_kv_pair_into(cache, bad, bad, start)
+    with pytest.raises(ValueError, match="^Invalid KV key: q$"):
+        kvc.quantize_kv_into(cache, "q", x, 0)
+    with pytest.raises(TypeError, match="^KV quantization expects \\[B,L,H,D\\] BF16 values$"):
+        kvc.quantize_kv_into(cache, "k", x.float(), 0)
+    with pytest.raises(ValueError, match="^KV quantization shape, capacity, or device mismatch$"):
+        kvc.quantize_kv_into(cache, "k", x, 6)
+    wrong_scale = dict(cache, k_scale=torch.ones(1, 8, 2, 2))
+    with pytest.raises(ValueError, match="^INT8 KV scale shape/device mismatch$"):
+        kvc.quantize_kv_into(wrong_scale, "k", x, 0)
+    with pytest.raises(TypeError, match="FP32 scale are required"):
+        kvc.quantize_kv_into(dict(cache, k_scale=cache["k_scale"].double()), "k", x, 0)
+    with pytest.raises(ValueError, match="^Invalid KV valid length$"):
+        kvc.dequantize_kv(cache, "k", 9)
+    for k, v in before.items():
+        assert torch.equal(cache[k], v)
