@@ -54,6 +54,16 @@ def _assume_finite() -> bool:
     return os.environ.get("HYB_ASSUME_FINITE_KV", "0") == "1"
 
 
+def _kernel_layout(x: torch.Tensor) -> torch.Tensor:
+    """The kernels read [B, L, H, D] rows with a unit stride on head_dim, 16-byte aligned.
+    The reference accepts any layout, so a tensor in another one is copied once into that form
+    (the DiT's projections already have it, and pass through untouched)."""
+    st = x.stride()
+    if st[-1] == 1 and x.data_ptr() % 16 == 0 and all(s % 8 == 0 for s in st[:-1]):
+        return x
+    return x.clone(memory_format=torch.contiguous_format)
+
+
 def _new_out(B, L, H, D, device):
     return torch.empty((B, L, H, D), dtype=torch.bfloat16, device=device)
 
@@ -257,6 +267,8 @@ def causal_attention_with_cache_mp(
     img_q, txt_q = q
     img_k, txt_k = k
     img_v, txt_v = v
+    img_q, txt_q, img_k, txt_k, img_v, txt_v = (
+        _kernel_layout(x) for x in (img_q, txt_q, img_k, txt_k, img_v, txt_v))
     img_output_dtype = img_q.dtype
     txt_output_dtype = txt_q.dtype
 

@@ -289,3 +289,16 @@ def test_kv_cache_errors_are_the_reference_ones_and_write_nothing():
         kvc.dequantize_kv(cache, "k", 9)
     for k, v in before.items():
         assert torch.equal(cache[k], v)
+
+
+def test_inputs_in_other_layouts_are_copied_once_into_kernel_rows():
+    x = torch.randn(1, 6, 2, 128).to(torch.bfloat16)
+    assert hatt._kernel_layout(x) is x                                   # the DiT's layout passes through
+    assert hatt._kernel_layout(x[:, 2:]) is not None and hatt._kernel_layout(x[:, 2:]).data_ptr() == x[:, 2:].data_ptr()
+    t = x.transpose(2, 3).contiguous().transpose(2, 3)                  # head_dim not the unit stride
+    y = hatt._kernel_layout(t)
+    assert y.stride(-1) == 1 and torch.equal(y, t)
+    flat = torch.randn(1 * 6 * 2 * 128 + 1).to(torch.bfloat16)
+    odd = flat[1:].view(1, 6, 2, 128)                                    # contiguous but 2 bytes off
+    z = hatt._kernel_layout(odd)
+    assert z.data_ptr() % 16 == 0 and torch.equal(z, odd)
