@@ -248,6 +248,14 @@ def check_device_status(device: torch.device, reset: bool = True) -> None:
         raise ValueError("Cannot quantize non-finite KV values")
 
 
+def require_same_device(device: torch.device, what: str, *tensors) -> None:
+    """Every tensor the kernels will read or write through a raw pointer must live on ``device``
+    (a host tensor's pointer would be dereferenced on the GPU).  None entries are skipped."""
+    for t in tensors:
+        if t is not None and t.device != device:
+            raise RuntimeError(f"{what} must be on the same device: found {t.device}, expected {device}")
+
+
 def require_device(t: torch.Tensor) -> None:
     if not t.is_cuda:
         raise RuntimeError("hy_nomas_b200 kernels need CUDA tensors (no CPU path)")

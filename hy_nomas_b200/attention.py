@@ -130,6 +130,9 @@ def cached_attention_local(
     else:
         raise ValueError(f"b200 cached attention does not support {fmt_name!r} storage")
     cache_batch = kv_cache["k"].shape[0]
+    _lib.require_same_device(dev, "cached attention tensors", img_k, img_v, txt_q, txt_k, txt_v, kv_cache["k"],
+                             kv_cache["v"], history_mask, text_mask, hist_rows, out_img, out_txt, lse,
+                             *(kv_cache[n] for n in ("k_scale", "v_scale") if torch.is_tensor(kv_cache.get(n))))
     if out_img is None:
         out_img = _new_out(B, Li, H, D, dev)
     if out_txt is None:
@@ -288,6 +291,9 @@ def causal_attention_with_cache_mp(
             "Current Q and KV cache must be on the same device: "
             f"img_q={img_q.device}, txt_q={txt_q.device}, cache={cache_device}")
     _lib.require_device(img_q)
+    _lib.require_same_device(cache_device, "Current Q/K/V, masks and KV cache", img_k, img_v, txt_k, txt_v,
+                             text_mask, cache_mask, kv_cache.get("history_rows"),
+                             *(kv_cache[n] for n in ("k_scale", "v_scale") if torch.is_tensor(kv_cache.get(n))))
 
     from . import communications as comm
 

@@ -302,3 +302,19 @@ def test_inputs_in_other_layouts_are_copied_once_into_kernel_rows():
     odd = flat[1:].view(1, 6, 2, 128)                                    # contiguous but 2 bytes off
     z = hatt._kernel_layout(odd)
     assert z.data_ptr() % 16 == 0 and torch.equal(z, odd)
+
+
+def test_tensors_on_another_device_are_refused_before_any_kernel():
+    """A tensor on another device would hand the kernels a pointer they cannot dereference;
+    the reference fails on such inputs in torch's own device checks, this build before any
+    launch."""
+    from hy_nomas_b200 import _lib
+    elsewhere = torch.empty(1, 4, dtype=torch.bool, device="meta")
+    _lib.require_same_device(torch.device("cpu"), "x", torch.zeros(1), None)
+    with pytest.raises(RuntimeError, match="must be on the same device"):
+        _lib.require_same_device(torch.device("cpu"), "x", torch.zeros(1), elsewhere)
+    x = torch.zeros(1, 16, 2, 128, dtype=torch.bfloat16)
+    t = torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)
+    cache = {"k": torch.zeros(1, 32, 2, 128, dtype=torch.bfloat16), "v": torch.zeros(1, 32, 2, 128, dtype=torch.bfloat16)}
+    with pytest.raises(RuntimeError, match="must be on the same device"):
+        hatt.cached_attention_local(x, x, x, t, t, t, cache, 0, text_mask=elsewhere)
