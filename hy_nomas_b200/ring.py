@@ -240,6 +240,7 @@ class RingAttention:
             raise ValueError(f"ring shard must be [1, {Ls}, {H}, {_D}] on rank {r}")
         if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
             raise ValueError("ring attention takes bf16 q/k/v")
+        _lib.require_same_device(dev, "ring q/k/v and outputs", q, k, v, out, lse)
         out = out if out is not None else torch.empty_like(q)
         ranks = dist.get_process_group_ranks(group) if (P > 1 and group is not None) else list(range(P))
         nxt, prv = ranks[(r + 1) % P], ranks[(r - 1) % P]
@@ -412,6 +413,7 @@ class GatherAttention:
             raise ValueError(f"ring shard must be [1, {Ls}, {H}, {_D}] on rank {self.rank}")
         if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
             raise ValueError("ring attention takes bf16 q/k/v")
+        _lib.require_same_device(dev, "ring q/k/v and outputs", q, k, v, out, lse)
         out = out if out is not None else torch.empty_like(q)
         self.launches = 0
         if Ls == 0:
