@@ -250,7 +250,11 @@ def check_device_status(device: torch.device, reset: bool = True) -> None:
 
 def require_same_device(device: torch.device, what: str, *tensors) -> None:
     """Every tensor the kernels will read or write through a raw pointer must live on ``device``
-    (a host tensor's pointer would be dereferenced on the GPU).  None entries are skipped."""
+    (a host tensor's pointer would be dereferenced on the GPU).  None entries are skipped; a
+    CUDA device given without an index means the current one."""
+    device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     for t in tensors:
         if t is not None and t.device != device:
             raise RuntimeError(f"{what} must be on the same device: found {t.device}, expected {device}")
