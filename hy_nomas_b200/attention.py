@@ -146,11 +146,22 @@ def cached_attention_local(
     ws_obj = workspace if isinstance(workspace, Workspace) else None
     workspace = ws_obj.get(int(ws_bytes), dev) if ws_obj is not None else \
         torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=dev)
+    # The kernels read the masks through raw pointers for every row of this call's geometry, so
+    # their shapes are checked here (the reference fails on the same inputs in torch's shape
+    # checks); a one-row history mask over a batched cache is broadcast, as SDPA broadcasts it.
     if history_mask is not None:
         history_mask = history_mask.to(torch.bool)
+        need = kv_cache["k"].shape[1] if hist_rows is not None else cache_valid_len
+        if history_mask.ndim != 2 or history_mask.shape[0] not in (1, cache_batch) or history_mask.shape[1] < need:
+            raise ValueError(f"history mask must be bool [1 or {cache_batch}, >= {need}], "
+                             f"got {tuple(history_mask.shape)}")
         if history_mask.stride(-1) != 1:
             history_mask = history_mask.contiguous()
+        if history_mask.shape[0] != cache_batch:
+            history_mask = history_mask.expand(cache_batch, -1)
     if text_mask is not None:
+        if Lt > 0 and tuple(text_mask.shape) != (B, Lt):
+            raise ValueError(f"text mask must be bool [{B}, {Lt}], got {tuple(text_mask.shape)}")
         text_mask = text_mask.to(torch.bool).contiguous()
     empty = _lib.Tensor4()
     args = _lib.CachedAttnArgs()

@@ -318,3 +318,18 @@ def test_tensors_on_another_device_are_refused_before_any_kernel():
     cache = {"k": torch.zeros(1, 32, 2, 128, dtype=torch.bfloat16), "v": torch.zeros(1, 32, 2, 128, dtype=torch.bfloat16)}
     with pytest.raises(RuntimeError, match="must be on the same device"):
         hatt.cached_attention_local(x, x, x, t, t, t, cache, 0, text_mask=elsewhere)
+
+
+def test_mask_shapes_are_checked_before_any_kernel():
+    x = torch.zeros(1, 16, 2, 128, dtype=torch.bfloat16)
+    t = torch.zeros(1, 3, 2, 128, dtype=torch.bfloat16)
+    cache = {"k": torch.zeros(1, 32, 2, 128, dtype=torch.bfloat16), "v": torch.zeros(1, 32, 2, 128, dtype=torch.bfloat16)}
+    with pytest.raises(ValueError, match=r"history mask must be bool \[1 or 1, >= 20\], got \(1, 10\)"):
+        hatt.cached_attention_local(x, x, x, t, t, t, cache, 20, history_mask=torch.ones(1, 10, dtype=torch.bool))
+    with pytest.raises(ValueError, match="history mask must be"):
+        hatt.cached_attention_local(x, x, x, t, t, t, cache, 20, history_mask=torch.ones(3, 32, dtype=torch.bool))
+    with pytest.raises(ValueError, match=r"history mask must be bool \[1 or 1, >= 32\]"):
+        hatt.cached_attention_local(x, x, x, t, t, t, cache, 4, history_mask=torch.ones(1, 20, dtype=torch.bool),
+                                    hist_rows=torch.arange(4, dtype=torch.int32))
+    with pytest.raises(ValueError, match=r"text mask must be bool \[1, 3\], got \(1, 2\)"):
+        hatt.cached_attention_local(x, x, x, t, t, t, cache, 20, text_mask=torch.ones(1, 2, dtype=torch.bool))
