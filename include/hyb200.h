@@ -83,7 +83,8 @@ typedef struct hyb_cached_attn_args {
   int32_t abi_version;     /* HYB_ABI_VERSION */
   int32_t B, H, D;         /* batch, heads on this rank, head_dim (128) */
   int32_t cache_batch;     /* batch of the history tensors: B, or 1 (read-only broadcast) */
-  int32_t valid_len;       /* history tokens [0, valid_len) read from hist_k/hist_v */
+  int32_t valid_len;       /* history tokens [0, valid_len) read from hist_k/hist_v; at most their
+                              capacity (views carry no extent, so this is the caller's to ensure) */
   int32_t img_len, txt_len;
   int32_t attend_txt;      /* 1: current text keys are attended (cache_txt or update_cache) */
   int32_t group_tokens;    /* block-causal granularity in tokens (G frames x tokens/frame), 0 = off */
@@ -95,7 +96,8 @@ typedef struct hyb_cached_attn_args {
   hyb_tensor4 img_q, img_k, img_v;            /* Q BF16 [B, img_len, H, D]; K/V BF16, E4M3 or INT8 */
   hyb_tensor4 txt_q, txt_k, txt_v;            /* BF16 [B, txt_len, H, D] */
   const int32_t* hist_rows; /* [valid_len] cache row of composed history position t, or NULL
-                               (identity); sink + sliding-window rings use it */
+                               (identity); sink + sliding-window rings use it.  Every row must lie
+                               in [0, capacity of hist_k); the device does not check it */
   const uint8_t* cache_mask; int64_t cache_mask_sb;  /* bool [cache_batch, cap] (cache rows) or NULL */
   const uint8_t* text_mask;  int64_t text_mask_sb;   /* bool [B, txt_len] or NULL */
   void* out_img; int64_t oi_sb, oi_st, oi_sh;        /* bf16 [B, img_len, H, D] */
