@@ -401,6 +401,10 @@ def causal_attention_with_cache_mp(
     if hist_rows is not None:
         if hist_rows.numel() != cache_valid_len:
             raise ValueError("cache_valid_len must equal the window cache's history length")
+        # A window's own maps index its slots by construction; a map supplied without its window
+        # is checked once (one host sync), since the staging kernel reads the rows it names.
+        if window is None and hist_rows.numel() and (int(hist_rows.min()) < 0 or int(hist_rows.max()) >= cache_shape[1]):
+            raise ValueError("history_rows must name rows of the cache")
         history_mask = cache_mask if (cache_mask is not None and cache_valid_len > 0) else None
     else:
         history_mask = cache_mask[:, :cache_valid_len] if (cache_mask is not None and cache_valid_len > 0) else None

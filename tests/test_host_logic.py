@@ -333,3 +333,16 @@ def test_mask_shapes_are_checked_before_any_kernel():
                                     hist_rows=torch.arange(4, dtype=torch.int32))
     with pytest.raises(ValueError, match=r"text mask must be bool \[1, 3\], got \(1, 2\)"):
         hatt.cached_attention_local(x, x, x, t, t, t, cache, 20, text_mask=torch.ones(1, 2, dtype=torch.bool))
+
+
+def test_a_row_map_without_its_window_must_name_cache_rows(monkeypatch):
+    """The drop-in reads history through ``history_rows``; a map that does not come with its
+    window cache is range-checked before the staging kernel could read a row outside the cache."""
+    from hy_nomas_b200 import _lib
+    monkeypatch.setattr(_lib, "require_device", lambda t: None)   # the check precedes every launch
+    x = torch.zeros(1, 16, 2, 128, dtype=torch.bfloat16)
+    t = torch.zeros(1, 1, 2, 128, dtype=torch.bfloat16)
+    cache = {"k": torch.zeros(1, 32, 2, 128, dtype=torch.bfloat16), "v": torch.zeros(1, 32, 2, 128, dtype=torch.bfloat16),
+             "history_rows": torch.tensor([0, 5, 40], dtype=torch.int32)}
+    with torch.no_grad(), pytest.raises(ValueError, match="history_rows must name rows of the cache"):
+        hatt.causal_attention_with_cache_mp((x, t), (x, t), (x, t), cache, cache_valid_len=3, attn_mode="flash3")
