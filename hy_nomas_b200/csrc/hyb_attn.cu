@@ -224,11 +224,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
   uint8_t* sV = sK + kStages * kTileBytes;         // [kStages][kTileBytes]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages * kTileBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + kStages;
-  uint64_t* v_full = k_empty + kStages;
-  uint64_t* v_empty = v_full + kStages;
-  uint64_t* s_full = v_empty + kStages;  // [2] one per query tile
+  uint64_t* kv_full = bars + 1;            // [kStages]: K and V of the tile landed
+  uint64_t* kv_empty = kv_full + kStages;  // [kStages]: every MMA reading the stage completed
+  uint64_t* s_full = kv_empty + kStages;   // [2] one per query tile
   uint64_t* p_full = s_full + 2;         // [2]
   uint64_t* o_full = p_full + 2;         // [1]
   uint64_t* mma_done = o_full + 1;       // [1]
@@ -251,10 +249,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -304,56 +300,52 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const int k0 = tr.tile(j_begin + j) * kBN;
         const int st = j % kStages;
         const uint32_t ph = (j / kStages) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag)) break;
-        mbar_expect_tx(&k_full[st], kTileBytes);
-        tma_load_3d(sK + st * kTileBytes, &tmK, &k_full[st], 0, k0, bh);
-        tma_load_3d(sK + st * kTileBytes + kHalfTile, &tmK, &k_full[st], 64, k0, bh);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag)) {
-          issued = j;
-          mbar_drain(&k_full[st], ph);
-          break;
-        }
-        mbar_expect_tx(&v_full[st], kTileBytes);
-        tma_load_3d(sV + st * kTileBytes, &tmV, &v_full[st], 0, k0, bh);
-        tma_load_3d(sV + st * kTileBytes + kHalfTile, &tmV, &v_full[st], 64, k0, bh);
+        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag)) break;
+        mbar_expect_tx(&kv_full[st], 2 * kTileBytes);
+        tma_load_3d(sK + st * kTileBytes, &tmK, &kv_full[st], 0, k0, bh);
+        tma_load_3d(sK + st * kTileBytes + kHalfTile, &tmK, &kv_full[st], 64, k0, bh);
+        tma_load_3d(sV + st * kTileBytes, &tmV, &kv_full[st], 0, k0, bh);
+        tma_load_3d(sV + st * kTileBytes + kHalfTile, &tmV, &kv_full[st], 64, k0, bh);
         issued = j + 1;
       }
       if (*abort_flag) {
         mbar_drain(q_full, 0);
-        for (int j = max(0, issued - kStages); j < issued; ++j) {
-          mbar_drain(&k_full[j % kStages], (j / kStages) & 1);
-          mbar_drain(&v_full[j % kStages], (j / kStages) & 1);
-        }
+        for (int j = max(0, issued - kStages); j < issued; ++j) mbar_drain(&kv_full[j % kStages], (j / kStages) & 1);
       }
     } else if (warp == 1 && lane == 0) {
       // ---------------------------------------------------------- MMA issuer
+      // The issuing thread shares its SM sub-partition with two softmax warps, and every
+      // mbarrier operation costs it on the order of 100 cycles during which the tensor pipe
+      // can drain, so it waits and commits as little as possible (one K/V wait and one
+      // stage-free commit per key tile) and forms each operand descriptor as a base plus a
+      // constant.
       constexpr uint32_t kIdescQK = idesc_bf16_f32(kBM, kBN, false, false);
       constexpr uint32_t kIdescPV = idesc_bf16_f32(kBM, kHD, false, true);
-      const uint32_t sQa = smem_u32(sQ);
-      const uint32_t sKa = smem_u32(sK);
-      const uint32_t sVa = smem_u32(sV);
+      const SDesc dq = sdesc_sw128_parts(smem_u32(sQ), 16, 1024);
+      const SDesc dk = sdesc_sw128_parts(smem_u32(sK), 16, 1024);
+      const SDesc dv = sdesc_sw128_parts(smem_u32(sV), kHalfTile, 1024);
       auto issue_qk = [&](int qi, int st) {
         const uint32_t d = tmem + static_cast<uint32_t>(qi) * 128u;
+        const uint32_t a0 = dq.lo + static_cast<uint32_t>((qi * kTileBytes) >> 4);
+        const uint32_t b0 = dk.lo + static_cast<uint32_t>((st * kTileBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kHD / 16; ++kk) {
-          const uint32_t koff = static_cast<uint32_t>((kk >> 2) * kHalfTile + (kk & 3) * 32);
-          const uint64_t ad = sdesc_sw128(sQa + qi * kTileBytes + koff, 16, 1024);
-          const uint64_t bd = sdesc_sw128(sKa + st * kTileBytes + koff, 16, 1024);
-          umma_ss(d, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
+          const uint32_t koff = static_cast<uint32_t>(((kk >> 2) * kHalfTile + (kk & 3) * 32) >> 4);
+          umma_ss2(d, a0 + koff, dq.hi, b0 + koff, dk.hi, kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int qi, int st, bool first) {
+        const uint32_t b0 = dv.lo + static_cast<uint32_t>((st * kTileBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bd = sdesc_sw128(sVa + st * kTileBytes + kk * 2048, kHalfTile, 1024);
-          umma_ts(tmem + kTmemO + static_cast<uint32_t>(qi) * 128u,
-                  tmem + static_cast<uint32_t>(qi) * 128u + kk * 8, bd, kIdescPV,
-                  (!first || kk > 0) ? 1u : 0u);
+          umma_ts2(tmem + kTmemO + static_cast<uint32_t>(qi) * 128u,
+                   tmem + static_cast<uint32_t>(qi) * 128u + kk * 8, b0 + kk * (2048 >> 4), dv.hi, kIdescPV,
+                   (!first || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(q_full, 0, abort_flag);
       if (ok && n > 0) {
-        ok = mbar_wait(&k_full[0], 0, abort_flag);
+        ok = mbar_wait(&kv_full[0], 0, abort_flag);
         if (ok) {
           tc_fence_after();
           issue_qk(0, 0);
@@ -362,7 +354,6 @@ __global__ void __launch_bounds__(kThreads2, 1)
             issue_qk(1, 0);
             tc_commit(&s_full[1]);
           }
-          tc_commit(&k_empty[0]);
         }
       }
       // Fixed issue order per key tile j: P.V of query tile 0, Q.K^T of tile 0 for j+1,
@@ -372,12 +363,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const int st = j % kStages;
         const bool more = j + 1 < n;
         const int st1 = (j + 1) % kStages;
-        if (!mbar_wait(&v_full[st], (j / kStages) & 1, abort_flag)) break;
         if (!mbar_wait(&p_full[0], j & 1, abort_flag)) break;
         tc_fence_after();
         issue_pv(0, st, j == 0);
         if (more) {
-          if (!mbar_wait(&k_full[st1], ((j + 1) / kStages) & 1, abort_flag)) break;
+          if (!mbar_wait(&kv_full[st1], ((j + 1) / kStages) & 1, abort_flag)) break;
           tc_fence_after();
           issue_qk(0, st1);
           tc_commit(&s_full[0]);
@@ -386,15 +376,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
           if (!mbar_wait(&p_full[1], j & 1, abort_flag)) break;
           tc_fence_after();
           issue_pv(1, st, j == 0);
-        }
-        tc_commit(&v_empty[st]);
-        if (more) {
-          if (has1) {
+          if (more) {
             issue_qk(1, st1);
             tc_commit(&s_full[1]);
           }
-          tc_commit(&k_empty[st1]);
         }
+        tc_commit(&kv_empty[st]);
       }
       tc_commit(o_full);
       tc_commit(mma_done);

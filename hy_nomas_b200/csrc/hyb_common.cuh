@@ -203,6 +203,43 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
+// The two 32-bit halves of a 128-byte-swizzle shared-memory descriptor (layout as
+// sdesc_sw128).  Between the K-slices and stages of one operand only the start-address field
+// (low half, bits [0,14), 16-byte units) changes, so a slice's descriptor is
+// {base.lo + (byte offset >> 4), base.hi}: one integer add per MMA in the issuing thread.
+struct SDesc {
+  uint32_t lo, hi;
+};
+__device__ __forceinline__ SDesc sdesc_sw128_parts(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  SDesc d;
+  d.lo = ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+  d.hi = ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+  return d;
+}
+
+// umma_ss / umma_ts with the descriptors given as 32-bit halves.
+__device__ __forceinline__ void umma_ss2(uint32_t d_tmem, uint32_t alo, uint32_t ahi, uint32_t blo, uint32_t bhi,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 a, b;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "mov.b64 a, {%1, %2};\n\t"
+      "mov.b64 b, {%3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts2(uint32_t d_tmem, uint32_t a_tmem, uint32_t blo, uint32_t bhi,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 b;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 b, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], b, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 32 lanes x 32 columns of 32-bit tensor memory -> 32 registers per thread, waited.
 __device__ __forceinline__ void tmem_ld32_wait(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
