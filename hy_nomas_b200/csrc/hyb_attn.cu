@@ -185,6 +185,48 @@ __device__ __forceinline__ void unit_of(const UnitMap& um, int x, int& bh, int& 
   ki = um.prefix[i + 1] - um.prefix[i];
 }
 
+// Epilogue stores through a per-warp 4 KB shared-memory buffer.  A warp holds 32 rows (lane =
+// row) of 32 columns; written directly, every store instruction would touch 32 rows with 16
+// bytes each.  Transposed through shared memory (16-byte granules XOR-swizzled by row, no bank
+// conflicts), each instruction writes whole 128-byte (fp32) or 64-byte (bf16) row chunks.
+// fp32: row r of the warp goes to base + r * kHD (rows contiguous, as the split partials are);
+// rows with r >= nrows are not written.
+__device__ __forceinline__ void warp_store_f32_rows(uint8_t* ebuf, const float (&v)[32], float* base, int nrows,
+                                                    int lane) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+    *reinterpret_cast<float4*>(ebuf + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+        make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+  __syncwarp();
+  const int g = lane & 7;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    const float4 x = *reinterpret_cast<const float4*>(ebuf + r * 128 + ((g ^ (r & 7)) << 4));
+    if (r < nrows) reinterpret_cast<float4*>(base + static_cast<size_t>(r) * kHD)[g] = x;
+  }
+  __syncwarp();
+}
+// bf16: 16 packed pairs per lane; row r goes to the row pointer held by lane r (null: skip).
+__device__ __forceinline__ void warp_store_bf16_rows(uint8_t* ebuf, const uint32_t (&o)[16], __nv_bfloat16* dst,
+                                                     int lane) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+    *reinterpret_cast<uint4*>(ebuf + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(o[4 * g], o[4 * g + 1], o[4 * g + 2], o[4 * g + 3]);
+  __syncwarp();
+  const int g = lane & 3;
+  const unsigned long long mine = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane >> 2);
+    const uint4 x = *reinterpret_cast<const uint4*>(ebuf + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
+    const unsigned long long d = __shfl_sync(0xffffffffu, mine, r);
+    if (d != 0ull) reinterpret_cast<uint4*>(d)[g] = x;
+  }
+  __syncwarp();
+}
+
 // Bounded wait that ignores the abort flag (used to drain in-flight async work on exit).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const long long t0 = clock64();
@@ -509,13 +551,18 @@ __global__ void __launch_bounds__(kThreads2, 1)
       bool have_o = ok && n > 0 && mbar_wait(o_full, 0, abort_flag);
       have_o = __all_sync(0xffffffffu, have_o);
       tc_fence_after();
+      // Every MMA has completed (or the CTA aborted and waits for nothing more), so the K ring
+      // is free: 4 KB of it per softmax warp stages the epilogue's row transposes.
+      uint8_t* ebuf = sK + (warp - 4) * 4096;
       const bool in_range = qrow < p.Lq;
       if (nsplit > 1) {
         // Partial result of this key slice: O / l in fp32 and its LSE (-inf when the slice
         // saw no visible key); query validity is applied by the merge.
         const float inv_l = l > 0.f ? __frcp_rn(l) : 0.f;
         const size_t prow = ((static_cast<size_t>(split) * p.B + b) * p.H + h) * p.Lq + qrow;
-        float* dst = in_range ? p.part_o + prow * kHD : nullptr;
+        const int row0 = qt0 + quarter * 32;   // the warp's first row: its rows are contiguous
+        float* wbase = p.part_o + (prow - lane) * kHD;
+        const int nrows = imin(32, p.Lq - row0);
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           uint32_t r[32];
@@ -525,13 +572,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = 0u;
           }
-          if (dst != nullptr) {
-            float4* d4 = reinterpret_cast<float4*>(dst + c4 * 32);
+          float v[32];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              d4[i] = make_float4(__uint_as_float(r[4 * i]) * inv_l, __uint_as_float(r[4 * i + 1]) * inv_l,
-                                  __uint_as_float(r[4 * i + 2]) * inv_l, __uint_as_float(r[4 * i + 3]) * inv_l);
-          }
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * inv_l;
+          warp_store_f32_rows(ebuf, v, wbase + c4 * 32, nrows, lane);
         }
         if (in_range) p.part_lse[prow] = l > 0.f ? (m_run * kLn2 + __logf(l)) : -INFINITY;
       } else if (p.acc_o != nullptr) {
@@ -619,11 +663,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i)
             o[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
-          if (dst != nullptr) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-          }
+          warp_store_bf16_rows(ebuf, o, dst != nullptr ? dst + c4 * 32 : nullptr, lane);
         }
         if (p.lse != nullptr && in_range) {
           p.lse[static_cast<size_t>(bh) * p.Lq + qrow] =
