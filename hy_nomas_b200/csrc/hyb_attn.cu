@@ -251,8 +251,10 @@ constexpr int kPairRows = 2 * kBM;
 // fits (keys <= 32 * kMaxSmemBitWords); otherwise the softmax reads it through L1.
 constexpr int kMaxSmemBitWords = 4096;
 
-// kEmuPer8: of every 8 consecutive scores, that many take exp2 on the FMA pipe
-// (exp2_poly) and the rest on MUFU, to balance the two units against the tensor pipe.
+// kEmuPer8: that many eighths of a row's 64 score pairs take exp2 on the FMA pipe
+// (exp2_poly2) and the rest on MUFU, to balance the two units against the tensor pipe.  The
+// emulated pairs are the last ones of the row, computed when most scores are already
+// consumed, so the polynomial's temporaries do not raise register pressure.
 template <int kEmuPer8>
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -513,8 +515,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
           const int c0 = 2 * c;
           const float2 x = ffma2(make_float2(s[32 * q4 + c0], s[32 * q4 + c0 + 1]), sl2x2, negm);
           float2 e;
-          if ((c0 & 7) >= 8 - kEmuPer8) {
-            e = make_float2(exp2_poly(x.x), exp2_poly(x.y));
+          if (16 * q4 + c >= kBN / 2 - 8 * kEmuPer8) {
+            e = exp2_poly2(x);
           } else {
             e = make_float2(ex2(x.x), ex2(x.y));
           }
@@ -558,7 +560,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
       if (nsplit > 1) {
         // Partial result of this key slice: O / l in fp32 and its LSE (-inf when the slice
         // saw no visible key); query validity is applied by the merge.
-        const float inv_l = l > 0.f ? __frcp_rn(l) : 0.f;
+        const bool seen = m_run != -INFINITY;  // some key of the slice is visible to this row
+        const float inv_l = seen ? __frcp_rn(l) : 0.f;
         const size_t prow = ((static_cast<size_t>(split) * p.B + b) * p.H + h) * p.Lq + qrow;
         const int row0 = qt0 + quarter * 32;   // the warp's first row: its rows are contiguous
         float* wbase = p.part_o + (prow - lane) * kHD;
@@ -577,16 +580,17 @@ __global__ void __launch_bounds__(kThreads2, 1)
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * inv_l;
           warp_store_f32_rows(ebuf, v, wbase + c4 * 32, nrows, lane);
         }
-        if (in_range) p.part_lse[prow] = l > 0.f ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+        if (in_range) p.part_lse[prow] = seen ? (m_run * kLn2 + __logf(l)) : -INFINITY;
       } else if (p.acc_o != nullptr) {
         // Ring step: merge this launch's rows into the running output.
         const bool merge = (p.acc_mode & 1) != 0;
         const bool fin = (p.acc_mode & 2) != 0;
         const size_t lrow = static_cast<size_t>(bh) * p.Lq + qrow;
-        const float lse_b = l > 0.f ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+        const bool seen = m_run != -INFINITY;
+        const float lse_b = seen ? (m_run * kLn2 + __logf(l)) : -INFINITY;
         const float lse_a = (in_range && merge) ? p.acc_lse[lrow] : -INFINITY;
         const AccWeights aw = acc_weights(lse_a, lse_b);
-        const float cb = l > 0.f ? aw.wb * __frcp_rn(l) : 0.f;
+        const float cb = seen ? aw.wb * __frcp_rn(l) : 0.f;
         float* arow = in_range ? p.acc_o + ((static_cast<size_t>(b) * p.Lq + qrow) * p.H + h) * kHD : nullptr;
         __nv_bfloat16* dst = (in_range && fin) ? p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg +
                                                      (qrow % p.oi_seg) * p.oi_t + h * p.oi_h
@@ -640,7 +644,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
         bool valid = in_range;
         if (in_range && p.qbits != nullptr)
           valid = (__ldg(p.qbits + static_cast<size_t>(b) * p.qwords + (qrow >> 5)) >> (qrow & 31)) & 1u;
-        const float inv_l = (l > 0.f && valid) ? __frcp_rn(l) : 0.f;
+        const bool seen = m_run != -INFINITY;
+        const float inv_l = (seen && valid) ? __frcp_rn(l) : 0.f;
         __nv_bfloat16* dst = nullptr;
         if (in_range) {
           if (img_row) {
@@ -667,7 +672,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         }
         if (p.lse != nullptr && in_range) {
           p.lse[static_cast<size_t>(bh) * p.Lq + qrow] =
-              (l > 0.f && valid) ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+              (seen && valid) ? (m_run * kLn2 + __logf(l)) : -INFINITY;
         }
       }
     }
@@ -1300,7 +1305,8 @@ int launch_attn2_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
   return HYB_OK;
 }
 
-// Share of exponentials computed on the FMA pipe, in eighths (HYB_EXP_EMU overrides).
+// Share of exponentials computed on the FMA pipe, in eighths of the score pairs (HYB_EXP_EMU
+// overrides).
 int exp_emu_per8() {
   static int v = -1;
   if (v < 0) {

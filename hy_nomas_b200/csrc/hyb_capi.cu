@@ -51,9 +51,13 @@ extern "C" int hyb_device_supported(void) { return hyb::device_cc_major() == 10 
 namespace hyb {
 namespace {
 __global__ void exp2_poly_kernel(const float* x, float* y, long long n) {
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<long long>(gridDim.x) * blockDim.x)
-    y[i] = exp2_poly(x[i]);
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; 2 * i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const bool two = 2 * i + 1 < n;
+    const float2 e = exp2_poly2(make_float2(x[2 * i], two ? x[2 * i + 1] : 0.f));
+    y[2 * i] = e.x;
+    if (two) y[2 * i + 1] = e.y;
+  }
 }
 }  // namespace
 }  // namespace hyb
@@ -62,7 +66,7 @@ extern "C" int hyb_exp2_poly_eval(const float* x, float* y, int64_t n, void* str
   if (n < 0 || (n > 0 && (x == nullptr || y == nullptr)))
     return hyb::fail(HYB_ERR_INVALID_ARG, "exp2_poly_eval: bad arguments");
   if (n == 0) return HYB_OK;
-  long long blocks = (n + 255) / 256;
+  long long blocks = ((n + 1) / 2 + 255) / 256;
   if (blocks > 4096) blocks = 4096;
   hyb::exp2_poly_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
   HYB_CHECK_LAUNCH();

@@ -315,35 +315,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA/ALU pipes (offloads the MUFU unit).  Range reduction x = n + f with
-// n = round-to-nearest(x) (via the 1.5 * 2^23 shifter) and f in [-1/2, 1/2]; 2^f from a
-// degree-3 polynomial fitted here by relative-error-weighted least squares on Chebyshev
-// nodes of [-1/2, 1/2] (max relative error 7.5e-5, far below the 2^-9 rounding of the
-// bf16 P it feeds); 2^n is applied by adding n to the exponent field.  x < -125 gives 0,
-// so masked (-inf) scores contribute nothing.  Valid for x <= 127.
-__device__ __forceinline__ float exp2_poly(float x) {
-  constexpr float kC0 = 0.99992807f;
-  constexpr float kC1 = 0.69326100f;
-  constexpr float kC2 = 0.24261112f;
-  constexpr float kC3 = 0.05517161f;
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  const float xc = fmaxf(x, -127.f);
-  const float t = __fadd_rn(xc, kShift);
-  const float n = __fsub_rn(t, kShift);
-  const float f = __fsub_rn(xc, n);
-  const float p = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
-  const int ni = __float_as_int(t) - 0x4B400000;
-  const float r = __int_as_float(__float_as_int(p) + (ni << 23));
-  return xc < -125.f ? 0.f : r;
-}
-
-// Two base-2 exponentials per MUFU op on a packed f16 pair (f16 in, f16 out).
-__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
 // Packed fp32 pair arithmetic (one instruction for two lanes of work on sm_100).
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   unsigned long long r;
@@ -359,6 +330,39 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
       : "=l"(r)
       : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
   return *reinterpret_cast<float2*>(&r);
+}
+
+// 2^x for a pair of scores on the FMA/ALU pipes (offloads the MUFU unit), in packed fp32x2
+// arithmetic: about 11 instructions for two exponentials.  Range reduction x = n + f with
+// n = round-to-nearest(x) (via the 1.5 * 2^23 shifter) and f in [-1/2, 1/2]; 2^f from a
+// degree-3 polynomial fitted here by relative-error-weighted least squares on Chebyshev nodes
+// of [-1/2, 1/2] (max relative error 7.5e-5, far below the 2^-9 rounding of the bf16 P it
+// feeds); 2^n is applied by adding n to the exponent field: the shifter's bits shifted left by
+// 23 are n << 23 modulo 2^32.  Inputs are clamped to -126, so x <= -126 (a masked -inf score
+// included) gives a nonnegative value below 2^-125, not exactly 0: callers decide "no visible
+// key" from the running maximum, never from the row sum.  Valid for x <= 127.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kC0 = 0.99992807f;
+  constexpr float kC1 = 0.69326100f;
+  constexpr float kC2 = 0.24261112f;
+  constexpr float kC3 = 0.05517161f;
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  const float2 xc = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
+  const float2 t = fadd2(xc, make_float2(kShift, kShift));
+  const float2 n = fadd2(t, make_float2(-kShift, -kShift));
+  const float2 f = ffma2(n, make_float2(-1.f, -1.f), xc);
+  float2 p = ffma2(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
+  p = ffma2(p, f, make_float2(kC1, kC1));
+  p = ffma2(p, f, make_float2(kC0, kC0));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+// Two base-2 exponentials per MUFU op on a packed f16 pair (f16 in, f16 out).
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
 
 // Three-input max (one instruction on sm_100).

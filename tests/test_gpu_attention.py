@@ -269,8 +269,9 @@ def test_empty_text_and_single_query(cuda_lib):
 
 
 def test_exp2_poly_accuracy(cuda_lib):
-    """The FMA-pipe exponential against CUDA's exp2f: relative error <= 1e-4 wherever the
-    result is a normal float, exactly 0 below -125 and for -inf."""
+    """The FMA-pipe exponential (packed pairs) against exp2 in float64: relative error <= 1e-4
+    wherever the result is a normal float; below -125 and for -inf a nonnegative value under
+    2^-125 (the kernel decides "no visible key" from the running maximum, not from P)."""
     from hy_nomas_b200 import _lib
     dev = torch.device("cuda")
     x = torch.cat([torch.linspace(-125.0, 12.0, 2_000_001), torch.tensor([-126.0, -1e4, float("-inf")])])
@@ -282,7 +283,8 @@ def test_exp2_poly_accuracy(cuda_lib):
     normal = x > -125.0
     rel = ((y.double() - ref).abs() / ref)[normal]
     assert rel.max().item() <= 1e-4, rel.max().item()
-    assert torch.all(y[x < -125.0] == 0)
+    tail = y[x < -125.0]
+    assert torch.all(tail >= 0) and torch.all(tail < 2.0 ** -125)
 
 
 @pytest.mark.parametrize("splits", [1, 2, 5, 16])
