@@ -86,7 +86,7 @@ class AttnArgs(ctypes.Structure):
         ("oi_seg", c_i64), ("oi_sseg", c_i64),
         ("out_txt", c_ptr), ("ot_sb", c_i64), ("ot_st", c_i64), ("ot_sh", c_i64),
         ("lse", c_ptr), ("dev_status", c_ptr),
-        ("kv_splits", c_i32), ("pad_", c_i32), ("part_o", c_ptr), ("part_lse", c_ptr),
+        ("kv_splits", c_i32), ("v_f16", c_i32), ("part_o", c_ptr), ("part_lse", c_ptr),
         ("acc_o", c_ptr), ("acc_lse", c_ptr), ("acc_mode", c_i32), ("pad2_", c_i32),
     ]
 

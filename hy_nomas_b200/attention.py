@@ -218,6 +218,7 @@ def cached_attention_local(
         at.kbits, at.kwords = base + lay.kbits, lay.kwords
         at.qbits, at.qwords = base + lay.qbits, lay.qwords
         at.kv_splits = lay.kv_splits
+        at.v_f16 = 1   # the staged V is fp16 (P.V in fp16)
         at.part_o, at.part_lse = base + lay.part_o, base + lay.part_lse
         at.out_img = args.out_img
         at.oi_sb, at.oi_st, at.oi_sh = oi[0], oi[1], oi[2]

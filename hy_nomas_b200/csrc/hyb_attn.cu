@@ -255,7 +255,8 @@ constexpr int kMaxSmemBitWords = 4096;
 // (exp2_poly2) and the rest on MUFU, to balance the two units against the tensor pipe.  The
 // emulated pairs are the last ones of the row, computed when most scores are already
 // consumed, so the polynomial's temporaries do not raise register pressure.
-template <int kEmuPer8>
+// kVF16: V staged in fp16 and P rounded to fp16 for P.V (else both bf16).
+template <int kEmuPer8, bool kVF16>
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnKParams p,
@@ -364,7 +365,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
       // stage-free commit per key tile) and forms each operand descriptor as a base plus a
       // constant.
       constexpr uint32_t kIdescQK = idesc_bf16_f32(kBM, kBN, false, false);
-      constexpr uint32_t kIdescPV = idesc_bf16_f32(kBM, kHD, false, true);
+      constexpr uint32_t kIdescPV =
+          kVF16 ? idesc_f16_f32(kBM, kHD, false, true) : idesc_bf16_f32(kBM, kHD, false, true);
       const SDesc dq = sdesc_sw128_parts(smem_u32(sQ), 16, 1024);
       const SDesc dk = sdesc_sw128_parts(smem_u32(sK), 16, 1024);
       const SDesc dv = sdesc_sw128_parts(smem_u32(sV), kHalfTile, 1024);
@@ -525,7 +527,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
           } else {
             l2a = fadd2(l2a, e);
           }
-          pk[c] = pack_bf16x2(e.x, e.y);
+          pk[c] = kVF16 ? pack_f16x2(e.x, e.y) : pack_bf16x2(e.x, e.y);
         }
         tmem_st16(t_s + 16 * q4, pk);
       }
@@ -774,7 +776,9 @@ struct StageParams {
   int B, H, L, nout, nseg;
   StageSeg seg[2][3];
   void* out[2];       // [B, H, L, 128]
-  int out_f16[2];     // 1: output in fp16 (the P.V operand), 0: bf16
+  int out_f16[2];     // 1: output in fp16 (the P.V operand), 0: bf16.  Either way a value is the
+                      // bf16 the reference decodes (dequantize_kv rounds code * scale to bf16):
+                      // fp16 holds every such bf16 value exactly in the range of K/V activations
 };
 
 // Eight consecutive values of one (batch, token, head) row as fp32: bf16 sources exactly,
@@ -843,7 +847,8 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
         uint32_t* w = reinterpret_cast<uint32_t*>(&packed);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          w[i] = p.out_f16[o] ? pack_f16x2(v[2 * i], v[2 * i + 1]) : pack_bf16x2(v[2 * i], v[2 * i + 1]);
+          w[i] = p.out_f16[o] ? pack_f16x2(bf16_round(v[2 * i]), bf16_round(v[2 * i + 1]))
+                              : pack_bf16x2(v[2 * i], v[2 * i + 1]);
         *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out[o]) + out_off) = packed;
       }
     }
@@ -1288,25 +1293,25 @@ WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt,
   return w;
 }
 
-template <int kEmuPer8>
+template <int kEmuPer8, bool kVF16>
 int launch_attn2_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnKParams& kp,
                    const UnitMap& um, cudaStream_t stream) {
   const int smem = 1024 + kTileBytes * (2 + 2 * kStages) + 256 + kMaxSmemBitWords * 4;
   static bool attr_set = false;
   if (!attr_set) {
-    HYB_CUDA_TRY(cudaFuncSetAttribute(attn_fwd2_kernel<kEmuPer8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    HYB_CUDA_TRY(cudaFuncSetAttribute(attn_fwd2_kernel<kEmuPer8, kVF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       smem));
     attr_set = true;
   }
   const long long units = static_cast<long long>(kp.B) * kp.H * um.per_bh;
   if (units <= 0 || units > INT_MAX) return fail(HYB_ERR_UNSUPPORTED, "attention: %lld work units", units);
-  attn_fwd2_kernel<kEmuPer8><<<static_cast<unsigned>(units), kThreads2, smem, stream>>>(mq, mk, mv, kp, um);
+  attn_fwd2_kernel<kEmuPer8, kVF16><<<static_cast<unsigned>(units), kThreads2, smem, stream>>>(mq, mk, mv, kp, um);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
 
-// Share of exponentials computed on the FMA pipe, in eighths of the score pairs (HYB_EXP_EMU
-// overrides).
+// Share of exponentials computed on the FMA pipe, in eighths of the score pairs: 0 unless
+// HYB_EXP_EMU selects 2 or more (built variants: none, a quarter).
 int exp_emu_per8() {
   static int v = -1;
   if (v < 0) {
@@ -1317,14 +1322,12 @@ int exp_emu_per8() {
 }
 
 int launch_attn2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnKParams& kp,
-                 const UnitMap& um, cudaStream_t stream) {
-  switch (exp_emu_per8()) {
-    case 0: return launch_attn2_t<0>(mq, mk, mv, kp, um, stream);
-    case 1: return launch_attn2_t<1>(mq, mk, mv, kp, um, stream);
-    case 3: return launch_attn2_t<3>(mq, mk, mv, kp, um, stream);
-    case 4: return launch_attn2_t<4>(mq, mk, mv, kp, um, stream);
-    default: return launch_attn2_t<2>(mq, mk, mv, kp, um, stream);
-  }
+                 const UnitMap& um, bool v_f16, cudaStream_t stream) {
+  // Exponentials on the FMA pipe: none by default (measured fastest); HYB_EXP_EMU=2 gives a
+  // quarter of every row's pairs.
+  const bool emu = exp_emu_per8() >= 2;
+  if (v_f16) return emu ? launch_attn2_t<2, true>(mq, mk, mv, kp, um, stream) : launch_attn2_t<0, true>(mq, mk, mv, kp, um, stream);
+  return emu ? launch_attn2_t<2, false>(mq, mk, mv, kp, um, stream) : launch_attn2_t<0, false>(mq, mk, mv, kp, um, stream);
 }
 
 // Validate the arguments and translate them into kernel parameters (no device access).
@@ -1411,9 +1414,9 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   CUtensorMap mq, mk, mv;
   if ((rc = make_map(&mq, a->q, BH, a->Lq)) != HYB_OK) return rc;
   if ((rc = make_map(&mk, a->k, BH, a->Lk > 0 ? a->Lk : 1)) != HYB_OK) return rc;
-  if ((rc = make_map(&mv, a->v, BH, a->Lk > 0 ? a->Lk : 1)) != HYB_OK) return rc;
+  if ((rc = make_map(&mv, a->v, BH, a->Lk > 0 ? a->Lk : 1, a->v_f16 != 0)) != HYB_OK) return rc;
   const UnitMap um = plan_units(kp, kp.kv_splits, device_sm_count());
-  int rc2 = launch_attn2(mq, mk, mv, kp, um, stream);
+  int rc2 = launch_attn2(mq, mk, mv, kp, um, a->v_f16 != 0, stream);
   if (rc2 != HYB_OK || um.max_k <= 1) return rc2;
   const long long rows = static_cast<long long>(kp.B) * kp.H * kp.Lq;
   merge_splits_kernel<<<grid_for(rows * 32, 256), 256, 0, stream>>>(kp, um);
@@ -1632,7 +1635,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     sp.out[0] = k_all;
     sp.out[1] = v_all;
     sp.out_f16[0] = 0;
-    sp.out_f16[1] = 0;
+    sp.out_f16[1] = 1;   // V (and so P) in fp16 for P.V
     stage_kernel<<<grid_for(static_cast<long long>(a->B) * a->H * w.Lk * 16, 256), 256, 0, stream>>>(sp);
     HYB_CHECK_LAUNCH();
   }
@@ -1688,6 +1691,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   at.lse = a->lse;
   at.dev_status = a->dev_status;
   at.kv_splits = w.kv_splits;
+  at.v_f16 = 1;
   at.part_o = reinterpret_cast<float*>(ws + w.part_o);
   at.part_lse = reinterpret_cast<float*>(ws + w.part_lse);
   return attn_core(&at, stream);

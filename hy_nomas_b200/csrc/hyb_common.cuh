@@ -381,6 +381,9 @@ __device__ __forceinline__ float2 unpack_f16x2(uint32_t u) {
   return __half22float2(*reinterpret_cast<const __half2*>(&u));
 }
 
+// x rounded to the nearest bf16, returned as fp32.
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -120,9 +120,10 @@ def _sample_cache(kv_cache: dict, b: int) -> dict:
     return d
 
 
-def _accumulate(lib, stream, status, H, q_head_major, Lq, k, v, Lk, kbits, kwords, scale, splits_hint):
+def _accumulate(lib, stream, status, H, q_head_major, Lq, k, v, Lk, kbits, kwords, scale, splits_hint, v_f16=0):
     """One accumulator-mode launch: rows [Lq] of ``q_head_major`` against keys [Lk] (every
-    key visible where its bit is set) -> fp32 rows [Lq, H, 128] and natural-log LSE [H, Lq]."""
+    key visible where its bit is set) -> fp32 rows [Lq, H, 128] and natural-log LSE [H, Lq].
+    ``v_f16``: the staged values are fp16 (the cached attention's workspace) rather than bf16."""
     dev = q_head_major.device
     acc = torch.empty((Lq, H, _D), dtype=torch.float32, device=dev)
     acc_lse = torch.empty((H, Lq), dtype=torch.float32, device=dev)
@@ -141,6 +142,7 @@ def _accumulate(lib, stream, status, H, q_head_major, Lq, k, v, Lk, kbits, kword
     a.lse = None
     a.dev_status = status.data_ptr()
     a.kv_splits = max(1, int(splits_hint))
+    a.v_f16 = int(v_f16)
     if a.kv_splits > 1:
         part_o = torch.empty((a.kv_splits * H * Lq * _D,), dtype=torch.float32, device=dev)
         part_lse = torch.empty((a.kv_splits * H * Lq,), dtype=torch.float32, device=dev)
@@ -208,7 +210,7 @@ def intra_segment_attention(img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, 
             qt, _ = _stage(lib, stream, cur[3])
             lay = workspace_layout(1, H, at.Lk - Lt, 0, Lt, True)
             acc_t, lse_t = _accumulate(lib, stream, status, H, qt, Lt, at.k, at.v, at.Lk, at.kbits, at.kwords,
-                                       at.softmax_scale, lay.kv_splits)
+                                       at.softmax_scale, lay.kv_splits, v_f16=at.v_f16)
             kt, vt = _stage(lib, stream, cur[4], cur[5])
             kwords_t = ((Lt + 127) // 128) * 4
             for a in live:

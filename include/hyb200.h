@@ -182,7 +182,9 @@ typedef struct hyb_attn_args {
   float* lse;
   int32_t* dev_status;
   int32_t kv_splits;         /* >1: each query pair's key tiles are split into this many slices */
-  int32_t pad_;
+  int32_t v_f16;             /* 1: v holds fp16 values and the softmax weights P are rounded to fp16
+                                (11-bit significand) for P.V; 0: v and P in bf16 (8-bit significand).
+                                bf16 values convert to fp16 exactly within fp16's range */
   float* part_o;             /* fp32 [kv_splits, B, H, Lq, D] partial rows (kv_splits > 1) */
   float* part_lse;           /* fp32 [kv_splits, B, H, Lq] partial LSE (kv_splits > 1) */
   /* Running output of a ring (KV-passing) schedule, or NULL.  With acc_o set, every query is an

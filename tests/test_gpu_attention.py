@@ -1,18 +1,19 @@
 """The tcgen05 cached-attention kernel against the oracle and the reference's outputs.
 
-Tolerances.  The north star asks for max-abs-err 2e-2 and cosine >= 0.9995.  The kernel's
-precision contract is bf16 operands, fp32 accumulation, bf16 P (relative rounding 2^-9) and a
-bf16 output (the reference returns the input dtype).  Two bf16 effects exceed a flat 2e-2 on
-the benchmark's x8 outlier channels: (1) the output's own rounding (outputs reach |o| ~ 20,
-where one bf16 ulp is 0.125), and (2) cancellation: an output element that sums P-weighted
-values of +-20 down to ~1 carries the 2^-9 rounding of P relative to those values, not to the
-result.  The elementwise bound is therefore
+Tolerances.  The north star asks for max-abs-err 2e-2 and cosine >= 0.9995.  The cached path
+computes with bf16 Q/K, fp16 V and P (P.V in fp16 with fp32 accumulation) and returns bf16
+(the reference returns the input dtype).  The bf16 output's own rounding exceeds a flat 2e-2
+on the benchmark's x8 outlier channels (outputs reach |o| ~ 20, where half a bf16 ulp is
+0.03-0.06); the reference's own outputs carry exactly that error (tests/test_parity_floor.py),
+and tests/test_gpu_parity_gate.py shows the kernel's fp32 rows within the flat gate and its
+bf16 outputs at the reference's floor.  The elementwise bounds here are wider and also cover
+the paths that keep bf16 P (ring, intra-segment): against the fp32 oracle
     |out - ref| <= 2e-2 + 2^-7 * |ref| + 2^-8 * (softmax(S) @ |V|)
-(2e-2, plus one output ulp, plus twice the P-rounding error on the element's weighted value
-magnitude, computed by the oracle), together with cosine >= 0.9995 over all valid rows,
-against the fp32 oracle on the same decoded inputs.  Against the reference's own bf16 outputs
-(golden fixtures, which carry their own bf16 rounding) the relative term is 1e-2.  Padded
-text query rows are exactly zero."""
+(2e-2, plus one output ulp, plus twice a bf16 P's rounding on the element's weighted value
+magnitude, computed by the oracle), with cosine >= 0.9995 over all valid rows.  Against the
+reference's own bf16 outputs (golden fixtures, which carry their own rounding) the relative
+term is 1e-2, and the north-star gate against the exact result is asserted and printed as
+well.  Padded text query rows are exactly zero."""
 import numpy as np
 import pytest
 import torch
@@ -23,6 +24,7 @@ from hy_nomas_b200 import kv_cache as kvc
 from hy_nomas_b200.synthetic import make_generator, seeded_kv
 from oracle import attention as oatt
 from oracle import quant as oq
+from parity import check_bf16, metrics
 
 pytestmark = pytest.mark.gpu
 
@@ -160,6 +162,12 @@ def test_drop_in_matches_reference_outputs(cuda_lib, case):
     valid = torch.from_numpy(g["text_mask"])
     assert ((out_txt[valid] - ref_txt[valid]).abs() <= ATOL + 1e-2 * ref_txt[valid].abs()).all()
     assert torch.all(out_txt[~valid] == 0)
+    # the north-star gate against the exact result of the same inputs (printed)
+    import test_parity_floor as floor
+    exact, ref_rows = floor._case(case)
+    mae_ref, cos_ref = metrics(ref_rows, exact)
+    print(f"{case}: reference bf16 vs exact max_abs={mae_ref:.4e} cos={cos_ref:.7f}")
+    check_bf16(torch.cat([out_img.flatten(), out_txt[valid].flatten()]), exact, f"{case} drop-in bf16 output")
     if update:
         n = Li + (Lt if cache_txt else 0)
         for key in ("k", "v"):
