@@ -54,6 +54,10 @@ def parse():
                          "each upload / compute / read-back, and the host link alone; printed to stderr")
     ap.add_argument("--ring-schedule", default="allgather", choices=["allgather", "ring"],
                     help="ring workload: every block to every rank over peer memory, or neighbour passing")
+    ap.add_argument("--measure-fp8-peak", action="store_true",
+                    help="print the dense FP8 GEMM peak of this GPU (burst and 4 s sustained) and exit")
+    ap.add_argument("--no-config3", action="store_true",
+                    help="config 2: skip the config-3 ring measurement reported in the same line")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager calls instead of replaying one captured CUDA graph of the call")
     ap.add_argument("--workload", default="config2", choices=["config2", "config4", "ring", "rollout"],
@@ -70,6 +74,48 @@ def load_peaks():
         d = json.loads(p.read_text())
         return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
     return 1590.0, 6650.0, "fallback"
+
+
+def measure_fp8_peak(device, sustained_s=0.0):
+    """Dense FP8 (e4m3) GEMM throughput on this GPU: torch._scaled_mm 8192^3 (2 N^3 FLOP),
+    best of 10 launches (burst) and, with sustained_s > 0, back to back for that long.
+    TFLOP/s."""
+    N = 8192
+    a = torch.randn(N, N, device=device).to(torch.float8_e4m3fn)
+    b = torch.randn(N, N, device=device).to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device=device)
+
+    def mm():
+        return torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+
+    for _ in range(3):
+        mm()
+    torch.cuda.synchronize(device)
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        mm()
+        e1.record()
+        torch.cuda.synchronize(device)
+        best = min(best, e0.elapsed_time(e1))
+    out = {"burst": round(2 * N ** 3 / (best * 1e-3) / 1e12, 1)}
+    if sustained_s > 0:
+        n = 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        t = time.time()
+        while time.time() - t < sustained_s:
+            for _ in range(20):
+                mm()
+            n += 20
+            torch.cuda.synchronize(device)
+        e1.record()
+        torch.cuda.synchronize(device)
+        out["sustained"] = round(2 * N ** 3 * n / (e0.elapsed_time(e1) * 1e-3) / 1e12, 1)
+    del a, b
+    torch.cuda.empty_cache()
+    return out
 
 
 def load_traffic():
@@ -285,7 +331,10 @@ def build_problem(rank, world, device, hist_frames=HIST_FRAMES):
         del hk, hv
     Ls = Li // world
     img = [seeded_kv((1, Ls, H_TOTAL, D), gen, device=device) for _ in range(3)]
-    txt = [seeded_kv((1, TXT, H_TOTAL, D), gen, device=device) for _ in range(3)]
+    # the text tokens are replicated on every rank (the reference's SP callers hold the whole
+    # text and slice its heads), so they come from one generator shared by all ranks
+    gen_txt = make_generator(1236 + 1000, device=device)
+    txt = [seeded_kv((1, TXT, H_TOTAL, D), gen_txt, device=device) for _ in range(3)]
     cache_mask = torch.zeros(1, cap, dtype=torch.bool, device=device)
     cache_mask[:, :Lh] = True
     return dict(cache=cache, img=img, txt=txt, cache_mask=cache_mask, Lh=Lh, Li=Li, Ls=Ls, Hl=Hl)
@@ -332,6 +381,88 @@ def print_e2e_timeline(step_fn, host_in, device, steps, world, rank, static_outp
           file=out)
 
 
+# ------------------------------------------------------------------------------ parity check
+# Before timing, every rank checks its own output rows of a few sampled heads against the exact
+# attention of the same inputs, computed in float64 with plain torch on its GPU (what the drop-in
+# returns in bf16 must be within 2e-2 of it beyond the bf16 rounding any bf16 output carries,
+# cosine >= 0.9995).  Inputs a rank does not hold (other ranks' sequence shards, the owner's
+# history of a head) arrive over the process group, outside the timed region.
+PARITY_HEADS = (0, H_TOTAL - 1)
+
+
+def _exact_rows(q, k, v, vis):
+    """float64 softmax(q k^T / sqrt(D)) v of q [Lq, D] over k/v [Lk, D] with visibility [Lq, Lk]."""
+    s = (q.double() @ k.double().T) / (q.shape[-1] ** 0.5)
+    s = s.masked_fill(~vis, float("-inf"))
+    return torch.softmax(s, dim=-1) @ v.double()
+
+
+def _gate(got, exact):
+    """(max-abs error, cosine, bf16 floor of the exact rows) of bf16 rows against float64 rows."""
+    g, e = got.double().flatten(), exact.double().flatten()
+    floor = (e.float().to(torch.bfloat16).double() - e).abs().max().item()
+    mae = (g - e).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(g[None], e[None]).item()
+    return mae, cos, floor
+
+
+def _reduce_parity(rows, world, device):
+    """Combine per-rank (mae, cos, floor, excess) lists: worst over heads and ranks."""
+    import torch.distributed as dist
+    mae = max(r[0] for r in rows)
+    cos = min(r[1] for r in rows)
+    excess = max(r[0] - (2e-2 + r[2]) for r in rows)
+    floor = max(r[2] for r in rows)
+    if world > 1:
+        t = torch.tensor([mae, -cos, excess, floor], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        mae, cos, excess, floor = t[0].item(), -t[1].item(), t[2].item(), t[3].item()
+    return {"max_abs": round(mae, 6), "cos": round(cos, 7), "bf16_floor": round(floor, 6),
+            "gate": "max_abs <= 2e-2 + bf16 rounding floor of the exact rows, cos >= 0.9995",
+            "heads_checked": list(PARITY_HEADS), "ranks_checked": world,
+            "reference": "float64 torch attention of the same inputs on each rank's GPU",
+            "ok": bool(excess <= 0.0 and cos >= 0.9995)}
+
+
+def verify_ulysses(prob, outs, rank, world, device):
+    """Parity of this rank's output rows (sequence shard ``rank``) for the sampled heads."""
+    import torch.distributed as dist
+    out_img, out_txt = outs
+    Lh, Li, Ls, Hl = prob["Lh"], prob["Li"], prob["Ls"], prob["Hl"]
+    cache, img, txt = prob["cache"], prob["img"], prob["txt"]
+    out_img = out_img.reshape(1, Ls, H_TOTAL, D)
+    out_txt = out_txt.reshape(1, TXT, H_TOTAL, D)
+    rows = []
+    for h in PARITY_HEADS:
+        owner, hl = h // Hl, h % Hl
+        hist = torch.empty((2, Lh, D), dtype=torch.bfloat16, device=device)
+        if rank == owner:   # the owner's head-sharded history, decoded as the reference decodes it
+            for i, n in enumerate("kv"):
+                hist[i] = (cache[n][0, :Lh, hl].float() * cache[f"{n}_scale"][0, :Lh, hl]).to(torch.bfloat16)
+        if world > 1:
+            dist.broadcast(hist, src=owner)
+        kv_img = []
+        for x in (img[1], img[2]):
+            mine = x[0, :, h].contiguous()
+            if world > 1:
+                parts = [torch.empty_like(mine) for _ in range(world)]
+                dist.all_gather(parts, mine)
+                mine = torch.cat(parts, 0)
+            kv_img.append(mine)
+        k = torch.cat([hist[0], kv_img[0], txt[1][0, :, h]], 0)
+        v = torch.cat([hist[1], kv_img[1], txt[2][0, :, h]], 0)
+        Lk = k.shape[0]
+        kpos = torch.arange(Lk, device=device)
+        kframe = torch.where((kpos >= Lh) & (kpos < Lh + Li), (kpos - Lh) // T, torch.full_like(kpos, -1))
+        qframe = (rank * Ls + torch.arange(Ls, device=device)) // T
+        vis = kframe[None, :] <= qframe[:, None]
+        exact_img = _exact_rows(img[0][0, :, h], k, v, vis)
+        exact_txt = _exact_rows(txt[0][0, :, h], k, v, torch.ones(TXT, Lk, dtype=torch.bool, device=device))
+        got = torch.cat([out_img[0, :, h], out_txt[0, :, h]], 0)
+        rows.append(_gate(got, torch.cat([exact_img, exact_txt], 0)))
+    return _reduce_parity(rows, world, device)
+
+
 def run_b200(args):
     from hy_nomas_b200 import _lib
     from hy_nomas_b200 import attention as hatt
@@ -369,6 +500,8 @@ def run_b200(args):
 
     for _ in range(args.warmup):
         step(*img, *txt)
+    torch.cuda.synchronize(device)
+    parity = verify_ulysses(prob, step(*img, *txt), rank, world, device)
     torch.cuda.synchronize(device)
     graph = None if args.no_graph else capture_step(lambda: step(*img, *txt), device)
     run_step = (lambda: step(*img, *txt)) if graph is None else graph.replay
@@ -413,9 +546,11 @@ def run_b200(args):
     kern = time_attention_kernel(prob, device, args.steps)
     cfg_no = 4 if args.workload == "config4" else 2
     peak_bf16, peak_hbm, peak_src = load_peaks()
+    fp8 = measure_fp8_peak(device) if rank == 0 else {"burst": None}
     local_flops = attention_flops(Lh, Li, TXT, Hl, D, True, T)
     achieved = local_flops / (kern["ms"] * 1e-3) / 1e12
-    traffic = load_traffic().get("attn_fwd_config2_bytes_per_launch") if args.workload == "config2" else None
+    tr = load_traffic() if args.workload == "config2" else {}
+    traffic = tr.get("attn_fwd_config2_bytes_per_launch")
     if traffic is not None and world > 1:
         traffic = traffic * Hl / H_TOTAL
 
@@ -427,11 +562,19 @@ def run_b200(args):
     if not args.no_graph:
         call.release()
     torch.cuda.synchronize(device)
+    config3 = None
+    if args.workload == "config2" and not args.no_config3:
+        # BASELINE config 3 (ring SP over the same ranks), reported beside config 2
+        del prob, cache, cmask, img, txt
+        torch.cuda.empty_cache()
+        config3 = ring_measurement(args, rank, world, device)
+    gpus = None
     if world > 1:
         from hy_nomas_b200 import communications as comm2
         from hy_nomas_b200 import parallel_states as ps2
         comm2.release_peer_exchanges()
         ps2.destroy_sequence_parallel_group()
+        gpus = _gpus_active(world, device)
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -439,7 +582,8 @@ def run_b200(args):
         "metric": METRIC if cfg_no == 2 else METRIC4, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
-        "vs_baseline": None, "dtype": "bf16 MMA / fp32 softmax; e4m3 KV cache", "data": "synthetic (seeded N(0,1), 4 outlier channels/head x8)",
+        "vs_baseline": None, "dtype": "bf16 Q.K^T / fp16 P.V MMAs, fp32 softmax; e4m3 KV cache",
+        "data": "synthetic (seeded N(0,1), 4 outlier channels/head x8)",
         "config": {"workload": ("config 2: 1x B200 single block (N>1: Ulysses SP over the same chunk)" if cfg_no == 2
                                 else "config 4: 4-frame chunk vs 48-frame FP8 cache (N>1: Ulysses SP)"),
                    "heads": H_TOTAL, "head_dim": D, "history_tokens": Lh, "chunk_image_tokens": Li,
@@ -460,37 +604,71 @@ def run_b200(args):
                 "ms_per_step": round(ems, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_bf16, "unit": "TFLOP/s",
                      "frac": round(achieved / peak_bf16, 4), "traffic": traffic,
-                     "kernel": "attn_fwd2_kernel (tcgen05 kind::f16, bf16 operands)",
+                     "traffic_source": tr.get("source"),
+                     "kernel": "attn_fwd2_kernel (tcgen05 kind::f16: bf16 Q.K^T, fp16 P.V)",
                      "kernel_ms": round(kern["ms"], 4), "peak_source": f"{peak_src} bf16 dense (cuBLAS)",
+                     "fp8_peak": fp8["burst"],
+                     "frac_of_fp8_peak": round(achieved / fp8["burst"], 4) if fp8["burst"] else None,
+                     "fp8_peak_source": "measured live: torch._scaled_mm e4m3 8192^3, best of 10",
                      "algorithmic_unit": "4*H*D FLOP per visible (query, key) pair"},
         "cpu_baseline": cpu,
         "clocks": clocks,
+        "parity": parity,
+        "gpus_active": gpus if gpus is not None else 1,
+        "config3": config3,
     }
     print(json.dumps(line), flush=True)
+
+
+def _gpus_active(world, device):
+    """Distinct physical GPUs (PCI bus ids) the ranks ran on."""
+    import torch.distributed as dist
+    bus = torch.cuda.get_device_properties(device).pci_bus_id if hasattr(
+        torch.cuda.get_device_properties(device), "pci_bus_id") else device.index
+    mine = torch.tensor([int(bus), device.index], dtype=torch.int64, device=device)
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine)
+    return len({tuple(x.tolist()) for x in parts})
 
 
 RING_FRAMES = 21
 RING_METRIC = "chunk-causal attn TFLOP/s (config 3: ring SP, 21 x 1560-token frame-causal sequence, FP8 KV blocks)"
 
 
-def run_ring(args):
+def _e4m3_decoded(x):
+    """bf16 [L, D] rows -> the bf16 values the ring's e4m3 blocks decode to: per row
+    s = absmax / 448 (1 for a zero row), codes = e4m3(x / s) (round to nearest even), value =
+    bf16(code * s); the quantise-on-write rule of the KV blocks restated for the check.  It runs
+    on the CPU: torch's float -> float8_e4m3fn cast on CUDA breaks some exact rounding ties
+    differently from IEEE round-to-nearest-even (about 1 % of rows differ by one code), the CPU
+    cast does not."""
+    dev = x.device
+    xf = x.float().cpu()
+    amax = xf.abs().amax(-1, keepdim=True)
+    sc = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    codes = (xf / sc).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return (codes.float() * sc).to(torch.bfloat16).to(dev)
+
+
+def ring_measurement(args, rank, world, device):
     """Config 3: frame-causal self-attention of 21 frames x 1560 tokens (32,760), 24 heads,
-    zig-zag sharded over N ranks; FP8 K/V blocks travel the ring (strong scaling)."""
+    zig-zag sharded over the ranks; FP8 K/V blocks travel the ring (strong scaling).  Returns
+    the measurement as a dict (the same on every rank: times are the max over ranks)."""
     from hy_nomas_b200 import _lib
     from hy_nomas_b200 import ring
     from hy_nomas_b200.flops import attention_flops
     from hy_nomas_b200.synthetic import make_generator, seeded_kv
     import torch.distributed as dist
 
-    rank, world, local = dist_setup(args.gpus)
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
     L = RING_FRAMES * T
     plan = ring.RingPlan(L, world, "zigzag")
     gen = make_generator(1237, device=device)
     # the same global sequence on every rank (seeded), each rank keeps its shard
     full = [seeded_kv((1, L, H_TOTAL, D), gen, device=device) for _ in range(3)]
     q, k, v = (plan.shard(x, rank).contiguous() for x in full)
+    # the sampled heads of the whole sequence, for the parity check
+    sampled = {h: (full[0][0, :, h].clone(), _e4m3_decoded(full[1][0, :, h]), _e4m3_decoded(full[2][0, :, h]))
+               for h in PARITY_HEADS}
     del full
     torch.cuda.empty_cache()
     flops_total = attention_flops(0, L, 0, H_TOTAL, D, False, T)
@@ -507,6 +685,19 @@ def run_ring(args):
     for _ in range(args.warmup):
         step(q, k, v)
     torch.cuda.synchronize(device)
+    # parity of this rank's rows (its two zig-zag chunks) for the sampled heads
+    step(q, k, v)
+    torch.cuda.synchronize(device)
+    seg0, pos0, pos1 = plan.positions(rank)
+    qpos = torch.cat([pos0 + torch.arange(seg0, device=device),
+                      pos1 + torch.arange(plan.length(rank) - seg0, device=device)])
+    kframe = torch.arange(L, device=device) // T
+    vis = kframe[None, :] <= (qpos // T)[:, None]
+    rows = []
+    for h, (qh, kh, vh) in sampled.items():
+        rows.append(_gate(out[0, :, h], _exact_rows(qh[qpos], kh, vh, vis)))
+    parity = _reduce_parity(rows, world, device)
+    del sampled, vis
     graph = None if args.no_graph else capture_step(lambda: step(q, k, v), device)
     run_step = (lambda: step(q, k, v)) if graph is None else graph.replay
     for _ in range(args.warmup):
@@ -514,7 +705,7 @@ def run_ring(args):
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(device.index)
     sampler.start()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -568,15 +759,9 @@ def run_ring(args):
     ring.release_ring_states()
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    line = {
+    return {
         "metric": RING_METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16 MMA / fp32 softmax; e4m3 KV blocks on the ring",
-        "data": "synthetic (seeded N(0,1), 4 outlier channels/head x8)",
+        "ms_per_step": round(ms, 4), "scaling": "strong",
         "config": {"workload": "config 3: ring SP, 21 frames x 1560 tokens, frame-causal", "heads": H_TOTAL,
                    "head_dim": D, "seq_len": L, "tokens_per_frame": T, "layout": "zig-zag (2N chunks)",
                    "parallelism": f"ring_sp{world}" if world > 1 else "single",
@@ -592,13 +777,32 @@ def run_ring(args):
                 "ms_per_step": round(ems, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_bf16, "unit": "TFLOP/s",
                      "frac": round(achieved / peak_bf16, 4), "traffic": None,
-                     "kernel": "attn_fwd2_kernel (tcgen05 kind::f16, bf16 operands)",
+                     "kernel": "attn_fwd2_kernel (tcgen05 kind::f16: bf16 Q.K^T, fp16 P.V)",
                      "kernel_ms_per_step": round(kern_ms, 4), "kernel_ms_max_rank": round(kern_ms_max, 4),
                      "peak_source": f"{peak_src} bf16 dense (cuBLAS)",
                      "algorithmic_unit": "4*H*D FLOP per visible (query, key) pair"},
-        "cpu_baseline": None,
+        "parity": parity,
         "clocks": clocks,
     }
+
+
+def run_ring(args):
+    """Config 3 on its own line (``--workload ring``)."""
+    import torch.distributed as dist
+    rank, world, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    m = ring_measurement(args, rank, world, device)
+    gpus = _gpus_active(world, device) if world > 1 else 1
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = dict(m)
+    line.update({"steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
+                 "dtype": "bf16 Q.K^T / fp16 P.V MMAs, fp32 softmax; e4m3 KV blocks on the ring",
+                 "data": "synthetic (seeded N(0,1), 4 outlier channels/head x8)", "cpu_baseline": None,
+                 "gpus_active": gpus})
     print(json.dumps(line), flush=True)
 
 
@@ -814,6 +1018,10 @@ def run_reference(args):
 
 def main():
     args = parse()
+    if args.measure_fp8_peak:
+        print(json.dumps({"fp8_e4m3_gemm_tflops": measure_fp8_peak(torch.device("cuda", 0), sustained_s=4.0),
+                          "how": "torch._scaled_mm e4m3 8192^3, best of 10 (burst) and back to back for 4 s"}))
+        return
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "ring":

@@ -16,7 +16,7 @@ import torch
 PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libhyb200.so"
 
-HYB_ABI_VERSION = 2
+HYB_ABI_VERSION = 3
 
 HYB_OK = 0
 HYB_ERR_INVALID_ARG = -1
@@ -119,7 +119,7 @@ SIGNATURES = {
                                     c_ptr]),
     "hyb_ring_gather_stage": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(c_ptr), c_i32,
                                       ctypes.POINTER(c_i32), ctypes.POINTER(c_i32), ctypes.POINTER(c_i32),
-                                      c_ptr, c_ptr, c_ptr]),
+                                      c_ptr, c_ptr, c_i32, c_ptr]),
     "hyb_peer_open": (c_i32, [c_ptr, ctypes.POINTER(c_ptr)]),
     "hyb_peer_close": (c_i32, [c_ptr]),
     "hyb_peer_free": (c_i32, [c_ptr]),
@@ -153,6 +153,7 @@ SIGNATURES = {
     "hyb_ulysses_unpack_o": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr,
                                      c_i64, c_i64, c_i64, c_ptr]),
     "hyb_exp2_poly_eval": (c_i32, [c_ptr, c_ptr, c_i64, c_ptr]),
+    "hyb_peer_barrier": (c_i32, [c_i32, c_i32, ctypes.POINTER(PeerSync), c_ptr]),
 }
 
 _LIB = None

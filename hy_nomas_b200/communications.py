@@ -28,36 +28,43 @@ from . import _lib
 
 @dataclass(frozen=True)
 class SPCommunicationMetadata:
-    """Host-side sizes shared by all attention layers in one model forward."""
+    """Per-rank sizes of one sequence-parallel model forward: ``sequence_lengths[r]`` image tokens
+    held by rank r before the sequence->head exchange, ``head_sizes[r]`` heads held after it.
+    The type and its two field names are what the reference's block passes as ``sp_metadata``
+    and reads back (hymm/distributed/communications.py:16-21)."""
 
     sequence_lengths: Tuple[int, ...]
     head_sizes: Tuple[int, ...]
 
 
 def prepare_sp_communication(local_sequence_length, heads, device, group):
-    """Exchange sequence/head sizes once, before the layer loop (one host sync)."""
-    world_size = dist.get_world_size(group)
-    local = torch.tensor([[local_sequence_length, heads]], dtype=torch.int64, device=device)
-    if world_size > 1:
-        sizes = torch.empty((world_size, 2), dtype=torch.int64, device=device)
-        dist.all_gather_into_tensor(sizes, local, group=group)
-    else:
-        sizes = local
-    rows = sizes.tolist()
-    sequence_lengths = tuple(row[0] for row in rows)
-    all_heads = tuple(row[1] for row in rows)
-    if any(length < 0 for length in sequence_lengths):
+    """Gather every rank's (tokens, heads) once per forward so the per-layer exchanges need no
+    size collectives (the reference's helper of the same name, communications.py:24-43).  The
+    table crosses to the host once; heads must agree across ranks and divide by the group size,
+    otherwise ValueError with the reference's messages."""
+    ranks = dist.get_world_size(group)
+    mine = torch.tensor([local_sequence_length, heads], dtype=torch.int64, device=device).unsqueeze(0)
+    table = mine
+    if ranks > 1:
+        table = mine.new_empty((ranks, 2))
+        dist.all_gather_into_tensor(table, mine, group=group)
+    per_rank = [tuple(pair) for pair in table.cpu().tolist()]
+    tokens = tuple(t for t, _ in per_rank)
+    if min(tokens) < 0:
         raise ValueError("SP sequence lengths must be nonnegative")
-    if len(set(all_heads)) != 1 or heads <= 0 or heads % world_size:
+    if {h for _, h in per_rank} != {heads} or heads <= 0 or heads % ranks != 0:
         raise ValueError("SP ranks require identical head counts divisible by SP size")
-    return SPCommunicationMetadata(sequence_lengths, (heads // world_size,) * world_size)
+    return SPCommunicationMetadata(tokens, (heads // ranks,) * ranks)
 
 
 def _validate_sizes(sizes, world_size):
-    sizes = tuple(sizes)
-    if len(sizes) != world_size or any(type(size) is not int or size < 0 for size in sizes):
+    """Per-rank sizes as a tuple of nonnegative Python ints, one per rank, else ValueError with the
+    reference's message."""
+    out = tuple(sizes)
+    well_formed = len(out) == world_size and all(type(n) is int and n >= 0 for n in out)
+    if not well_formed:
         raise ValueError("Expected one nonnegative Python integer size per process-group rank")
-    return sizes
+    return out
 
 
 def exchange(send: torch.Tensor, group) -> torch.Tensor:
@@ -242,18 +249,43 @@ def _bf16_tensor(ptr: int, shape, device) -> torch.Tensor:
     return torch.as_tensor(_DeviceArray(ptr, shape, "<i2"), device=device).view(torch.bfloat16)
 
 
+def require_same_on_every_rank(group, values, what: str, device=None) -> None:
+    """Raise ValueError on every rank of ``group`` unless all ranks passed the same integers.
+
+    The push kernels write into the other ranks' buffers with this rank's sizes, so ranks that
+    disagree on a buffer size or a geometry would write past a peer's allocation (a device fault,
+    where the reference's collectives fail with an error); this collective check runs before
+    any buffer is allocated or written."""
+    vals = [int(v) for v in values]
+    n = len(vals)
+    dev = torch.device(device) if device is not None else torch.device("cpu")
+    mine = torch.tensor([n] + vals, dtype=torch.int64, device=dev)
+    world = dist.get_world_size(group)
+    counts = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(world)]
+    dist.all_gather(counts, mine[:1], group=group)
+    if len({int(c.item()) for c in counts}) != 1:
+        raise ValueError(f"{what}: ranks disagree on the number of sizes ({[int(c.item()) for c in counts]})")
+    rows = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(rows, mine, group=group)
+    table = [tuple(int(x) for x in r.tolist()[1:]) for r in rows]
+    if len(set(table)) != 1:
+        raise ValueError(f"{what}: ranks disagree on sizes / geometry: {table}")
+
+
 class PeerBuffers:
     """Device buffers every rank of ``group`` maps with CUDA IPC, plus the flag arrays of the
     device barrier that ends each push kernel.  ``ptrs[i][r]`` is buffer i of rank r as mapped
-    in this process; ``local[i]`` is this rank's own."""
+    in this process; ``local[i]`` is this rank's own.  Every rank must request the same sizes
+    (and pass the same ``geometry``): checked collectively first, ValueError on every rank."""
 
-    def __init__(self, group, sizes, device):
+    def __init__(self, group, sizes, device, geometry=()):
         self.group = group
         self.P = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.device = torch.device(device)
         self.lib = lib = _lib.load()
         sizes = [max(int(n), 256) for n in sizes] + [256]   # last: the barrier flags int32[<= 64]
+        require_same_on_every_rank(group, list(sizes) + [int(g) for g in geometry], "peer buffers", self.device)
         self.sizes = sizes
         self.local = []
         self._opened = []
@@ -321,7 +353,8 @@ class PeerExchange:
         self.lib = _lib.load()
         Hp, D = self.Hp, 128
         recv_bytes = P * Ls * 3 * B * Hp * D * 2
-        self.buf = PeerBuffers(group, [recv_bytes, recv_bytes, B * Ls * H * D * 2, B * Lt * H * D * 2], device)
+        self.buf = PeerBuffers(group, [recv_bytes, recv_bytes, B * Ls * H * D * 2, B * Lt * H * D * 2], device,
+                               geometry=(B, Ls, H, Lt))
         recv_shape = (P, Ls, 3 * B, Hp, D)
         self.recv = [_bf16_tensor(self.buf.local[0], recv_shape, self.device),
                      _bf16_tensor(self.buf.local[1], recv_shape, self.device)]

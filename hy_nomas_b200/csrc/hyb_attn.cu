@@ -862,6 +862,7 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
 constexpr int kMaxGatherChunks = 128;
 struct GatherParams {
   int L, H, Lmax, fmt, nchunks;
+  int v_f16;  // 1: V written in fp16 (the bf16 decode, converted exactly) for a P.V in fp16
   const uint8_t* blocks[64];
   int bounds[kMaxGatherChunks + 1];
   int owner[kMaxGatherChunks];
@@ -910,8 +911,10 @@ __global__ void __launch_bounds__(256) gather_stage_kernel(const GatherParams p)
       load_row8(sg, 0, row, h, sub, v);
       uint4 packed;
       uint32_t* w = reinterpret_cast<uint32_t*>(&packed);
+      const bool f16 = o == 1 && p.v_f16;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      for (int i = 0; i < 4; ++i)
+        w[i] = f16 ? pack_f16x2(bf16_round(v[2 * i]), bf16_round(v[2 * i + 1])) : pack_bf16x2(v[2 * i], v[2 * i + 1]);
       *reinterpret_cast<uint4*>((o == 0 ? p.out_k : p.out_v) + out_off) = packed;
     }
   }
@@ -1479,7 +1482,7 @@ extern "C" int hyb_stage_head_major(int32_t B, int32_t L, int32_t H, int32_t D, 
 extern "C" int hyb_ring_gather_stage(int32_t P, int32_t fmt, int32_t L, int32_t H, int32_t D, int32_t Lmax,
                                      const void* const* blocks, int32_t nchunks, const int32_t* bounds,
                                      const int32_t* owner, const int32_t* row0, void* out_k, void* out_v,
-                                     void* stream) {
+                                     int32_t v_f16, void* stream) {
   if (D != kHD) return fail(HYB_ERR_UNSUPPORTED, "gather stage: head_dim %d != 128", D);
   if (fmt != HYB_FMT_E4M3 && fmt != HYB_FMT_INT8) return fail(HYB_ERR_UNSUPPORTED, "gather stage: format %d", fmt);
   if (P <= 0 || P > 64 || L < 0 || H <= 0 || Lmax <= 0 || nchunks <= 0 || nchunks > kMaxGatherChunks ||
@@ -1491,6 +1494,7 @@ extern "C" int hyb_ring_gather_stage(int32_t P, int32_t fmt, int32_t L, int32_t 
   p.Lmax = Lmax;
   p.fmt = fmt;
   p.nchunks = nchunks;
+  p.v_f16 = v_f16 != 0;
   for (int r = 0; r < P; ++r) {
     if (blocks[r] == nullptr || (reinterpret_cast<uintptr_t>(blocks[r]) & 15u))
       return fail(HYB_ERR_INVALID_ARG, "gather stage: block %d", r);
@@ -1716,15 +1720,50 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 namespace {
 constexpr int kMaxDevices = 128;
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kMaxDevices] = {};  // device address of g_noalloc_scratch, per device
+// Device address of g_noalloc_scratch per device, and the unique id of the CUDA context it was
+// resolved in: a context that was reset and created again loads the module anew, so the
+// address is looked up again there instead of reusing a stale one.
+void* g_noalloc_addr[kMaxDevices] = {};
+unsigned long long g_noalloc_ctx[kMaxDevices] = {};
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current CUDA context (0 if it cannot be read).
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(f);
+    looked_up = true;
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
 }  // namespace
 
 extern "C" int hyb_cached_attention_noalloc(const hyb_cached_attn_args* a, void* stream) {
   if (a == nullptr || a->abi_version != HYB_ABI_VERSION)
     return fail(HYB_ERR_INVALID_ARG, "cached attention (no-alloc): null args or ABI version mismatch");
+  if (a->D != kHD) return fail(HYB_ERR_UNSUPPORTED, "cached attention (no-alloc): head_dim %d != 128", a->D);
+  if (a->B <= 0 || a->H <= 0 || a->valid_len < 0 || a->img_len < 0 || a->txt_len < 0 || a->group_tokens < 0)
+    return fail(HYB_ERR_INVALID_ARG, "cached attention (no-alloc): negative sizes");
   const int64_t need = hyb_cached_attention_workspace_bytes(a->B, a->H, a->D, a->valid_len, a->img_len,
                                                             a->txt_len, a->attend_txt);
-  if (need < 0) return fail(HYB_ERR_UNSUPPORTED, "cached attention (no-alloc): head_dim must be 128");
+  if (need < 0) return fail(HYB_ERR_INVALID_ARG, "cached attention (no-alloc): unsupported sizes");
   if (need > kNoAllocScratchBytes)
     return fail(HYB_ERR_WORKSPACE,
                 "cached attention (no-alloc): these sizes need %lld bytes of staging scratch but the "
@@ -1734,16 +1773,19 @@ extern "C" int hyb_cached_attention_noalloc(const hyb_cached_attn_args* a, void*
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(HYB_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(HYB_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  const unsigned long long ctx = current_context_id();
   void* scratch = nullptr;
   {
-    // First call on a device (with that device current): resolve the array's device address.
+    // First call on a device (and in each new context of it), with that device current:
+    // resolve the array's device address.
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_addr[dev] == nullptr) {
+    if (g_noalloc_addr[dev] == nullptr || ctx == 0 || g_noalloc_ctx[dev] != ctx) {
       void* addr = nullptr;
       e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
       if (e != cudaSuccess)
         return fail(HYB_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
       g_noalloc_addr[dev] = addr;
+      g_noalloc_ctx[dev] = ctx;
     }
     scratch = g_noalloc_addr[dev];
   }

@@ -348,6 +348,12 @@ __global__ void __launch_bounds__(256) push_bytes_kernel(const PushBytesParams p
   grid_signal_and_wait(p.sync);
 }
 
+// A barrier alone (one block): every rank arrives when its stream reaches this launch, i.e.
+// after every earlier kernel on it, and waits (bounded) for all the others.  Placed before a
+// push into buffers that the other ranks read after the previous push's barrier, it orders
+// their reads of the previous call before this call's writes.
+__global__ void __launch_bounds__(64) barrier_kernel(const PeerSync s) { grid_signal_and_wait(s); }
+
 int peer_sync_of(const hyb_peer_sync* ps, int P, int rank, PeerSync* out) {
   if (ps == nullptr || ps->state == nullptr) return fail(HYB_ERR_INVALID_ARG, "peer sync: null state");
   out->P = P;
@@ -574,6 +580,17 @@ extern "C" int hyb_ulysses_push_o(int32_t P, int32_t rank, int32_t B, int32_t Ls
   if (rc != HYB_OK) return rc;
   const long long chunks = static_cast<long long>(P) * (static_cast<long long>(p.Hp) * Ls * B + static_cast<long long>(B) * Lt * p.Hp) * 16;
   push_o_kernel<<<grid_for(chunks > 0 ? chunks : 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
+
+extern "C" int hyb_peer_barrier(int32_t P, int32_t rank, const hyb_peer_sync* sync, void* stream) {
+  if (P <= 1 || P > kMaxRanks || rank < 0 || rank >= P)
+    return fail(HYB_ERR_INVALID_ARG, "peer barrier: bad arguments (2..%d ranks)", kMaxRanks);
+  PeerSync s;
+  int rc = peer_sync_of(sync, P, rank, &s);
+  if (rc != HYB_OK) return rc;
+  barrier_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(s);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }

@@ -304,7 +304,9 @@ class GatherAttention:
     kernel then decodes all P blocks into a head-major bf16 K/V of the whole sequence in
     position order, and one attention launch covers this rank's query chunks against it.
     Moves the same bytes per rank as the neighbour ring (P - 1 blocks in, P - 1 out) without
-    P attention launches and partial merges.  ``emulate=True`` runs every rank in one process
+    P attention launches and partial merges.  A device barrier before each push keeps a call's
+    writes behind every peer's decode of the previous call's blocks (one block buffer per rank,
+    safe under CUDA-graph replay because the barrier's epochs live in device memory).  ``emulate=True`` runs every rank in one process
     over a shared local buffer (tests on one GPU)."""
 
     def __init__(self, plan: RingPlan, rank: int, heads: int, device, *, tokens_per_frame: int,
@@ -325,7 +327,7 @@ class GatherAttention:
             self._keep = shared
         elif P > 1:
             from .communications import PeerBuffers
-            self.peers = PeerBuffers(group, [P * self.block_bytes], dev)
+            self.peers = PeerBuffers(group, [P * self.block_bytes], dev, geometry=(L, H, Lmax, self.code_fmt))
             base = self.peers.local[0]
             self._push_dst = self.peers.table(0, offset=rank * self.block_bytes)
         else:
@@ -365,6 +367,12 @@ class GatherAttention:
 
     def exchange(self, stream: int) -> None:
         if self.peers is not None:
+            # Every peer decodes the blocks of the previous call after that call's push barrier
+            # (hyb_ring_gather_stage on its stream), so this call's push may overwrite them only
+            # once every rank has passed the entry barrier, i.e. finished that decode.
+            _lib.check(self.lib.hyb_peer_barrier(self.plan.world, self.rank, ctypes.byref(self.peers.sync), stream),
+                       "ring block barrier")
+            self.launches += 1
             _lib.check(self.lib.hyb_peer_push_bytes(self.plan.world, self.rank, self.slots[self.rank].buf.data_ptr(),
                                                     self.block_bytes, self._push_dst, ctypes.byref(self.peers.sync),
                                                     stream), "ring block push")
@@ -376,9 +384,10 @@ class GatherAttention:
         _lib.check(self.lib.hyb_stage_head_major(1, Ls, H, _D, ctypes.byref(qv), None, self.qh.data_ptr(), None,
                                                  stream), "ring stage q")
         kv_k, kv_v = self.kv[0].data_ptr(), self.kv[1].data_ptr()
+        # V (and so P.V's softmax weights) in fp16: the bf16 decode converted exactly
         _lib.check(self.lib.hyb_ring_gather_stage(plan.world, self.code_fmt, L, H, _D, self.Lmax, self.block_tab,
                                                   self.nchunks, self.bounds, self.owner, self.row0, kv_k, kv_v,
-                                                  stream), "ring gather stage")
+                                                  1, stream), "ring gather stage")
         a = _lib.AttnArgs()
         a.abi_version = _lib.HYB_ABI_VERSION
         a.B, a.H, a.D, a.Lq, a.Lk = 1, H, _D, Ls, L
@@ -396,6 +405,7 @@ class GatherAttention:
         a.lse = lse.data_ptr() if lse is not None else None
         a.dev_status = self.status.data_ptr()
         a.kv_splits = self.kv_splits
+        a.v_f16 = 1
         if self.kv_splits > 1:
             a.part_o, a.part_lse = self.part_o.data_ptr(), self.part_lse.data_ptr()
         if self.event_log is not None:

@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define HYB_ABI_VERSION 2
+#define HYB_ABI_VERSION 3
 
 /* status codes */
 #define HYB_OK 0
@@ -220,12 +220,13 @@ int hyb_stage_head_major(int32_t B, int32_t L, int32_t H, int32_t D, const hyb_t
 /* Sequence-parallel K/V blocks of P ranks -> head-major bf16 K and V [H, L, 128] of the whole
  * sequence.  Block r (blocks[r], as mapped here) is [K codes | V codes | K scales | V scales]
  * for Lmax rows of H heads; position pos in chunk c ([bounds[c], bounds[c+1])) is row
- * row0[c] + pos - bounds[c] of block owner[c].  Decode as hyb_kv_dequant.  Replaces the
- * per-step kv buffers of the reference ring (dynamic_ring_attention.py:115-286). */
+ * row0[c] + pos - bounds[c] of block owner[c].  Decode as hyb_kv_dequant; with v_f16 = 1 the
+ * decoded bf16 V is stored as fp16 (exact), the operand of hyb_attn_fwd with v_f16 = 1.
+ * Replaces the per-step kv buffers of the reference ring (dynamic_ring_attention.py:115-286). */
 int hyb_ring_gather_stage(int32_t P, int32_t fmt, int32_t L, int32_t H, int32_t D, int32_t Lmax,
                           const void* const* blocks, int32_t nchunks, const int32_t* bounds,
                           const int32_t* owner, const int32_t* row0, void* out_k, void* out_v,
-                          void* stream);
+                          int32_t v_f16, void* stream);
 
 /* Key-visibility bitmap for hyb_attn_fwd with keys [0, Lk) of every batch row visible:
  * bits [B, kwords] uint32.  No reference counterpart (the reference ring attends every key of
@@ -278,6 +279,13 @@ int hyb_ulysses_push_o(int32_t P, int32_t rank, int32_t B, int32_t Ls, int32_t L
                        const void* o_send, const hyb_tensor4* txt, void* const* out, void* const* txt_out,
                        const hyb_peer_sync* sync, void* stream);
 
+/* The device barrier alone (one block): each rank arrives once its stream reaches the launch
+ * and waits, bounded, for every other rank (HYB_DEV_TIMEOUT in dev_status after ~2 s).  No
+ * reference counterpart (the reference's NCCL send/recv pairs each transfer with its own
+ * receive, dynamic_ring_attention.py:45-83); ring_attention's all-gather schedule launches it
+ * before pushing a call's blocks, so no rank overwrites a block a peer is still decoding. */
+int hyb_peer_barrier(int32_t P, int32_t rank, const hyb_peer_sync* sync, void* stream);
+
 /* All-gather contribution over peer memory: `bytes` (a multiple of 16) from src to dst[d] on
  * every rank d (skipping dst[d] == src), then the barrier.  The ring schedule of
  * ring_attention passes its e4m3 K/V blocks this way (every block to every rank at once over
@@ -308,9 +316,10 @@ int hyb_ulysses_unpack_o(int32_t P, int32_t B, int32_t Ls, int32_t Ls_max, int32
  * ignored and the staging scratch is a fixed 64 MiB array of static device memory inside
  * this library, which every GPU that loads the library holds until the process exits.
  * Sizes whose scratch (hyb_cached_attention_workspace_bytes) exceeds 64 MiB are rejected
- * with HYB_ERR_WORKSPACE.  The first call on each device looks up the array's device
- * address (cudaGetSymbolAddress) with that device current; make that first call before any
- * stream capture.  The function calls no allocator.  All calls on a device share the one
+ * with HYB_ERR_WORKSPACE; negative sizes with HYB_ERR_INVALID_ARG.  The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress) with that device current,
+ * and so does the first call in a context created anew after a device reset; make those first
+ * calls before any stream capture.  The function calls no allocator.  All calls on a device share the one
  * array, so calls that can overlap on the GPU (different streams, or concurrent host
  * threads) race on it and must be serialised by the caller. */
 int hyb_cached_attention_noalloc(const hyb_cached_attn_args* args, void* stream);

@@ -48,7 +48,7 @@ int main(void) {
   F(hyb_cached_attn_args, out_txt) F(hyb_cached_attn_args, lse) F(hyb_cached_attn_args, workspace_bytes)
   F(hyb_cached_attn_args, dev_status)
   F(hyb_attn_args, q) F(hyb_attn_args, kwords) F(hyb_attn_args, qbits) F(hyb_attn_args, oi_sseg)
-  F(hyb_attn_args, lse) F(hyb_attn_args, dev_status) F(hyb_attn_args, kv_splits) F(hyb_attn_args, part_lse)
+  F(hyb_attn_args, lse) F(hyb_attn_args, dev_status) F(hyb_attn_args, kv_splits) F(hyb_attn_args, v_f16) F(hyb_attn_args, part_lse)
   F(hyb_attn_args, img_k_len) F(hyb_attn_args, k_pos1) F(hyb_attn_args, acc_o) F(hyb_attn_args, acc_mode)
   printf("hyb_peer_sync %zu\n", sizeof(hyb_peer_sync));
   F(hyb_peer_sync, state) F(hyb_peer_sync, dev_status)

@@ -112,3 +112,40 @@ def test_ulysses_layouts_over_gloo_match_reference():
 def test_dead_peer_is_reported_not_hung():
     res = _run(_worker_dead_peer)
     assert res[0] == "ok", res[0]
+
+
+def _worker_size_agreement(rank, world, init_file, result_dir):
+    import sys
+    sys.path.insert(0, str(REPO))
+    status = "ok"
+    try:
+        from hy_nomas_b200 import communications as comm
+        _init(rank, world, init_file)
+        # the same sizes on every rank pass
+        comm.require_same_on_every_rank(None, [4096, 4096, 256, 1, 780, 24, 1], "peer buffers")
+        # one rank with another geometry: every rank raises before any buffer exists
+        mine = [4096, 256, 780 if rank == 0 else 781]
+        try:
+            comm.require_same_on_every_rank(None, mine, "peer buffers")
+            status = "no error for disagreeing sizes"
+        except ValueError as e:
+            assert "disagree" in str(e), str(e)
+        # a different number of sizes is caught as well, without a mismatched collective
+        try:
+            comm.require_same_on_every_rank(None, [1, 2, 3][:2 + rank], "peer buffers")
+            status = "no error for a different count"
+        except ValueError as e:
+            assert "number of sizes" in str(e), str(e)
+        dist.destroy_process_group()
+    except Exception:
+        status = traceback.format_exc()
+    with open(os.path.join(result_dir, f"r{rank}"), "w") as f:
+        f.write(status)
+
+
+def test_peer_buffer_sizes_are_checked_on_every_rank():
+    """Peer buffers are sized from each rank's own geometry; ranks that disagree raise
+    ValueError on every rank before anything is allocated (a write past a peer's buffer would
+    be a device fault)."""
+    res = _run(_worker_size_agreement)
+    assert res == {0: "ok", 1: "ok"}, res

@@ -110,3 +110,19 @@ def test_no_alloc_entry_point_rejects_oversized_problems():
     rc = lib.hyb_cached_attention_noalloc(ctypes.byref(args), torch.cuda.current_stream(dev).cuda_stream)
     assert rc == _lib.HYB_ERR_WORKSPACE
     assert "fixed per-device scratch" in _lib.last_error()
+
+
+def test_no_alloc_entry_point_reports_negative_sizes_as_invalid_arguments():
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    cache, cur, hmask, tmask = _case(304, dev, H=1, Lh=64, Li=32, Lt=3)
+    out_img = torch.empty(1, 32, 1, 128, dtype=torch.bfloat16, device=dev)
+    out_txt = torch.empty(1, 3, 1, 128, dtype=torch.bfloat16, device=dev)
+    args = _args(cache, cur, hmask, tmask, out_img, out_txt, 0)
+    args.valid_len = -5
+    rc = lib.hyb_cached_attention_noalloc(ctypes.byref(args), torch.cuda.current_stream(dev).cuda_stream)
+    assert rc == _lib.HYB_ERR_INVALID_ARG
+    assert "negative sizes" in _lib.last_error()
+    args.valid_len, args.D = 64, 64
+    rc = lib.hyb_cached_attention_noalloc(ctypes.byref(args), torch.cuda.current_stream(dev).cuda_stream)
+    assert rc == _lib.HYB_ERR_UNSUPPORTED
