@@ -54,6 +54,9 @@ def parse():
                          "each upload / compute / read-back, and the host link alone; printed to stderr")
     ap.add_argument("--ring-schedule", default="allgather", choices=["allgather", "ring"],
                     help="ring workload: every block to every rank over peer memory, or neighbour passing")
+    ap.add_argument("--library-comparison", action="store_true",
+                    help="time this kernel and flashinfer's CUTLASS sm100a FMHA (fmha_varlen) on the same bf16 "
+                         "Q/K/V of config-2 size, chunk-bidirectional, and print both (one GPU)")
     ap.add_argument("--measure-fp8-peak", action="store_true",
                     help="print the dense FP8 GEMM peak of this GPU (burst and 4 s sustained) and exit")
     ap.add_argument("--no-config3", action="store_true",
@@ -1016,8 +1019,74 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def library_comparison(steps):
+    """Config-2 shapes (24 heads x 128, 6,241 queries against 31,201 keys), every key visible
+    (chunk-bidirectional: a frame-causal mask is not expressible in the library call), bf16
+    Q/K/V resident in HBM: device time of this library's attention launch (hyb_attn_fwd on the
+    staged operands) and of flashinfer's CUTLASS sm100a FMHA (fmha_varlen), the Blackwell
+    library kernel closest to the incumbent FA4 / MagiAttention kernels (not installed here).
+    A comparison column only: the library kernel is never on this repository's path."""
+    import flashinfer
+    from hy_nomas_b200 import _lib
+    from hy_nomas_b200 import attention as hatt
+    from hy_nomas_b200.synthetic import make_generator, seeded_kv
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    H, Lh, Li, Lt = H_TOTAL, HIST_FRAMES * T, CHUNK_FRAMES * T, TXT
+    gen = make_generator(77, device=dev)
+    hist = {"k": seeded_kv((1, Lh, H, D), gen, device=dev), "v": seeded_kv((1, Lh, H, D), gen, device=dev)}
+    cur = [seeded_kv((1, L, H, D), gen, device=dev) for L in (Li, Lt) for _ in range(3)]
+    ws = hatt.Workspace()
+    hatt.cached_attention_local(*cur, hist, Lh, group_tokens=0, workspace=ws)
+    lib = _lib.load()
+    args = ws.attn_args
+    stream = torch.cuda.current_stream(dev)
+
+    def ours():
+        _lib.check(lib.hyb_attn_fwd(args, stream.cuda_stream), "attention")
+
+    q = torch.cat([cur[0], cur[3]], 1)[0].contiguous()                      # [Lq, H, D]
+    k = torch.cat([hist["k"], cur[1], cur[4]], 1)[0].contiguous()           # [Lk, H, D]
+    v = torch.cat([hist["v"], cur[2], cur[5]], 1)[0].contiguous()
+    qo = torch.tensor([0, q.shape[0]], dtype=torch.int32, device=dev)
+    kvo = torch.tensor([0, k.shape[0]], dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+
+    def theirs():
+        flashinfer.prefill.fmha_varlen(q, k, v, qo, kvo, out=out, causal=False, sm_scale=D ** -0.5)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    from hy_nomas_b200.flops import attention_flops
+    fl = attention_flops(Lh, Li, Lt, H, D, True, 0)
+    ms_ours, ms_lib = timed(ours), timed(theirs)
+    o_ours = ws.keep[0]
+    ref_rows = out[:Li].float()
+    agree = (o_ours[0].float() - ref_rows).abs().max().item()
+    return {"workload": "config-2 shapes, chunk-bidirectional, bf16 Q/K/V resident", "tflop": round(fl / 1e12, 4),
+            "this_kernel": {"ms": round(ms_ours, 4), "tflops": round(fl / ms_ours / 1e9, 1),
+                            "kernel": "attn_fwd2_kernel (bf16 Q.K^T, fp16 P.V; operands staged by the call)"},
+            "flashinfer_fmha_varlen": {"ms": round(ms_lib, 4), "tflops": round(fl / ms_lib / 1e9, 1),
+                                       "version": flashinfer.__version__,
+                                       "kernel": "CUTLASS sm100a FMHA (bf16, non-causal)"},
+            "max_abs_difference_image_rows": round(agree, 5)}
+
+
 def main():
     args = parse()
+    if args.library_comparison:
+        print(json.dumps(library_comparison(max(args.steps, 10))), flush=True)
+        return
     if args.measure_fp8_peak:
         print(json.dumps({"fp8_e4m3_gemm_tflops": measure_fp8_peak(torch.device("cuda", 0), sustained_s=4.0),
                           "how": "torch._scaled_mm e4m3 8192^3, best of 10 (burst) and back to back for 4 s"}))
