@@ -987,24 +987,71 @@ def cpu_baseline(heads, reps=2):
                       f"{reps} reps, {dt:.2f} s per step"}
 
 
+def reference_problem(heads, seed=1236):
+    """Config 2 for the reference's own function: the history quantised into an INT8 cache by
+    the reference quantiser (int8_kv_cache.py:161-179), the chunk's Q/K/V in bf16."""
+    import importlib
+    from hy_nomas_b200.synthetic import make_generator, seeded_kv
+    i8 = importlib.import_module("hymm.models.dit.modules.int8_kv_cache")
+    gen = make_generator(seed)
+    Lh, Li = HIST_FRAMES * T, CHUNK_FRAMES * T
+    cap = Lh + Li + TXT
+    cache = i8.make_int8_kv_block(1, cap, heads, D, device="cpu")
+    i8.quantize_kv_pair_into(cache, seeded_kv((1, Lh, heads, D), gen), seeded_kv((1, Lh, heads, D), gen), 0)
+    cur = [seeded_kv((1, L, heads, D), gen) for L in (Li, TXT) for _ in range(3)]
+    return dict(cache=cache, cur=cur, Lh=Lh, Li=Li)
+
+
+def reference_step(native, p):
+    """One config-2 chunk through the reference's causal_attention_with_cache_mp (torch mode,
+    nomas_cpt.py:335-884): one call per query frame, frame f attending the history, the
+    chunk's earlier frames (written into the INT8 cache by the previous call's update_cache)
+    and itself, which is the frame-level block-causal rule."""
+    cache = {k: (t.clone() if isinstance(t, torch.Tensor) else t) for k, t in p["cache"].items()}
+    iq, ik, iv, tq, tk, tv = p["cur"]
+    with torch.no_grad():
+        for f in range(CHUNK_FRAMES):
+            sl = slice(f * T, (f + 1) * T)
+            native.causal_attention_with_cache_mp(
+                (iq[:, sl], tq), (ik[:, sl], tk), (iv[:, sl], tv), cache, cache_valid_len=p["Lh"] + f * T,
+                attn_mode="torch", text_mask=None, update_cache=True, cache_txt=False, cache_mask=None)
+
+
 def run_reference(args):
+    """The reference arm: the reference's own CPU implementation of the path on the host cores.
+    Where HY_NOMAS_REF names a reference checkout, its causal_attention_with_cache_mp itself
+    (kind "reference"); elsewhere (the GPU boxes carry no checkout) the oracle restatement of
+    the same path (kind "port")."""
     if args.gpus > 1:
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
     from hy_nomas_b200.flops import attention_flops
+    from oracle import reference as oref
     torch.set_num_threads(os.cpu_count() or 1)
     heads = args.cpu_heads
-    p = cpu_problem(heads)
+    if oref.checkout() is not None:
+        import importlib
+        oref.install_stub()
+        native = importlib.import_module("hymm.models.dit.nomas_cpt")
+        p = reference_problem(heads)
+        kind = "reference"
+        sample = (f"config 2 with {heads} of {H_TOTAL} heads per step: causal_attention_with_cache_mp "
+                  f"(attn_mode='torch', INT8 cache, update_cache per frame), one call per query frame")
+        step = lambda: reference_step(native, p)  # noqa: E731
+    else:
+        p = cpu_problem(heads)
+        kind = "port"
+        sample = f"config 2 with {heads} of {H_TOTAL} heads per step (decode + append + SDPA)"
+        step = lambda: cpu_step(p)  # noqa: E731
     for _ in range(args.warmup):
-        cpu_step(p)
+        step()
     t = time.perf_counter()
     for _ in range(args.steps):
-        cpu_step(p)
+        step()
     dt = (time.perf_counter() - t) / args.steps
     fl = attention_flops(p["Lh"], p["Li"], TXT, heads, D, True, T)
     value = fl / dt / 1e12
-    sample = f"config 2 with {heads} of {H_TOTAL} heads per step (decode + append + SDPA)"
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2),
@@ -1013,7 +1060,7 @@ def run_reference(args):
         "config": {"workload": "config 2: 1x B200 single block", "heads_sampled": heads,
                    "history_tokens": p["Lh"], "chunk_image_tokens": p["Li"], "tokens_per_frame": T},
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": sample},
+                         "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

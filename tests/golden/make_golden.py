@@ -54,19 +54,12 @@ REPO = HERE.parent.parent
 
 
 def _install_stub() -> None:
-    ref = os.environ.get("HY_NOMAS_REF")
-    if not ref or not (Path(ref) / "hymm").is_dir():
-        raise SystemExit("set HY_NOMAS_REF to the Hy-Nomas reference checkout (the directory holding hymm/)")
-    stub = Path(tempfile.mkdtemp(prefix="hyb_stub_"))
-    (stub / "diffusers" / "models").mkdir(parents=True)
-    (stub / "diffusers" / "__init__.py").write_text("")
-    (stub / "diffusers" / "models" / "__init__.py").write_text(
-        "import torch.nn as nn\nclass ModelMixin(nn.Module):\n    pass\n")
-    (stub / "diffusers" / "configuration_utils.py").write_text(
-        "class ConfigMixin:\n    pass\ndef register_to_config(fn):\n    return fn\n")
-    sys.path.insert(0, str(stub))
-    sys.path.insert(0, str(Path(ref)))
     sys.path.insert(0, str(REPO))
+    from oracle.reference import install_stub
+    try:
+        install_stub()
+    except RuntimeError as e:
+        raise SystemExit(str(e))
 
 
 def bf(t: torch.Tensor) -> np.ndarray:

@@ -1,10 +1,10 @@
 """The installer on the reference's own DiT module (CPU, where a reference checkout is named by
 HY_NOMAS_REF; skipped elsewhere).  ``hymm.models.dit.nomas_cpt`` imports with a 10-line
-``diffusers`` stub (tests/golden/make_golden.py).  An unmodified
+``diffusers`` stub (``oracle/reference.py``).  An unmodified
 ``MMDoubleStreamBlock.forward_with_cache`` call (nomas_cpt.py:1292-1416) must reach the patched
 module attribute: CPU tensors fall back to the native function with an identical result, and
 an eligible call is handed to the B200 drop-in with the block's own arguments."""
-import importlib.util
+import importlib
 import os
 from pathlib import Path
 
@@ -14,7 +14,6 @@ import torch
 from hy_nomas_b200 import attention as hatt
 from hy_nomas_b200 import install as hinst
 
-GOLDEN = Path(__file__).resolve().parent / "golden"
 
 pytestmark = pytest.mark.skipif(
     not (os.environ.get("HY_NOMAS_REF") and (Path(os.environ["HY_NOMAS_REF"]) / "hymm").is_dir()),
@@ -23,10 +22,8 @@ pytestmark = pytest.mark.skipif(
 
 @pytest.fixture(scope="module")
 def native():
-    spec = importlib.util.spec_from_file_location("make_golden", GOLDEN / "make_golden.py")
-    mod = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(mod)
-    mod._install_stub()
+    from oracle.reference import install_stub
+    install_stub()
     return importlib.import_module("hymm.models.dit.nomas_cpt")
 
 
