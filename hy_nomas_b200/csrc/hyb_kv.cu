@@ -14,11 +14,11 @@
 namespace hyb {
 namespace {
 
-constexpr int kRowLanes = 16;  // lanes per row: 16 x 8 bf16 = 128 values
+constexpr int kRowLanes = 8;  // lanes per row: 8 x 16 bf16 = 128 values
 
 struct AppendParams {
   int fmt;
-  int B, L, L2, H;  // rows [0, L) from src, [L, L + L2) from src2
+  int L, L2, H;  // rows [0, L) from src, [L, L + L2) from src2; the batch index is blockIdx.y
   long long start;
   const __nv_bfloat16* src[2];
   long long s_b[2], s_t[2], s_h[2];
@@ -29,9 +29,10 @@ struct AppendParams {
   float* scale[2];
   long long c_b, c_t, c_h;
   int* status;
+  int step_t, step_h;  // the grid stride (groups) split as step_t * H + step_h
 };
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
+__device__ __forceinline__ void unpack8(const uint4& u, float* x) {
   const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -41,104 +42,120 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
   }
 }
 
-// x / s rounded to nearest, from r = RN(1/s): q0 = RN(x r), then two residual steps
-// q' = RN(q + r (x - s q)) with the residual formed exactly by the fma.  The first step
-// leaves q1 within one ulp of x / s; correcting a quotient that close with a correctly
-// rounded reciprocal gives RN(x / s) (P. Markstein, "Computation of elementary functions on
-// the IBM RISC System/6000 processor", IBM J. Res. Develop. 34(1), 1990; restated in Muller
-// et al., Handbook of Floating-Point Arithmetic, on FMA-based division).  The argument needs
-// x, s and the residuals in the normal range: callers use it for |x|, s >= 2^-90 only.
-__device__ __forceinline__ float div_rn_by(float x, float s, float r) {
-  const float q0 = __fmul_rn(x, r);
-  const float q1 = __fmaf_rn(__fmaf_rn(-s, q0, x), r, q0);
-  return __fmaf_rn(__fmaf_rn(-s, q1, x), r, q1);
+// max(|a|, |b|, |c|), NaN if any operand is NaN (so a row's non-finite values survive the
+// reduction and are caught from the peak alone).
+__device__ __forceinline__ float absmax3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(fabsf(a)), "f"(fabsf(b)), "f"(fabsf(c)));
+  return r;
+}
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 
-__device__ __forceinline__ float quotient(float x, float s, float r, bool fast_row) {
-  if (fast_row && fabsf(x) >= 0x1p-90f) return div_rn_by(x, s, r);
-  return __fdiv_rn(x, s);
+// RN(p / R) for R = 127 or 448 from RN(1 / R) by two residual corrections (the division
+// scheme named at div_rn_by2 below, with a constant divisor).  Checked against IEEE division
+// for every positive finite bf16 p, subnormal quotients included, which covers every row peak.
+template <int FMT>
+__device__ __forceinline__ float row_scale(float peak) {
+  constexpr float R = FMT == HYB_FMT_INT8 ? 127.0f : 448.0f;
+  constexpr float rR = FMT == HYB_FMT_INT8 ? 0x1.020408p-7f : 0x1.24924ap-9f;  // RN(1 / R)
+  const float q0 = __fmul_rn(peak, rR);
+  const float q1 = __fmaf_rn(__fmaf_rn(-R, q0, peak), rR, q0);
+  return __fmaf_rn(__fmaf_rn(-R, q1, peak), rR, q1);
 }
 
-// div_rn_by for a pair, in packed fp32x2 arithmetic (5 instructions for two quotients).  Valid
-// for every x of a row whose scale s is at least 2^-90: the residuals x - s q stay normal unless
-// |x| < 2^-103, and such an x has |x / s| < 2^-13, whose e4m3 and INT8 codes are 0 whatever
-// the last bit of the quotient.
+// x / s rounded to nearest for a pair, from r = RN(1/s): q0 = RN(x r), then two residual steps
+// q' = RN(q + r (x - s q)) with the residual formed exactly by the fma.  The first step leaves
+// q1 within one ulp of x / s; correcting a quotient that close with a correctly rounded
+// reciprocal gives RN(x / s) (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Develop. 34(1), 1990; restated in Muller et al.,
+// Handbook of Floating-Point Arithmetic, on FMA-based division).  Valid for every x of a row
+// whose scale s is at least 2^-90: the residuals stay normal unless |x| < 2^-103, and such an x
+// has |x / s| < 2^-13, whose e4m3 and INT8 codes are 0 whatever the last bit of the quotient.
+// The sign of a zero quotient is not kept (x = -0 gives +0): the E4M3 caller restores it on the
+// codes, and INT8 has no negative zero.
 __device__ __forceinline__ float2 div_rn_by2(float2 x, float s, float r) {
   const float2 rr = make_float2(r, r);
   const float2 ns = make_float2(-s, -s);
   const float2 q0 = fmul2(x, rr);
   const float2 q1 = ffma2(ffma2(ns, q0, x), rr, q0);
-  const float2 q2 = ffma2(ffma2(ns, q1, x), rr, q1);
-  // A zero quotient takes the sign of x (-0 for a tiny negative x, as x / s gives): the last
-  // step may add +0 to -0.  A nonzero quotient already has x's sign.
-  return make_float2(__int_as_float(__float_as_int(q2.x) | (__float_as_int(x.x) & 0x80000000)),
-                     __int_as_float(__float_as_int(q2.y) | (__float_as_int(x.y) & 0x80000000)));
+  return ffma2(ffma2(ns, q1, x), rr, q1);
 }
 
-// Quantise one 128-value row held by a 16-lane group (8 values per lane): absmax over the
-// group, the row scale, and the 8 codes of this lane.  Returns the 8 code bytes.
-__device__ __forceinline__ uint2 quantise_row8(const float (&x)[8], int fmt, unsigned half_mask, float& s_out,
-                                               bool& nonfinite) {
-  float peak = 0.f;
+// Codes of 4 values (one 32-bit word, value i in byte i) from their quotients.
+template <int FMT>
+__device__ __forceinline__ uint32_t codes4(float2 ya, float2 yb, uint32_t wa, uint32_t wb) {
+  if constexpr (FMT == HYB_FMT_INT8) {
+    // y >= 0 ? floor(RN(y + 0.5)) : ceil(RN(y - 0.5)) is trunc(RN(y + copysign(0.5, y))); with
+    // |y| <= 127 (1 + 2^-23) it lies in [-127, 127], so the reference's clamp never binds.
+    const float y[4] = {ya.x, ya.y, yb.x, yb.y};
+    uint32_t c[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    peak = fmaxf(peak, fabsf(x[i]));
-    nonfinite |= !isfinite(x[i]);
+    for (int i = 0; i < 4; ++i)
+      c[i] = static_cast<uint32_t>(__float2int_rz(__fadd_rn(y[i], copysignf(0.5f, y[i]))));
+    return __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
+  } else {
+    // |y| <= 448 up to rounding; the saturating conversion maps anything beyond to +-448
+    // exactly as the reference's clamp does.  The sign bits of the four bf16 inputs (their
+    // high bytes) are ORed in: a no-op except for x = -0, whose code is 0x80 (-0 / s = -0).
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(ya, __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(yb, __NV_SATFINITE, __NV_E4M3);
+    return (lo | (hi << 16)) | (__byte_perm(wa, wb, 0x7531) & 0x80808080u);
   }
+}
+
+// Quantise one 128-value row held by an 8-lane group (16 values per lane: raw[0] holds values
+// [8 l, 8 l + 8), raw[1] values [64 + 8 l, 72 + 8 l) of lane l).  Returns the row scale and
+// this lane's 16 code bytes in the same two halves.
+template <int FMT>
+__device__ __forceinline__ float quantise_row16(const uint4 (&raw)[2], unsigned gmask, uint2 (&codes)[2],
+                                                bool& nonfinite) {
+  float x[16];
+  unpack8(raw[0], x);
+  unpack8(raw[1], x + 8);
+  float peak = absmax3_nan(x[0], x[1], x[2]);
+  peak = max_nan(peak, absmax3_nan(x[3], x[4], x[5]));
+  peak = max_nan(peak, absmax3_nan(x[6], x[7], x[8]));
+  peak = max_nan(peak, absmax3_nan(x[9], x[10], x[11]));
+  peak = max_nan(peak, absmax3_nan(x[12], x[13], x[14]));
+  peak = max_nan(peak, fabsf(x[15]));
 #pragma unroll
   for (int off = kRowLanes / 2; off >= 1; off >>= 1)
-    peak = fmaxf(peak, __shfl_xor_sync(half_mask, peak, off, kRowLanes));
-  const float denom = (fmt == HYB_FMT_INT8) ? 127.0f : 448.0f;
-  const float s = peak > 0.f ? __fdiv_rn(peak, denom) : 1.0f;
-  s_out = s;
-  const bool fast_row = s >= 0x1p-90f;
+    peak = max_nan(peak, __shfl_xor_sync(gmask, peak, off, kRowLanes));
+  nonfinite |= !(peak <= 3.40282347e38f);  // a NaN or an infinity anywhere in the row
+  const float s = peak > 0.f ? row_scale<FMT>(peak) : 1.0f;
   const float r = __frcp_rn(s);
-  uint32_t w[2];
-  if (fmt == HYB_FMT_INT8) {
+  const bool fast_row = s >= 0x1p-90f;
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(raw);
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t acc = 0;
-      float2 yp[2];
+  for (int half = 0; half < 2; ++half) {
+    uint32_t c[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int i = half * 8 + q * 4;
+      float2 ya = make_float2(x[i], x[i + 1]);
+      float2 yb = make_float2(x[i + 2], x[i + 3]);
       if (fast_row) {
-        yp[0] = div_rn_by2(make_float2(x[half * 4], x[half * 4 + 1]), s, r);
-        yp[1] = div_rn_by2(make_float2(x[half * 4 + 2], x[half * 4 + 3]), s, r);
+        ya = div_rn_by2(ya, s, r);
+        yb = div_rn_by2(yb, s, r);
       } else {
-        yp[0] = make_float2(__fdiv_rn(x[half * 4], s), __fdiv_rn(x[half * 4 + 1], s));
-        yp[1] = make_float2(__fdiv_rn(x[half * 4 + 2], s), __fdiv_rn(x[half * 4 + 3], s));
+        ya = make_float2(__fdiv_rn(ya.x, s), __fdiv_rn(ya.y, s));
+        yb = make_float2(__fdiv_rn(yb.x, s), __fdiv_rn(yb.y, s));
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float y = (i & 1) ? yp[i >> 1].y : yp[i >> 1].x;
-        float r = (y >= 0.f) ? floorf(__fadd_rn(y, 0.5f)) : ceilf(__fsub_rn(y, 0.5f));
-        r = fminf(fmaxf(r, -127.f), 127.f);
-        const int8_t c = static_cast<int8_t>(static_cast<int>(r));
-        acc |= static_cast<uint32_t>(static_cast<uint8_t>(c)) << (8 * i);
-      }
-      w[half] = acc;
+      c[q] = codes4<FMT>(ya, yb, w[i / 2], w[i / 2 + 1]);
     }
-  } else {
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t acc = 0;
-#pragma unroll
-      for (int i = 0; i < 4; i += 2) {
-        // |x / s| <= 448 up to rounding, and the saturating conversion maps anything beyond to
-        // +-448 exactly as a clamp would (a NaN row is flagged non-finite either way)
-        const float2 xp = make_float2(x[half * 4 + i], x[half * 4 + i + 1]);
-        const float2 y = fast_row ? div_rn_by2(xp, s, r) : make_float2(__fdiv_rn(xp.x, s), __fdiv_rn(xp.y, s));
-        const __nv_fp8x2_storage_t c2 = __nv_cvt_float2_to_fp8x2(y, __NV_SATFINITE, __NV_E4M3);
-        acc |= static_cast<uint32_t>(c2) << (8 * i);
-      }
-      w[half] = acc;
-    }
+    codes[half] = make_uint2(c[0], c[1]);
   }
-  return make_uint2(w[0], w[1]);
+  return s;
 }
 
-// One 16-lane group per (batch, token, head) row, K and V of the row together, two rows per
-// iteration: four 16-byte loads in flight per lane before any arithmetic.  Row indices are
-// 32-bit (the launcher checks B * (L + L2) * H * 16 < 2^31).
-constexpr int kAppendRowsPerIter = 2;
+// One 8-lane group per (token, head) row of one batch entry (blockIdx.y), the K and V rows of
+// a token together, ROWS rows per iteration (4 ROWS 16-byte loads in flight per lane before any
+// arithmetic).  Row r = t * H + h; the group's (t, h) advance by the grid stride without a
+// division.  Row indices are 32-bit (the launcher checks (L + L2) * H * 8 < 2^31).
 
 __device__ __forceinline__ const __nv_bfloat16* append_src(const AppendParams& p, int which, int b, int t, int h,
                                                            int sub) {
@@ -146,45 +163,61 @@ __device__ __forceinline__ const __nv_bfloat16* append_src(const AppendParams& p
                  : p.src2[which] + b * p.s2_b[which] + (t - p.L) * p.s2_t[which] + h * p.s2_h[which] + sub * 8;
 }
 
-__global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams p) {
+__device__ __forceinline__ void advance_row(int& t, int& h, int dt, int dh, int H) {
+  t += dt;
+  h += dh;
+  if (h >= H) {
+    h -= H;
+    ++t;
+  }
+}
+
+// ROWS rows per iteration: the loads of all of them (4 ROWS 16-byte loads per lane) are issued
+// before any arithmetic.  ROWS = 1 (the default) keeps 64 registers and four blocks of 256
+// threads per SM; ROWS = 2 holds twice the loads per lane at two blocks per SM (measured
+// slower on the config-2 chunk: 32.7 against 28.2 us, as was a software prefetch of the next row).
+template <int FMT, int ROWS>
+__global__ void __launch_bounds__(256, ROWS == 1 ? 4 : 2) kv_append_kernel(const AppendParams p) {
   const int Lt = p.L + p.L2;
-  const int rows = p.B * Lt * p.H;
+  const int b = blockIdx.y;
   const int sub = threadIdx.x & (kRowLanes - 1);
-  // The two 16-lane halves of a warp own different rows and may leave the loop on different
-  // iterations, so each half shuffles under its own lane mask.
-  const unsigned half_mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
+  // The four 8-lane groups of a warp own different rows and may leave the loop on different
+  // iterations, so each group shuffles under its own lane mask.
+  const unsigned gmask = 0xFFu << (threadIdx.x & 24);
   const int group = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) / kRowLanes);
-  const int groups = static_cast<int>(gridDim.x * blockDim.x / kRowLanes);
+  int t = group / p.H;
+  int h = group - t * p.H;
   bool nonfinite = false;
-  for (int base = group; base < rows; base += groups * kAppendRowsPerIter) {
-    int bb[kAppendRowsPerIter], tt[kAppendRowsPerIter], hh[kAppendRowsPerIter];
-    bool live[kAppendRowsPerIter];
-    uint4 raw[kAppendRowsPerIter][2];
+  while (t < Lt) {
+    int tt[ROWS], hh[ROWS];
+    bool live[ROWS];
+    uint4 raw[ROWS][2][2];
 #pragma unroll
-    for (int u = 0; u < kAppendRowsPerIter; ++u) {
-      const int row = base + u * groups;
-      live[u] = row < rows;
-      const int rr = live[u] ? row : base;
-      hh[u] = rr % p.H;
-      const int bt = rr / p.H;
-      tt[u] = bt % Lt;
-      bb[u] = bt / Lt;
-#pragma unroll
-      for (int which = 0; which < 2; ++which)
-        raw[u][which] = __ldg(reinterpret_cast<const uint4*>(append_src(p, which, bb[u], tt[u], hh[u], sub)));
-    }
-#pragma unroll
-    for (int u = 0; u < kAppendRowsPerIter; ++u) {
-      if (!live[u]) continue;   // uniform over the 16-lane group that owns the row
-      const long long dst_off = bb[u] * p.d_b + (tt[u] + p.start) * p.d_t + hh[u] * p.d_h + sub * 8;
-      const long long sc_off = bb[u] * p.c_b + (tt[u] + p.start) * p.c_t + hh[u] * p.c_h;
+    for (int u = 0; u < ROWS; ++u) {
+      tt[u] = t;
+      hh[u] = h;
+      live[u] = t < Lt;
+      const int tl = live[u] ? t : 0;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
-        float x[8];
-        unpack8(raw[u][which], x);
-        float s;
-        const uint2 codes = quantise_row8(x, p.fmt, half_mask, s, nonfinite);
-        *reinterpret_cast<uint2*>(static_cast<uint8_t*>(p.dst[which]) + dst_off) = codes;
+        const uint4* src = reinterpret_cast<const uint4*>(append_src(p, which, b, tl, h, 0));
+        raw[u][which][0] = __ldg(src + sub);
+        raw[u][which][1] = __ldg(src + 8 + sub);
+      }
+      advance_row(t, h, p.step_t, p.step_h, p.H);
+    }
+#pragma unroll
+    for (int u = 0; u < ROWS; ++u) {
+      if (!live[u]) continue;  // uniform over the 8-lane group that owns the row
+      const long long dst_off = b * p.d_b + (tt[u] + p.start) * p.d_t + hh[u] * p.d_h + sub * 8;
+      const long long sc_off = b * p.c_b + (tt[u] + p.start) * p.c_t + hh[u] * p.c_h;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        uint2 codes[2];
+        const float s = quantise_row16<FMT>(raw[u][which], gmask, codes, nonfinite);
+        uint8_t* dst = static_cast<uint8_t*>(p.dst[which]) + dst_off;
+        *reinterpret_cast<uint2*>(dst) = codes[0];
+        *reinterpret_cast<uint2*>(dst + 64) = codes[1];
         if (sub == 0) p.scale[which][sc_off] = s;
       }
     }
@@ -314,7 +347,6 @@ extern "C" int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, 
     return fail(HYB_ERR_INVALID_ARG, "kv append: code rows must be 8-byte aligned");
   AppendParams p;
   p.fmt = fmt;
-  p.B = B;
   p.L = L;
   p.L2 = L2;
   p.H = H;
@@ -341,13 +373,34 @@ extern "C" int hyb_kv_append_pair(int32_t fmt, int32_t B, int32_t L, int32_t H, 
   p.c_t = s_st;
   p.c_h = s_sh;
   p.status = dev_status;
-  const long long rows = static_cast<long long>(B) * (L + L2) * H;
-  if (rows * kRowLanes >= (1LL << 31))
-    return fail(HYB_ERR_UNSUPPORTED, "kv append: %lld rows in one call (split the call)", rows);
+  const long long rows = static_cast<long long>(L + L2) * H;  // per batch entry
+  if (rows * kRowLanes >= (1LL << 31) || B > 65535)
+    return fail(HYB_ERR_UNSUPPORTED, "kv append: %lld rows x %d batch entries in one call (split the call)", rows,
+                B);
   // about two iterations per group: enough loads in flight without a long grid-stride tail
-  long long blocks = (rows * kRowLanes + 256LL * 2 * kAppendRowsPerIter - 1) / (256LL * 2 * kAppendRowsPerIter);
+  static const int rows_per_iter = [] {
+    const char* e = getenv("HYB_APPEND_ROWS");
+    return e != nullptr && atoi(e) == 2 ? 2 : 1;
+  }();
+  const long long per_block = 256 / kRowLanes;
+  long long blocks = (rows + per_block * 2 * rows_per_iter - 1) / (per_block * 2 * rows_per_iter);
   blocks = blocks < 1 ? 1 : (blocks > 148LL * 64 ? 148LL * 64 : blocks);
-  kv_append_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  const long long stride = blocks * per_block;
+  p.step_t = static_cast<int>(stride / H);
+  p.step_h = static_cast<int>(stride % H);
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(B));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (fmt == HYB_FMT_INT8) {
+    if (rows_per_iter == 1)
+      kv_append_kernel<HYB_FMT_INT8, 1><<<grid, 256, 0, st>>>(p);
+    else
+      kv_append_kernel<HYB_FMT_INT8, 2><<<grid, 256, 0, st>>>(p);
+  } else {
+    if (rows_per_iter == 1)
+      kv_append_kernel<HYB_FMT_E4M3, 1><<<grid, 256, 0, st>>>(p);
+    else
+      kv_append_kernel<HYB_FMT_E4M3, 2><<<grid, 256, 0, st>>>(p);
+  }
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
