@@ -63,6 +63,9 @@ def parse():
                     help="config 2: skip the config-3 ring measurement reported in the same line")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager calls instead of replaying one captured CUDA graph of the call")
+    ap.add_argument("--sp-scheme", default="ulysses", choices=["ulysses", "kv"],
+                    help="rollout at N > 1: Ulysses over head-sharded windows, or KV-stationary over "
+                         "sequence-sharded windows (Q all-gather, partial rows scattered to their owners)")
     ap.add_argument("--workload", default="config2", choices=["config2", "config4", "ring", "rollout"],
                     help="config2: 4-frame chunk vs 16-frame FP8 cache (Ulysses for N > 1); "
                          "config4: the same chunk vs a 48-frame cache; "
@@ -592,7 +595,8 @@ def run_b200(args):
                    "heads": H_TOTAL, "head_dim": D, "history_tokens": Lh, "chunk_image_tokens": Li,
                    "text_tokens": TXT, "tokens_per_frame": T, "mask": "frame-level block-causal (G=1)",
                    "kv_cache": "fp8_e4m3 per-token-per-head scale", "append": "quantise-on-write of the chunk each step",
-                   "parallelism": f"ulysses_sp{world}" if world > 1 else "single",
+                   "parallelism": (f"ulysses_sp{world}" if scheme == "ulysses" else f"kv_stationary_sp{world}")
+                   if world > 1 else "single",
                    "exchange": ("peer memory (CUDA IPC push kernels + device barrier)"
                                 if world > 1 and os.environ.get("HYB_PEER_EXCHANGE", "1") != "0"
                                 else ("NCCL all_to_all_single" if world > 1 else None)),
@@ -815,8 +819,9 @@ SINK, KEEP, PREFILL = 1, 32, 64
 def run_rollout(args):
     """Config 5: a 64-frame rollout history kept as first-frame sink + the last 32 frames;
     every step attends one new 1560-token frame (24 heads) to the 33 history frames and
-    itself, then appends the frame into the window ring (quantise-on-write).  N > 1: Ulysses
-    SP, each rank holds its heads' window and 1560/N of the frame's tokens."""
+    itself, then appends the frame into the window ring (quantise-on-write).  N > 1, Ulysses:
+    each rank holds its heads' window and 1560/N of the frame's tokens.  N > 1, KV-stationary
+    (--sp-scheme kv): each rank holds its 1560/N-token slice of every frame for all heads."""
     from hy_nomas_b200 import _lib
     from hy_nomas_b200 import attention as hatt
     from hy_nomas_b200 import parallel_states as ps
@@ -831,13 +836,15 @@ def run_rollout(args):
     if world > 1:
         ps.initialize_sequence_parallel_group()
     os.environ["HYB_ASSUME_FINITE_KV"] = "1"
-    Hl = H_TOTAL // world
+    scheme = args.sp_scheme if world > 1 else "single"
+    Hl = H_TOTAL // world if scheme == "ulysses" else H_TOTAL
     Ls = T // world
+    Tw = Ls if scheme == "kv" else T      # tokens of each frame in this rank's window
     gen = make_generator(1238 + rank, device=device)
-    win = SinkWindowKVCache(1, Hl, T, SINK, KEEP, device=device)
+    win = SinkWindowKVCache(1, Hl, Tw, SINK, KEEP, device=device)
     with torch.no_grad():
         for _ in range(PREFILL):   # rollout history (untimed): 64 frames through the ring
-            win.append(seeded_kv((1, T, Hl, D), gen, device=device), seeded_kv((1, T, Hl, D), gen, device=device),
+            win.append(seeded_kv((1, Tw, Hl, D), gen, device=device), seeded_kv((1, Tw, Hl, D), gen, device=device),
                        assume_finite=True)
     img = [seeded_kv((1, Ls, H_TOTAL, D), gen, device=device) for _ in range(3)]
     txt = [img[0][:, :0] for _ in range(3)]
@@ -848,9 +855,15 @@ def run_rollout(args):
         from hy_nomas_b200 import communications as comm
         sp_metadata = comm.prepare_sp_communication(Ls, H_TOTAL, device, ps.nccl_info.sp_group)
     stream = torch.cuda.current_stream(device)
+    kvs = None
+    if scheme == "kv":
+        from hy_nomas_b200.kv_stationary import KVStationaryAttention
+        kvs = KVStationaryAttention(None, 1, Ls, H_TOTAL, 0, (SINK + KEEP) * Ls, device)
 
     def step(q_img, k_img, v_img, q_txt, k_txt, v_txt):
         with torch.no_grad():
+            if kvs is not None:
+                return kvs(q_img, k_img, v_img, q_txt, k_txt, v_txt, win)
             return hatt.causal_attention_with_cache_mp(
                 (q_img, q_txt), (k_img, k_txt), (v_img, v_txt), win.view(), cache_valid_len=win.valid_len,
                 update_cache=True, cache_txt=False, tokens_per_frame=T, seg_ar_attention_backend="b200",
@@ -886,6 +899,8 @@ def run_rollout(args):
     if world > 1:
         from hy_nomas_b200 import communications as comm2
         torch.cuda.synchronize(device)
+        if kvs is not None:
+            kvs.close()
         comm2.release_peer_exchanges()
         ps.destroy_sequence_parallel_group()
         dist.destroy_process_group()
@@ -903,7 +918,7 @@ def run_rollout(args):
                    "parallelism": f"ulysses_sp{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (155 MB FP8 window + 10 MB bf16 frame per step)",
                    "tflop_per_step": round(flops_total / 1e12, 4)},
-        "gpu_launches": args.steps * (6 + (2 if world > 1 else 0)),
+        "gpu_launches": args.steps * (8 if scheme == "kv" else 6 + (2 if world > 1 else 0)),
         "e2e": {"value": round(flops_total / (ems * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "ms_per_step": round(ems, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": None,

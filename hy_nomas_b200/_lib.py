@@ -16,7 +16,7 @@ import torch
 PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libhyb200.so"
 
-HYB_ABI_VERSION = 3
+HYB_ABI_VERSION = 4
 
 HYB_OK = 0
 HYB_ERR_INVALID_ARG = -1
@@ -49,6 +49,13 @@ class Tensor4(ctypes.Structure):
     ]
 
 
+class PartScatter(ctypes.Structure):
+    """hyb_part_scatter: partial rows written to their owner ranks (KV-stationary schedule)."""
+
+    _fields_ = [("o", c_ptr), ("lse", c_ptr), ("ranks", c_i32), ("rows", c_i32), ("index0", c_i32),
+                ("count", c_i32), ("slices", c_i32), ("pad_", c_i32)]
+
+
 class CachedAttnArgs(ctypes.Structure):
     """``hyb_cached_attn_args``."""
 
@@ -66,7 +73,7 @@ class CachedAttnArgs(ctypes.Structure):
         ("oi_seg", c_i64), ("oi_sseg", c_i64),
         ("out_txt", c_ptr), ("ot_sb", c_i64), ("ot_st", c_i64), ("ot_sh", c_i64),
         ("lse", c_ptr), ("workspace", c_ptr), ("workspace_bytes", c_i64),
-        ("dev_status", c_ptr), ("pad_", c_i32),
+        ("dev_status", c_ptr), ("img_k_len", c_i32), ("scatter", c_ptr),
     ]
 
 
@@ -88,6 +95,7 @@ class AttnArgs(ctypes.Structure):
         ("lse", c_ptr), ("dev_status", c_ptr),
         ("kv_splits", c_i32), ("v_f16", c_i32), ("part_o", c_ptr), ("part_lse", c_ptr),
         ("acc_o", c_ptr), ("acc_lse", c_ptr), ("acc_mode", c_i32), ("pad2_", c_i32),
+        ("scatter", c_ptr),
     ]
 
 
@@ -145,6 +153,9 @@ SIGNATURES = {
     "hyb_cached_attention_noalloc": (c_i32, [ctypes.POINTER(CachedAttnArgs), c_ptr]),
     "hyb_attn_fwd": (c_i32, [ctypes.POINTER(AttnArgs), c_ptr]),
     "hyb_lse_merge": (c_i32, [c_i32, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr]),
+    "hyb_merge_partials": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr,
+                                   c_ptr, c_i64, c_i64, c_i64, c_ptr, c_i64, c_i64, c_i64,
+                                   c_ptr, c_i64, c_ptr, c_ptr]),
     "hyb_ulysses_pack_qkv": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                                      ctypes.POINTER(Tensor4), ctypes.POINTER(Tensor4),
                                      ctypes.POINTER(Tensor4), c_ptr, c_ptr]),

@@ -26,6 +26,7 @@ Intra-segment action masks (``intra_seg_txt_offsets`` / ``intra_seg_vid_windows`
 """
 from __future__ import annotations
 
+import ctypes
 import os
 from typing import Optional
 
@@ -95,7 +96,7 @@ def cached_attention_local(
     img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, cache_valid_len, *,
     history_mask=None, text_mask=None, attend_txt=True, group_tokens=0,
     softmax_scale=None, out_img=None, out_img_strides=None, out_txt=None, lse=None,
-    hist_rows=None, workspace=None, q_pos0=0, k_pos0=0, img_kv_fmt=None,
+    hist_rows=None, workspace=None, q_pos0=0, k_pos0=0, img_kv_fmt=None, scatter=None,
 ):
     """Single-rank attention of the current chunk over [history | image | text].
 
@@ -110,10 +111,18 @@ def cached_attention_local(
     ``q_pos0`` / ``k_pos0`` shift the block-causal rule to global positions (ring steps);
     with ``img_kv_fmt`` (HYB_FMT_E4M3 / HYB_FMT_INT8) ``img_k`` / ``img_v`` are
     ``(codes, scale)`` pairs of a quantised block.
+
+    The image keys may be fewer than the image queries (``img_k`` [B, Lik, H, D]) only together
+    with ``scatter`` (an ``_lib.PartScatter``): a rank of a KV-stationary schedule attends every
+    query of the chunk to the keys it holds, and the partial rows go to their owner ranks'
+    buffers (no outputs here; returns ``(None, None)``).
     """
     lib = _lib.load()
     B, Li, H, D = img_q.shape
     Lt = txt_q.shape[1]
+    Lik = (img_k[0] if img_kv_fmt is not None else img_k).shape[1]
+    if Lik != Li and scatter is None:
+        raise ValueError(f"image keys ({Lik}) and queries ({Li}) differ without a partial scatter")
     dev = img_q.device
     if kv_cache is None:   # no history: a zero-length bf16 placeholder
         kv_cache = {"k": img_q[:, :0], "v": img_q[:, :0]}
@@ -133,11 +142,12 @@ def cached_attention_local(
     _lib.require_same_device(dev, "cached attention tensors", img_k, img_v, txt_q, txt_k, txt_v, kv_cache["k"],
                              kv_cache["v"], history_mask, text_mask, hist_rows, out_img, out_txt, lse,
                              *(kv_cache[n] for n in ("k_scale", "v_scale") if torch.is_tensor(kv_cache.get(n))))
-    if out_img is None:
+    if scatter is None and out_img is None:
         out_img = _new_out(B, Li, H, D, dev)
-    if out_txt is None:
+    if scatter is None and out_txt is None:
         out_txt = _new_out(B, Lt, H, D, dev)
-    oi = tuple(out_img_strides) if out_img_strides is not None else tuple(out_img.stride()[:3])
+    oi = tuple(out_img_strides) if out_img_strides is not None else \
+        (tuple(out_img.stride()[:3]) if out_img is not None else (0, 0, 0))
     if len(oi) == 3:
         oi = oi + (0, 0)
     ws_bytes = lib.hyb_cached_attention_workspace_bytes(B, H, D, cache_valid_len, Li, Lt, int(attend_txt))
@@ -177,12 +187,14 @@ def cached_attention_local(
     args.q_pos0, args.k_pos0 = int(q_pos0), int(k_pos0)
     args.img_q = _lib.bf16_view(img_q) if Li else empty
     if img_kv_fmt is None:
-        args.img_k = _lib.bf16_view(img_k) if Li else empty
-        args.img_v = _lib.bf16_view(img_v) if Li else empty
+        args.img_k = _lib.bf16_view(img_k) if Lik else empty
+        args.img_v = _lib.bf16_view(img_v) if Lik else empty
     else:
         # quantised current keys/values: (codes, scale) pairs in the given format
-        args.img_k = _lib.coded_view(img_k[0], img_k[1], img_kv_fmt) if Li else empty
-        args.img_v = _lib.coded_view(img_v[0], img_v[1], img_kv_fmt) if Li else empty
+        args.img_k = _lib.coded_view(img_k[0], img_k[1], img_kv_fmt) if Lik else empty
+        args.img_v = _lib.coded_view(img_v[0], img_v[1], img_kv_fmt) if Lik else empty
+    args.img_k_len = Lik if Lik != Li else 0
+    args.scatter = ctypes.cast(ctypes.pointer(scatter), ctypes.c_void_p) if scatter is not None else None
     args.txt_q = _lib.bf16_view(txt_q) if Lt else empty
     args.txt_k = _lib.bf16_view(txt_k) if Lt else empty
     args.txt_v = _lib.bf16_view(txt_v) if Lt else empty
@@ -194,17 +206,17 @@ def cached_attention_local(
     args.cache_mask_sb = history_mask.stride(0) if history_mask is not None else 0
     args.text_mask = _lib.ptr(text_mask)
     args.text_mask_sb = text_mask.stride(0) if text_mask is not None else 0
-    args.out_img = out_img.data_ptr()
+    args.out_img = _lib.ptr(out_img)
     args.oi_sb, args.oi_st, args.oi_sh, args.oi_seg, args.oi_sseg = oi
-    args.out_txt = out_txt.data_ptr()
-    args.ot_sb, args.ot_st, args.ot_sh = out_txt.stride()[:3]
+    args.out_txt = _lib.ptr(out_txt)
+    args.ot_sb, args.ot_st, args.ot_sh = out_txt.stride()[:3] if out_txt is not None else (0, 0, 0)
     args.lse = _lib.ptr(lse)
     args.workspace = workspace.data_ptr()
     args.workspace_bytes = workspace.numel()
     args.dev_status = _lib.device_status(dev).data_ptr()
     with torch.cuda.device(dev):
         _lib.check(lib.hyb_cached_attention(args, _lib.stream_ptr(dev)), "cached attention")
-    if ws_obj is not None:
+    if ws_obj is not None and scatter is None:
         with torch.cuda.device(dev):
             lay = workspace_layout(B, H, cache_valid_len, Li, Lt, attend_txt, D)
         base = workspace.data_ptr()

@@ -74,6 +74,12 @@ struct AttnKParams {
   float* acc_o;
   float* acc_lse;
   int acc_mode;
+  // Partial rows scattered to their owner ranks (hyb_part_scatter), active when sc_o is set:
+  // image row q to rank q / sc_rows, row q % sc_rows; text row t to every rank, row sc_rows + t;
+  // partial index sc_index0 + this CTA's key slice.
+  float* const* sc_o;
+  float* const* sc_lse;
+  int sc_ranks, sc_rows, sc_index0;
 };
 
 __host__ __device__ __forceinline__ int imin(int a, int b) { return a < b ? a : b; }
@@ -223,6 +229,25 @@ __device__ __forceinline__ void warp_store_bf16_rows(uint8_t* ebuf, const uint32
     const uint4 x = *reinterpret_cast<const uint4*>(ebuf + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
     const unsigned long long d = __shfl_sync(0xffffffffu, mine, r);
     if (d != 0ull) reinterpret_cast<uint4*>(d)[g] = x;
+  }
+  __syncwarp();
+}
+
+// fp32 rows of 32 columns, row r to the row pointer held by lane r (null: skip).
+__device__ __forceinline__ void warp_store_f32_rows_to(uint8_t* ebuf, const float (&v)[32], float* dst, int lane) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+    *reinterpret_cast<float4*>(ebuf + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+        make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+  __syncwarp();
+  const int g = lane & 7;
+  const unsigned long long mine = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    const float4 x = *reinterpret_cast<const float4*>(ebuf + r * 128 + ((g ^ (r & 7)) << 4));
+    const unsigned long long d = __shfl_sync(0xffffffffu, mine, r);
+    if (d != 0ull) reinterpret_cast<float4*>(d)[g] = x;
   }
   __syncwarp();
 }
@@ -559,7 +584,43 @@ __global__ void __launch_bounds__(kThreads2, 1)
       // is free: 4 KB of it per softmax warp stages the epilogue's row transposes.
       uint8_t* ebuf = sK + (warp - 4) * 4096;
       const bool in_range = qrow < p.Lq;
-      if (nsplit > 1) {
+      if (p.sc_o != nullptr) {
+        // Partial of this key slice to the row's owner(s), in their (peer-mapped) buffers:
+        // O / l in fp32 and the LSE (-inf when the slice saw no visible key).
+        const bool seen = m_run != -INFINITY;
+        const float inv_l = seen ? __frcp_rn(l) : 0.f;
+        const float lse_v = seen ? (m_run * kLn2 + __logf(l)) : -INFINITY;
+        const int R = p.sc_rows + (p.Lq - p.Li);
+        const size_t slab = ((static_cast<size_t>(p.sc_index0 + split) * p.B + b) * p.H + h) * R;
+        const bool txt_row = in_range && qrow >= p.Li;
+        // a text row goes to every rank; image rows to their one owner
+        const int ndest = __any_sync(0xffffffffu, txt_row) ? p.sc_ranks : 1;
+        for (int d = 0; d < ndest; ++d) {
+          float* dst = nullptr;
+          float* dl = nullptr;
+          if (in_range && (txt_row || d == 0)) {
+            const int owner = txt_row ? d : qrow / p.sc_rows;
+            const size_t lrow = slab + (txt_row ? p.sc_rows + (qrow - p.Li) : qrow % p.sc_rows);
+            dst = p.sc_o[owner] + lrow * kHD;
+            dl = p.sc_lse[owner] + lrow;
+          }
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t r[32];
+            if (have_o) {
+              tmem_ld32_wait(t_o + c4 * 32, r);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = 0u;
+            }
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * inv_l;
+            warp_store_f32_rows_to(ebuf, v, dst != nullptr ? dst + c4 * 32 : nullptr, lane);
+          }
+          if (dl != nullptr) *dl = lse_v;
+        }
+      } else if (nsplit > 1) {
         // Partial result of this key slice: O / l in fp32 and its LSE (-inf when the slice
         // saw no visible key); query validity is applied by the merge.
         const bool seen = m_run != -INFINITY;  // some key of the slice is visible to this row
@@ -761,6 +822,59 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const AttnKParams p, 
   }
 }
 
+// Owner side of a partial scatter: one warp per (batch, head, row) of this rank's buffers, the
+// lane's four columns of the `count` partials merged by log-sum-exp (the merge of
+// dynamic_ring_attention.py:86-105 over all partials at once).
+struct MergePartialsParams {
+  int count, B, H, rows, txt;
+  const float* o;
+  const float* lse;
+  __nv_bfloat16* out_img;
+  long long oi_b, oi_t, oi_h;
+  __nv_bfloat16* out_txt;
+  long long ot_b, ot_t, ot_h;
+  const uint8_t* text_mask;
+  long long tm_sb;
+  float* lse_out;
+};
+
+__global__ void __launch_bounds__(256) merge_partials_kernel(const MergePartialsParams p) {
+  const int R = p.rows + p.txt;
+  const long long total = static_cast<long long>(p.B) * p.H * R;
+  const long long slice = total;  // elements between consecutive partial indices (rows)
+  const int lane = threadIdx.x & 31;
+  for (long long r = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5; r < total;
+       r += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const int lr = static_cast<int>(r % R);
+    const long long bh = r / R;
+    const int h = static_cast<int>(bh % p.H);
+    const int b = static_cast<int>(bh / p.H);
+    float m = -INFINITY;
+    for (int sp = 0; sp < p.count; ++sp) m = fmaxf(m, __ldg(p.lse + sp * slice + r));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float wsum = 0.f;
+    if (m != -INFINITY) {
+      for (int sp = 0; sp < p.count; ++sp) {
+        const float w = __expf(__ldg(p.lse + sp * slice + r) - m);
+        wsum += w;
+        const float4 o = __ldg(reinterpret_cast<const float4*>(p.o + (sp * slice + r) * kHD) + lane);
+        acc.x += w * o.x;
+        acc.y += w * o.y;
+        acc.z += w * o.z;
+        acc.w += w * o.w;
+      }
+    }
+    const bool img = lr < p.rows;
+    const bool valid = img || p.text_mask == nullptr || p.text_mask[b * p.tm_sb + (lr - p.rows)] != 0;
+    const float inv = (wsum > 0.f && valid) ? 1.f / wsum : 0.f;
+    __nv_bfloat16* dst = img ? p.out_img + b * p.oi_b + static_cast<long long>(lr) * p.oi_t + h * p.oi_h
+                             : p.out_txt + b * p.ot_b + static_cast<long long>(lr - p.rows) * p.ot_t + h * p.ot_h;
+    *reinterpret_cast<uint2*>(dst + lane * 4) =
+        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+    if (p.lse_out != nullptr && lane == 0) p.lse_out[r] = (wsum > 0.f && valid) ? m + __logf(wsum) : -INFINITY;
+  }
+}
+
 // ------------------------------------------------------------------ staging kernels
 struct StageSeg {
   const int* rows;  // token -> source row map (history ring), or null
@@ -939,7 +1053,7 @@ __global__ void __launch_bounds__(256) key_bits_kernel(int B, int Lk, int kwords
 }
 
 struct MaskParams {
-  int B, Lh, Li, Lt, Lk, kwords, Lq, qwords, attend_txt;
+  int B, Lh, Li, Lik, Lt, Lk, kwords, Lq, qwords, attend_txt;  // Li image queries, Lik image keys
   const int* hist_rows;
   const uint8_t* cache_mask;
   long long cm_sb;
@@ -965,10 +1079,10 @@ __global__ void __launch_bounds__(256) mask_kernel(const MaskParams p) {
         if (k < p.Lh) {
           const int row = p.hist_rows != nullptr ? p.hist_rows[k] : k;
           vis = p.cache_mask == nullptr || p.cache_mask[(p.cm_bcast ? 0 : b) * p.cm_sb + row] != 0;
-        } else if (k < p.Lh + p.Li) {
+        } else if (k < p.Lh + p.Lik) {
           vis = true;
         } else if (k < p.Lk) {
-          vis = p.text_mask == nullptr || p.text_mask[b * p.tm_sb + (k - p.Lh - p.Li)] != 0;
+          vis = p.text_mask == nullptr || p.text_mask[b * p.tm_sb + (k - p.Lh - p.Lik)] != 0;
         } else {
           vis = false;
         }
@@ -1166,7 +1280,9 @@ UnitMap plan_units(const AttnKParams& kp, int cap, int sms) {
   const char* e = getenv("HYB_KV_SPLITS");
   const int forced = e != nullptr ? atoi(e) : 0;
   int uniform = 0;
-  if (forced >= 1) {
+  if (kp.sc_o != nullptr) {
+    uniform = cap;  // every pair cut into exactly the scatter's slice count
+  } else if (forced >= 1) {
     uniform = imin(forced, cap);
   } else if (cap <= 1) {
     uniform = 1;
@@ -1267,10 +1383,10 @@ UnitMap plan_units(const AttnKParams& kp, int cap, int sms) {
   return um;
 }
 
-WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lt, int attend_txt, int sms) {
+WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lik, int Lt, int attend_txt, int sms) {
   WorkspaceLayout w;
   w.Lq = Li + Lt;
-  w.Lk = Lh + Li + (attend_txt ? Lt : 0);
+  w.Lk = Lh + Lik + (attend_txt ? Lt : 0);
   w.kwords = ((w.Lk + kBN - 1) / kBN) * (kBN / 32);
   w.qwords = (w.Lq + 31) / 32;
   long long off = 0;
@@ -1355,12 +1471,12 @@ int fill_params(const hyb_attn_args* a, AttnKParams& kp) {
   if (!al16(a->q) || !al16(a->k) || !al16(a->v)) return fail(HYB_ERR_INVALID_ARG, "attention: q/k/v misaligned");
   if (a->kwords < ((a->Lk + kBN - 1) / kBN) * (kBN / 32) || (a->kwords % 4) != 0 || !al16(a->kbits))
     return fail(HYB_ERR_INVALID_ARG, "attention: kbits must hold 4 aligned words per key tile");
-  if (a->img_len > 0) {
+  if (a->img_len > 0 && a->scatter == nullptr) {  // a partial scatter writes no final rows here
     if (a->out_img == nullptr || !al16(a->out_img) || (a->oi_sb % 8) || (a->oi_st % 8) || (a->oi_sh % 8) ||
         (a->oi_sseg % 8) || a->oi_seg <= 0)
       return fail(HYB_ERR_INVALID_ARG, "attention: image output misaligned");
   }
-  if (a->Lq > a->img_len) {
+  if (a->Lq > a->img_len && a->scatter == nullptr) {
     if (a->out_txt == nullptr || !al16(a->out_txt) || (a->ot_sb % 8) || (a->ot_st % 8) || (a->ot_sh % 8))
       return fail(HYB_ERR_INVALID_ARG, "attention: text output misaligned");
   }
@@ -1403,6 +1519,24 @@ int fill_params(const hyb_attn_args* a, AttnKParams& kp) {
   kp.kv_splits = a->kv_splits > 1 ? a->kv_splits : 1;
   kp.part_o = a->part_o;
   kp.part_lse = a->part_lse;
+  if (a->scatter != nullptr) {
+    const hyb_part_scatter* sc = a->scatter;
+    if (sc->o == nullptr || sc->lse == nullptr || sc->ranks < 1 || sc->ranks > 64 || sc->rows <= 0 ||
+        sc->slices < 1 || sc->slices > 16 || sc->index0 < 0 || sc->index0 + sc->slices > sc->count)
+      return fail(HYB_ERR_INVALID_ARG, "attention: bad partial scatter (ranks %d, rows %d, slices %d, index0 %d, count %d)",
+                  sc->ranks, sc->rows, sc->slices, sc->index0, sc->count);
+    if (static_cast<long long>(sc->ranks) * sc->rows < a->img_len)
+      return fail(HYB_ERR_INVALID_ARG, "attention: %d ranks x %d rows do not own the %d image queries", sc->ranks,
+                  sc->rows, a->img_len);
+    if (a->acc_o != nullptr) return fail(HYB_ERR_INVALID_ARG, "attention: partial scatter with a ring accumulator");
+    kp.sc_o = sc->o;
+    kp.sc_lse = sc->lse;
+    kp.sc_ranks = sc->ranks;
+    kp.sc_rows = sc->rows;
+    kp.sc_index0 = sc->index0;
+    kp.kv_splits = sc->slices;
+    return HYB_OK;
+  }
   if (kp.kv_splits > 1 && (a->part_o == nullptr || a->part_lse == nullptr || !al16(a->part_o)))
     return fail(HYB_ERR_INVALID_ARG, "attention: kv_splits > 1 needs 16-byte aligned partial buffers");
   return HYB_OK;
@@ -1420,7 +1554,7 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   if ((rc = make_map(&mv, a->v, BH, a->Lk > 0 ? a->Lk : 1, a->v_f16 != 0)) != HYB_OK) return rc;
   const UnitMap um = plan_units(kp, kp.kv_splits, device_sm_count());
   int rc2 = launch_attn2(mq, mk, mv, kp, um, a->v_f16 != 0, stream);
-  if (rc2 != HYB_OK || um.max_k <= 1) return rc2;
+  if (rc2 != HYB_OK || um.max_k <= 1 || kp.sc_o != nullptr) return rc2;  // owners merge scattered rows
   const long long rows = static_cast<long long>(kp.B) * kp.H * kp.Lq;
   merge_splits_kernel<<<grid_for(rows * 32, 256), 256, 0, stream>>>(kp, um);
   HYB_CHECK_LAUNCH();
@@ -1450,6 +1584,46 @@ extern "C" int hyb_attn_work_plan(const hyb_attn_args* a, int32_t sms, int32_t* 
     splits[qp] = um.uniform > 0 ? um.uniform : um.prefix[i + 1] - um.prefix[i];
   }
   return um.npairs;
+}
+
+extern "C" int hyb_merge_partials(int32_t count, int32_t B, int32_t H, int32_t D, int32_t rows, int32_t txt_rows,
+                                  const float* part_o, const float* part_lse, void* out_img, int64_t oi_sb,
+                                  int64_t oi_st, int64_t oi_sh, void* out_txt, int64_t ot_sb, int64_t ot_st,
+                                  int64_t ot_sh, const uint8_t* text_mask, int64_t text_mask_sb, float* lse,
+                                  void* stream) {
+  if (D != kHD) return fail(HYB_ERR_UNSUPPORTED, "merge partials: head_dim %d != 128", D);
+  if (count < 1 || B < 0 || H < 0 || rows < 0 || txt_rows < 0 || part_o == nullptr || part_lse == nullptr ||
+      !al16(part_o))
+    return fail(HYB_ERR_INVALID_ARG, "merge partials: bad sizes or buffers");
+  if ((rows > 0 && (out_img == nullptr || (reinterpret_cast<uintptr_t>(out_img) & 7u) || (oi_sb % 4) || (oi_st % 4) ||
+                    (oi_sh % 4))) ||
+      (txt_rows > 0 && (out_txt == nullptr || (reinterpret_cast<uintptr_t>(out_txt) & 7u) || (ot_sb % 4) ||
+                        (ot_st % 4) || (ot_sh % 4))))
+    return fail(HYB_ERR_INVALID_ARG, "merge partials: outputs must be 8-byte aligned rows");
+  const long long total = static_cast<long long>(B) * H * (rows + txt_rows);
+  if (total == 0) return HYB_OK;
+  MergePartialsParams p;
+  p.count = count;
+  p.B = B;
+  p.H = H;
+  p.rows = rows;
+  p.txt = txt_rows;
+  p.o = part_o;
+  p.lse = part_lse;
+  p.out_img = static_cast<__nv_bfloat16*>(out_img);
+  p.oi_b = oi_sb;
+  p.oi_t = oi_st;
+  p.oi_h = oi_sh;
+  p.out_txt = static_cast<__nv_bfloat16*>(out_txt);
+  p.ot_b = ot_sb;
+  p.ot_t = ot_st;
+  p.ot_h = ot_sh;
+  p.text_mask = text_mask;
+  p.tm_sb = text_mask_sb;
+  p.lse_out = lse;
+  merge_partials_kernel<<<grid_for(total * 32, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
 }
 
 extern "C" int hyb_stage_head_major(int32_t B, int32_t L, int32_t H, int32_t D, const hyb_tensor4* src_k,
@@ -1530,7 +1704,7 @@ extern "C" int hyb_fill_key_bits(int32_t B, int32_t Lk, int32_t kwords, uint32_t
 extern "C" int64_t hyb_cached_attention_workspace_bytes(int32_t B, int32_t H, int32_t D, int32_t valid_len,
                                                         int32_t img_len, int32_t txt_len, int32_t attend_txt) {
   if (D != kHD || B < 0 || H < 0 || valid_len < 0 || img_len < 0 || txt_len < 0) return -1;
-  return layout_for(B, H, valid_len, img_len, txt_len, attend_txt, device_sm_count()).total;
+  return layout_for(B, H, valid_len, img_len, img_len, txt_len, attend_txt, device_sm_count()).total;
 }
 
 extern "C" int hyb_cached_attention_workspace_layout(int32_t B, int32_t H, int32_t D, int32_t valid_len,
@@ -1540,7 +1714,7 @@ extern "C" int hyb_cached_attention_workspace_layout(int32_t B, int32_t H, int32
   if (D != kHD) return fail(HYB_ERR_UNSUPPORTED, "workspace layout: head_dim %d != 128", D);
   if (B < 0 || H < 0 || valid_len < 0 || img_len < 0 || txt_len < 0)
     return fail(HYB_ERR_INVALID_ARG, "workspace layout: negative sizes");
-  const WorkspaceLayout w = layout_for(B, H, valid_len, img_len, txt_len, attend_txt, device_sm_count());
+  const WorkspaceLayout w = layout_for(B, H, valid_len, img_len, img_len, txt_len, attend_txt, device_sm_count());
   out->q = w.q;
   out->k = w.k;
   out->v = w.v;
@@ -1566,9 +1740,13 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     return fail(HYB_ERR_INVALID_ARG, "cached attention: negative sizes");
   if (a->cache_batch != a->B && a->cache_batch != 1)
     return fail(HYB_ERR_INVALID_ARG, "KV-cache batch mismatch: current=%d, cache=%d", a->B, a->cache_batch);
+  if (a->img_k_len < 0 || (a->scatter == nullptr && a->img_k_len > 0 && a->img_k_len != a->img_len))
+    return fail(HYB_ERR_INVALID_ARG, "cached attention: img_k_len %d differs from img_len %d without a partial "
+                "scatter", a->img_k_len, a->img_len);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const int Lh = a->valid_len, Li = a->img_len, Lt = a->txt_len;
-  const WorkspaceLayout w = layout_for(a->B, a->H, Lh, Li, Lt, a->attend_txt, device_sm_count());
+  const int Lik = a->img_k_len > 0 ? a->img_k_len : Li;
+  const WorkspaceLayout w = layout_for(a->B, a->H, Lh, Li, Lik, Lt, a->attend_txt, device_sm_count());
   if (a->workspace == nullptr || a->workspace_bytes < w.total || !al16(a->workspace))
     return fail(HYB_ERR_WORKSPACE, "cached attention: workspace %lld bytes < %lld needed",
                 (long long)a->workspace_bytes, (long long)w.total);
@@ -1578,8 +1756,8 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     if ((rc = check_view(a->hist_v, "hist_v", true)) != HYB_OK) return rc;
     if (a->hist_k.fmt != a->hist_v.fmt) return fail(HYB_ERR_INVALID_ARG, "KV cache K/V dtype mismatch");
   }
-  if (Li > 0) {
-    if ((rc = check_view(a->img_q, "img_q", false)) != HYB_OK) return rc;
+  if (Li > 0 && (rc = check_view(a->img_q, "img_q", false)) != HYB_OK) return rc;
+  if (Lik > 0) {
     if ((rc = check_view(a->img_k, "img_k", true)) != HYB_OK) return rc;
     if ((rc = check_view(a->img_v, "img_v", true)) != HYB_OK) return rc;
   }
@@ -1602,6 +1780,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   mp.B = a->B;
   mp.Lh = Lh;
   mp.Li = Li;
+  mp.Lik = Lik;
   mp.Lt = Lt;
   mp.Lk = w.Lk;
   mp.kwords = w.kwords;
@@ -1628,7 +1807,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     sp.nout = 2;
     sp.nseg = 0;
     const hyb_tensor4* srcs[2][3] = {{&a->hist_k, &a->img_k, &a->txt_k}, {&a->hist_v, &a->img_v, &a->txt_v}};
-    const int lens[3] = {Lh, Li, a->attend_txt ? Lt : 0};
+    const int lens[3] = {Lh, Lik, a->attend_txt ? Lt : 0};
     for (int si = 0; si < 3; ++si) {
       if (lens[si] == 0) continue;
       for (int o = 0; o < 2; ++o)
@@ -1671,6 +1850,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   at.Lk = w.Lk;
   at.hist_len = Lh;
   at.img_len = Li;
+  at.img_k_len = Lik;
   at.group_tokens = a->group_tokens;
   at.softmax_scale = a->softmax_scale;
   at.q_pos0 = a->q_pos0;
@@ -1698,6 +1878,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   at.v_f16 = 1;
   at.part_o = reinterpret_cast<float*>(ws + w.part_o);
   at.part_lse = reinterpret_cast<float*>(ws + w.part_lse);
+  at.scatter = a->scatter;
   return attn_core(&at, stream);
 }
 

@@ -25,6 +25,9 @@
  *                                chunk-causal ranges of attention/magi_attn.py:290-309
  *   hyb_lse_merge             <- flash_attn_fwd_out_correction / _softmax_lse_correction
  *                                hymm/models/dit/modules/attention/dynamic_ring_attention.py:86-105
+ *   hyb_part_scatter +        <- the same merge for sequence-parallel attention over a
+ *   hyb_merge_partials           sequence-sharded (KV-stationary) cache: partial rows written to
+ *                                their owner ranks by the attention epilogue, merged there
  *   hyb_ulysses_pack_qkv      <- pack_qkv + all_to_all_qkv send-side layout
  *                                reactor/hy_nomas_fusions.py:56-78, hymm/distributed/communications.py:270-280
  *   hyb_ulysses_unpack_o      <- _all_to_all_4D(scatter_idx=1, gather_idx=2) receive-side layout
@@ -40,7 +43,7 @@
 extern "C" {
 #endif
 
-#define HYB_ABI_VERSION 3
+#define HYB_ABI_VERSION 4
 
 /* status codes */
 #define HYB_OK 0
@@ -79,6 +82,24 @@ typedef struct hyb_tensor4 {
  * Text queries see every visible key.  History key t is visible iff cache_mask[b, t];
  * text key t iff text_mask[b, t].  Output rows of masked text queries are zero
  * (the flash3 path's pad_tokens semantics, nomas_cpt.py:823-829). */
+/* Partial rows scattered to their owners: sequence-parallel attention over a sequence-sharded
+ * ("KV-stationary") cache.  Every rank attends all queries of the chunk to the keys it holds;
+ * the epilogue writes each query row's partial result for its key slice (O / l in fp32 and the
+ * natural-log LSE, -inf when the slice saw no visible key) straight into the buffers of the rank
+ * that owns the row (peer-mapped memory), where hyb_merge_partials combines the partials.
+ * Image query q belongs to rank q / rows at local row q % rows; text query t is written to every
+ * rank, at local row rows + t.  Owner buffers (device arrays of `ranks` pointers, each the
+ * owner's buffer as mapped on the calling rank): o fp32 [count, B, H, rows + txt, D], lse fp32
+ * [count, B, H, rows + txt].  This launch writes partial indices [index0, index0 + slices): every
+ * query pair's key tiles are cut into exactly `slices` slices (1..16).  No reference counterpart
+ * in code (the reference passes K/V around a ring, dynamic_ring_attention.py:115-286; its merge
+ * formula, :86-105, is the one applied here). */
+typedef struct hyb_part_scatter {
+  float* const* o;
+  float* const* lse;
+  int32_t ranks, rows, index0, count, slices, pad_;
+} hyb_part_scatter;
+
 typedef struct hyb_cached_attn_args {
   int32_t abi_version;     /* HYB_ABI_VERSION */
   int32_t B, H, D;         /* batch, heads on this rank, head_dim (128) */
@@ -107,7 +128,11 @@ typedef struct hyb_cached_attn_args {
   float* lse;              /* fp32 [B, H, img_len + txt_len] natural-log LSE, or NULL */
   void* workspace; int64_t workspace_bytes;
   int32_t* dev_status;     /* int32 on the device, OR-ed with HYB_DEV_* bits, or NULL */
-  int32_t pad_;
+  int32_t img_k_len;       /* current image keys [B, img_k_len, H, D] in img_k/img_v; 0 means
+                              img_len (the chunk attends to itself).  A rank of a KV-stationary
+                              schedule passes all queries of the chunk and its own keys */
+  const hyb_part_scatter* scatter;  /* NULL, or: partial rows go to their owners (out_img/out_txt
+                                       unused, no merge here) */
 } hyb_cached_attn_args;
 
 /* Library identity. */
@@ -196,6 +221,8 @@ typedef struct hyb_attn_args {
   float* acc_lse;
   int32_t acc_mode;
   int32_t pad2_;
+  const hyb_part_scatter* scatter;  /* NULL, or: partial rows go to their owners (see above);
+                                       kv_splits and part_o/part_lse are then unused */
 } hyb_attn_args;
 int hyb_attn_fwd(const hyb_attn_args* args, void* stream);
 
@@ -239,6 +266,19 @@ int hyb_fill_key_bits(int32_t B, int32_t Lk, int32_t kwords, uint32_t* bits, voi
 int hyb_lse_merge(int32_t rows, int32_t H, int32_t D,
                   float* out_acc, float* lse_acc, const void* out_b, int32_t out_b_fmt,
                   const float* lse_b, void* stream);
+
+/* Owner side of hyb_part_scatter: the `count` partials of each row of this rank's buffers
+ * (o [count, B, H, rows + txt_rows, D], lse [count, B, H, rows + txt_rows]) merged by
+ * log-sum-exp (dynamic_ring_attention.py:86-105) into bf16 out_img [B, rows, H, D] and out_txt
+ * [B, txt_rows, H, D] (element strides).  A text row whose text_mask entry (bool [B, txt_rows],
+ * or NULL: all valid) is false, and a row that no partial saw, is written as zeros (the
+ * reference's padded text queries, nomas_cpt.py:807-829).  lse (fp32 [B, H, rows + txt_rows]) may
+ * be NULL. */
+int hyb_merge_partials(int32_t count, int32_t B, int32_t H, int32_t D, int32_t rows, int32_t txt_rows,
+                       const float* part_o, const float* part_lse,
+                       void* out_img, int64_t oi_sb, int64_t oi_st, int64_t oi_sh,
+                       void* out_txt, int64_t ot_sb, int64_t ot_st, int64_t ot_sh,
+                       const uint8_t* text_mask, int64_t text_mask_sb, float* lse, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Peer-memory exchange for Ulysses sequence parallelism (one process per GPU).  Buffers are

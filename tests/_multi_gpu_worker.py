@@ -2,7 +2,8 @@
 
 Runs the drop-in with Ulysses sequence parallelism over all ranks and checks, on rank 0, that
 the gathered result (and the head-sharded cache writes) equal a single-GPU call on the whole
-problem.  Prints "MULTI_GPU_OK" on success."""
+problem; then the ring schedules and the KV-stationary schedule against their one-process
+emulations.  Prints "MULTI_GPU_OK" on success."""
 import datetime
 import os
 import sys
@@ -120,6 +121,30 @@ def main():
                   (out_ring.float() - plan.shard(emu, rank).float()).abs().max().item())
             ok = False
     ring.release_ring_states()
+    # ---- KV-stationary schedule (Q all-gather, partial rows scattered by the attention epilogue
+    # to their owners over peer memory) over all ranks: equals the emulated single-process
+    # schedule bit for bit, over a rollout that wraps the window
+    from hy_nomas_b200.kv_stationary import KVStationaryAttention, kv_stationary_emulated
+    from hy_nomas_b200.window import SinkWindowKVCache
+    Hk, Ltk = 4, 1
+    Lsk = 96
+    Tk = Lsk * world
+    win = SinkWindowKVCache(1, Hk, Lsk, 1, 2, device=dev)
+    wins = [SinkWindowKVCache(1, Hk, Lsk, 1, 2, device=dev) for _ in range(world)]
+    kvs = KVStationaryAttention(None, 1, Lsk, Hk, Ltk, 3 * Lsk, dev)
+    gk = make_generator(515)
+    sl2 = slice(rank * Lsk, (rank + 1) * Lsk)
+    for step in range(4):
+        fq, fk, fv = (seeded_kv((1, Tk, Hk, D), gk).to(dev) for _ in range(3))
+        tq2, tk2, tv2 = (seeded_kv((1, Ltk, Hk, D), gk).to(dev) for _ in range(3))
+        with torch.no_grad():
+            o_img, o_txt = kvs(fq[:, sl2], fk[:, sl2], fv[:, sl2], tq2, tk2, tv2, win)
+            e_img, e_txt = kv_stationary_emulated(fq, fk, fv, tq2, tk2, tv2, wins, slices=kvs.slices)
+        if not (torch.equal(o_img, e_img[:, sl2]) and torch.equal(o_txt, e_txt)):
+            print("KV-stationary mismatch on rank", rank, "step", step,
+                  (o_img.float() - e_img[:, sl2].float()).abs().max().item())
+            ok = False
+    kvs.close()
     ok_t = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
     ok = bool(ok_t.item())

@@ -46,10 +46,13 @@ int main(void) {
   F(hyb_cached_attn_args, txt_v) F(hyb_attn_args, k_pos0)
   F(hyb_cached_attn_args, hist_rows) F(hyb_cached_attn_args, cache_mask) F(hyb_cached_attn_args, oi_seg)
   F(hyb_cached_attn_args, out_txt) F(hyb_cached_attn_args, lse) F(hyb_cached_attn_args, workspace_bytes)
-  F(hyb_cached_attn_args, dev_status)
+  F(hyb_cached_attn_args, dev_status) F(hyb_cached_attn_args, img_k_len) F(hyb_cached_attn_args, scatter)
   F(hyb_attn_args, q) F(hyb_attn_args, kwords) F(hyb_attn_args, qbits) F(hyb_attn_args, oi_sseg)
   F(hyb_attn_args, lse) F(hyb_attn_args, dev_status) F(hyb_attn_args, kv_splits) F(hyb_attn_args, v_f16) F(hyb_attn_args, part_lse)
   F(hyb_attn_args, img_k_len) F(hyb_attn_args, k_pos1) F(hyb_attn_args, acc_o) F(hyb_attn_args, acc_mode)
+  F(hyb_attn_args, scatter)
+  printf("hyb_part_scatter %zu\n", sizeof(hyb_part_scatter));
+  F(hyb_part_scatter, lse) F(hyb_part_scatter, ranks) F(hyb_part_scatter, count) F(hyb_part_scatter, slices)
   printf("hyb_peer_sync %zu\n", sizeof(hyb_peer_sync));
   F(hyb_peer_sync, state) F(hyb_peer_sync, dev_status)
   printf("hyb_workspace_layout %zu\n", sizeof(hyb_workspace_layout));
@@ -69,7 +72,7 @@ def test_ctypes_layouts_match_c(tmp_path):
     c = dict(line.rsplit(" ", 1) for line in out.strip().splitlines())
     types = {"hyb_tensor4": _lib.Tensor4, "hyb_cached_attn_args": _lib.CachedAttnArgs,
              "hyb_attn_args": _lib.AttnArgs, "hyb_workspace_layout": _lib.WorkspaceLayout,
-             "hyb_peer_sync": _lib.PeerSync}
+             "hyb_peer_sync": _lib.PeerSync, "hyb_part_scatter": _lib.PartScatter}
     for key, val in c.items():
         if "." in key:
             t, m = key.split(".")
@@ -103,6 +106,33 @@ def test_status_codes_for_rejected_calls():
     args = _lib.CachedAttnArgs()
     args.abi_version = 99
     assert lib.hyb_cached_attention(args, None) == _lib.HYB_ERR_INVALID_ARG
+
+
+def test_partial_scatter_arguments_are_checked_before_any_launch():
+    """A bad hyb_part_scatter (no slices, too few owner rows for the image queries, a ring
+    accumulator at the same time) and a bad owner merge are argument errors; nothing runs."""
+    lib = _lib.load()
+    table = (ctypes.c_void_p * 2)(16, 32)
+    a = _lib.AttnArgs()
+    a.abi_version = _lib.HYB_ABI_VERSION
+    a.B, a.H, a.D, a.Lq, a.Lk, a.img_len, a.img_k_len = 1, 2, 128, 300, 100, 300, 100
+    a.q = a.k = a.v = 256
+    a.kbits, a.kwords = 256, 4
+    for ranks, rows, slices, index0, count in ((2, 150, 0, 0, 2), (2, 100, 1, 0, 2), (2, 150, 2, 1, 2)):
+        sc = _lib.PartScatter(ctypes.cast(table, ctypes.c_void_p), ctypes.cast(table, ctypes.c_void_p),
+                              ranks, rows, index0, count, slices, 0)
+        a.scatter = ctypes.cast(ctypes.pointer(sc), ctypes.c_void_p)
+        assert lib.hyb_attn_fwd(ctypes.byref(a), None) == _lib.HYB_ERR_INVALID_ARG
+        assert "scatter" in _lib.last_error() or "own" in _lib.last_error()
+    assert lib.hyb_merge_partials(1, 1, 2, 64, 4, 0, 256, 256, 256, 8, 8, 8, None, 0, 0, 0, None, 0, None,
+                                  None) == _lib.HYB_ERR_UNSUPPORTED
+    assert lib.hyb_merge_partials(0, 1, 2, 128, 4, 0, 256, 256, 256, 8, 8, 8, None, 0, 0, 0, None, 0, None,
+                                  None) == _lib.HYB_ERR_INVALID_ARG
+    c = _lib.CachedAttnArgs()
+    c.abi_version = _lib.HYB_ABI_VERSION
+    c.B, c.H, c.D, c.cache_batch, c.img_len, c.img_k_len = 1, 2, 128, 1, 64, 32
+    assert lib.hyb_cached_attention(ctypes.byref(c), None) == _lib.HYB_ERR_INVALID_ARG
+    assert "img_k_len" in _lib.last_error()
 
 
 def test_workspace_size_formula():

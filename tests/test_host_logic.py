@@ -346,3 +346,14 @@ def test_a_row_map_without_its_window_must_name_cache_rows(monkeypatch):
              "history_rows": torch.tensor([0, 5, 40], dtype=torch.int32)}
     with torch.no_grad(), pytest.raises(ValueError, match="history_rows must name rows of the cache"):
         hatt.causal_attention_with_cache_mp((x, t), (x, t), (x, t), cache, cache_valid_len=3, attn_mode="flash3")
+
+
+def test_kv_stationary_slice_choice():
+    """Key slices per query pair of a partial-scatter launch: enough CTAs to fill the SMs,
+    never fewer than 4 key tiles a slice (config 5 at P = 8: 1,561 queries x 24 heads against
+    6,631 keys on each rank)."""
+    from hy_nomas_b200.kv_stationary import choose_slices
+    s = choose_slices(1, 24, 1561, 6631, 148)
+    assert 2 <= s <= 8
+    assert choose_slices(1, 24, 1561, 300, 148) == 1
+    assert choose_slices(1, 2, 256, 128 * 64, 148) >= 8
