@@ -72,3 +72,50 @@ def lse_merge(out_acc, lse_acc, out_b, lse_b):
     wa = wa.transpose(0, 1)[..., None]                  # [S, H, 1]
     wb = wb.transpose(0, 1)[..., None]
     return out_acc * wa + out_b * wb, lse
+
+
+def partial_attention(q, k, v, scale=None):
+    """Softmax attention of q [B, Lq, H, D] over k/v [B, Lk, H, D] in float64: returns the
+    normalised rows O [B, Lq, H, D] and their natural-log LSE [B, H, Lq] (-inf and zero rows
+    when there is no key), the partial result one rank contributes for its keys."""
+    B, Lq, H, D = q.shape
+    scale = scale or D ** -0.5
+    if k.shape[1] == 0:
+        return torch.zeros(B, Lq, H, D, dtype=torch.float64), torch.full((B, H, Lq), float("-inf"), dtype=torch.float64)
+    s = torch.einsum("bqhd,bkhd->bhqk", q.double(), k.double()) * scale
+    lse = torch.logsumexp(s, dim=-1)
+    p = torch.exp(s - lse[..., None])
+    return torch.einsum("bhqk,bkhd->bqhd", p, v.double()), lse
+
+
+def kv_stationary_step(q_slice, k_slice, v_slice, txt_q, txt_k, txt_v, hist_k, hist_v, group=None):
+    """One step of the KV-stationary schedule restated on CPU with torch.distributed collectives
+    (the protocol of hy_nomas_b200/kv_stationary.py; no reference counterpart in code, whose ring
+    passes K/V instead, dynamic_ring_attention.py:115-286).  Rank r holds its slice of the frame
+    (q/k/v_slice [B, Ls, H, D]), its history keys hist_k/hist_v [B, Lh_r, H, D] and the text
+    tokens (the same on every rank).  Q is all-gathered; each rank attends every query to its
+    keys (text keys on rank 0 only); the partial rows of image query q go to rank q // Ls and the
+    text rows to every rank; the owner merges them (lse_merge).  Returns this rank's image rows
+    [B, Ls, H, D] and the text rows [B, Lt, H, D] in float64."""
+    import torch.distributed as dist
+    P, r = dist.get_world_size(group), dist.get_rank(group)
+    B, Ls, H, D = q_slice.shape
+    Lt = txt_q.shape[1]
+    gathered = [torch.empty_like(q_slice) for _ in range(P)]
+    dist.all_gather(gathered, q_slice.contiguous(), group=group)
+    q_all = torch.cat(gathered + [txt_q], dim=1)                 # [B, P*Ls + Lt, H, D]
+    keys = [hist_k, k_slice] + ([txt_k] if r == 0 else [])
+    vals = [hist_v, v_slice] + ([txt_v] if r == 0 else [])
+    o, lse = partial_attention(q_all, torch.cat(keys, 1), torch.cat(vals, 1))
+    # every rank's partials reach every rank (all_gather stands in for the scatter to owners);
+    # the owner keeps its rows
+    o_all = [torch.empty_like(o) for _ in range(P)]
+    lse_all = [torch.empty_like(lse) for _ in range(P)]
+    dist.all_gather(o_all, o, group=group)
+    dist.all_gather(lse_all, lse, group=group)
+    rows = list(range(r * Ls, (r + 1) * Ls)) + list(range(P * Ls, P * Ls + Lt))
+    acc_o = o_all[0][:, rows][0]                                 # [S, H, D] (B = 1)
+    acc_lse = lse_all[0][0][:, rows]                             # [H, S]
+    for s in range(1, P):
+        acc_o, acc_lse = lse_merge(acc_o, acc_lse, o_all[s][:, rows][0], lse_all[s][0][:, rows])
+    return acc_o[None, :Ls], acc_o[None, Ls:]

@@ -106,20 +106,27 @@ def main():
     # ---- ring (KV passing) over all ranks: equals the emulated single-process schedule
     from hy_nomas_b200 import ring
     Lr, Tr = 8 * 96 + 5, 96
-    rq, rk, rv = (seeded_kv((1, Lr, 4, D), make_generator(77 + i)).to(dev) for i in range(3))
-    emu = ring.ring_attention_emulated(rq, rk, rv, world, tokens_per_frame=Tr)
+    # two inputs, called back to back with no host synchronisation between the calls: the
+    # second call's block push must wait (entry barrier) for every peer's decode of the first
+    inputs = [tuple(seeded_kv((1, Lr, 4, D), make_generator(77 + 10 * c + i)).to(dev) for i in range(3))
+              for c in range(2)]
     for schedule, layout in (("ring", "zigzag"), ("ring", "contiguous"), ("allgather", "zigzag"),
                              ("allgather", "contiguous")):
         plan = ring.RingPlan(Lr, world, layout)
-        emu = ring.ring_attention_emulated(rq, rk, rv, world, tokens_per_frame=Tr, layout=layout, schedule=schedule)
-        for _ in range(2):   # second pass reuses the cached plan and buffers
-            out_ring = ring.ring_attention(plan.shard(rq, rank).contiguous(), plan.shard(rk, rank).contiguous(),
-                                           plan.shard(rv, rank).contiguous(), None, seq_len=Lr,
-                                           tokens_per_frame=Tr, layout=layout, schedule=schedule)
-        if not torch.equal(out_ring, plan.shard(emu, rank)):
-            print("ring mismatch on rank", rank, schedule, layout,
-                  (out_ring.float() - plan.shard(emu, rank).float()).abs().max().item())
-            ok = False
+        emus = [ring.ring_attention_emulated(*x, world, tokens_per_frame=Tr, layout=layout, schedule=schedule)
+                for x in inputs]
+        outs = []
+        for rep in range(2):   # the second round reuses the cached plan and buffers
+            for rq, rk, rv in inputs:
+                outs.append(ring.ring_attention(plan.shard(rq, rank).contiguous(), plan.shard(rk, rank).contiguous(),
+                                                plan.shard(rv, rank).contiguous(), None, seq_len=Lr,
+                                                tokens_per_frame=Tr, layout=layout, schedule=schedule))
+        for i, out_ring in enumerate(outs):
+            want = plan.shard(emus[i % 2], rank)
+            if not torch.equal(out_ring, want):
+                print("ring mismatch on rank", rank, schedule, layout, "call", i,
+                      (out_ring.float() - want.float()).abs().max().item())
+                ok = False
     ring.release_ring_states()
     # ---- KV-stationary schedule (Q all-gather, partial rows scattered by the attention epilogue
     # to their owners over peer memory) over all ranks: equals the emulated single-process

@@ -149,3 +149,39 @@ def test_peer_buffer_sizes_are_checked_on_every_rank():
     be a device fault)."""
     res = _run(_worker_size_agreement)
     assert res == {0: "ok", 1: "ok"}, res
+
+
+def _worker_kv_stationary(rank, world, init_file, result_dir):
+    import sys
+    sys.path.insert(0, str(REPO))
+    status = "ok"
+    try:
+        from oracle import sp as osp
+        from oracle import attention as oatt
+        _init(rank, world, init_file)
+        g = torch.Generator().manual_seed(99)
+        B, H, D, Ls, Lt, frames = 1, 2, 128, 24, 1, 3
+        T = Ls * world
+        q, k, v = (torch.randn(B, T, H, D, generator=g).to(torch.bfloat16) for _ in range(3))
+        tq, tk, tv = (torch.randn(B, Lt, H, D, generator=g).to(torch.bfloat16) for _ in range(3))
+        hk, hv = (torch.randn(B, frames * T, H, D, generator=g).to(torch.bfloat16) for _ in range(2))
+        # this rank's slice of every history frame and of the current frame
+        mine = torch.cat([torch.arange(f * T + rank * Ls, f * T + (rank + 1) * Ls) for f in range(frames)])
+        sl = slice(rank * Ls, (rank + 1) * Ls)
+        o_img, o_txt = osp.kv_stationary_step(q[:, sl], k[:, sl], v[:, sl], tq, tk, tv, hk[:, mine], hv[:, mine])
+        ref_img, ref_txt = oatt.cached_attention(q, k, v, tq, tk, tv, hk, hv, attend_txt=True)
+        err = max((o_img - ref_img[:, sl].double()).abs().max().item(), (o_txt - ref_txt.double()).abs().max().item())
+        assert err < 1e-4, err
+        dist.destroy_process_group()
+    except Exception:
+        status = traceback.format_exc()
+    with open(os.path.join(result_dir, f"r{rank}"), "w") as f:
+        f.write(status)
+
+
+def test_kv_stationary_protocol_over_gloo():
+    """The KV-stationary schedule's protocol on 2 CPU ranks: Q all-gathered, every rank's
+    partial over its own slice of every frame (text keys on rank 0 only), each owner merging its
+    rows and every rank the text rows, equals attention over the whole history."""
+    res = _run(_worker_kv_stationary)
+    assert res == {0: "ok", 1: "ok"}, res
