@@ -595,8 +595,7 @@ def run_b200(args):
                    "heads": H_TOTAL, "head_dim": D, "history_tokens": Lh, "chunk_image_tokens": Li,
                    "text_tokens": TXT, "tokens_per_frame": T, "mask": "frame-level block-causal (G=1)",
                    "kv_cache": "fp8_e4m3 per-token-per-head scale", "append": "quantise-on-write of the chunk each step",
-                   "parallelism": (f"ulysses_sp{world}" if scheme == "ulysses" else f"kv_stationary_sp{world}")
-                   if world > 1 else "single",
+                   "parallelism": f"ulysses_sp{world}" if world > 1 else "single",
                    "exchange": ("peer memory (CUDA IPC push kernels + device barrier)"
                                 if world > 1 and os.environ.get("HYB_PEER_EXCHANGE", "1") != "0"
                                 else ("NCCL all_to_all_single" if world > 1 else None)),
@@ -915,7 +914,8 @@ def run_rollout(args):
                    "heads": H_TOTAL, "head_dim": D, "tokens_per_frame": T, "history_tokens": Lh,
                    "visible_keys": Lh + T, "sink_frames": SINK, "window_frames": KEEP, "prefill_frames": PREFILL,
                    "append": "quantise-on-write of each frame into its ring slot (no memmove)",
-                   "parallelism": f"ulysses_sp{world}" if world > 1 else "single",
+                   "parallelism": (f"ulysses_sp{world}" if scheme == "ulysses" else f"kv_stationary_sp{world}")
+                   if world > 1 else "single",
                    "l2": "inputs larger than L2 (155 MB FP8 window + 10 MB bf16 frame per step)",
                    "tflop_per_step": round(flops_total / 1e12, 4)},
         "gpu_launches": args.steps * (8 if scheme == "kv" else 6 + (2 if world > 1 else 0)),
