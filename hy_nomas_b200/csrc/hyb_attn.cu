@@ -752,6 +752,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
 // Combine the kv_splits partial results of every (batch, head, query row): LSE-weighted sum of
 // the normalised partial rows, written as bf16 at the row's final position (zero for padded
 // text queries), plus the final LSE when requested.  One warp per row, 4 dims per lane.
+constexpr int kMergeBatch = 4;  // partial rows loaded together by merge_splits_kernel
+
 __global__ void __launch_bounds__(256) merge_splits_kernel(const AttnKParams p, const __grid_constant__ UnitMap um) {
   const long long rows = static_cast<long long>(p.B) * p.H * p.Lq;
   const int lane = threadIdx.x & 31;
@@ -767,19 +769,34 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const AttnKParams p, 
     bool valid = true;
     if (p.qbits != nullptr)
       valid = (__ldg(p.qbits + static_cast<size_t>(b) * p.qwords + (qrow >> 5)) >> (qrow & 31)) & 1u;
+    // The partial rows are loaded four slices at a time before their arithmetic (four loads in
+    // flight per lane instead of one round trip per slice); the sums run in slice order.
     float m = -INFINITY;
     for (int sp = 0; sp < ns; ++sp) m = fmaxf(m, __ldg(p.part_lse + sp * slice + r));
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float wsum = 0.f;
     if (m != -INFINITY) {
-      for (int sp = 0; sp < ns; ++sp) {
-        const float w = __expf(__ldg(p.part_lse + sp * slice + r) - m);
-        wsum += w;
-        const float4 o = __ldg(reinterpret_cast<const float4*>(p.part_o + (sp * slice + r) * kHD) + lane);
-        acc.x += w * o.x;
-        acc.y += w * o.y;
-        acc.z += w * o.z;
-        acc.w += w * o.w;
+      for (int s0 = 0; s0 < ns; s0 += kMergeBatch) {
+        float lv[kMergeBatch];
+        float4 ov[kMergeBatch];
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) {
+          if (s0 + u < ns) {
+            lv[u] = __ldg(p.part_lse + (s0 + u) * slice + r);
+            ov[u] = __ldg(reinterpret_cast<const float4*>(p.part_o + ((s0 + u) * slice + r) * kHD) + lane);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) {
+          if (s0 + u < ns) {
+            const float w = __expf(lv[u] - m);
+            wsum += w;
+            acc.x += w * ov[u].x;
+            acc.y += w * ov[u].y;
+            acc.z += w * ov[u].z;
+            acc.w += w * ov[u].w;
+          }
+        }
       }
     }
     if (p.acc_o != nullptr) {

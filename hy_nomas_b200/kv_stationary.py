@@ -32,7 +32,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .attention import Workspace, cached_attention_local
+from .attention import Workspace, _assume_finite, cached_attention_local
 
 _D = 128
 
@@ -145,7 +145,9 @@ class KVStationaryAttention:
                        "KV-stationary partial barrier")
         _merge(self.owners.count, B, H, Ls, Lt, self.buf.local[2], self.buf.local[3], out_img, out_txt, text_mask, dev)
         if update_cache:
-            window.append(k, v)
+            # the drop-in's rule: without HYB_ASSUME_FINITE_KV=1 the reference's finite check
+            # runs first (a host synchronisation)
+            window.append(k, v, assume_finite=_assume_finite())
         return out_img, out_txt
 
     def close(self) -> None:
