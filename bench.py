@@ -269,7 +269,10 @@ def e2e_pipelined(step_fn, host_in, device, steps, warmup, world, static_outputs
         compute.wait_stream(h2d)
         compute.wait_stream(d2h)
 
-    run(max(6 if static_outputs else 2, warmup))   # a graphed call captures both buffer sets here
+    nwarm = max(6 if static_outputs else 2, warmup)
+    if static_outputs and nwarm % 2:
+        nwarm += 1   # static outputs alternate between two sets: the timed loop starts on set 0
+    run(nwarm)   # a graphed call captures both buffer sets here
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
@@ -858,11 +861,18 @@ def run_rollout(args):
     if scheme == "kv":
         from hy_nomas_b200.kv_stationary import KVStationaryAttention
         kvs = KVStationaryAttention(None, 1, Ls, H_TOTAL, 0, (SINK + KEEP) * Ls, device)
+        # outputs into two caller buffers used alternately (the call's out_img / out_txt), so the
+        # end-to-end loop (which reads step i back while step i+1 runs) allocates nothing
+        kv_outs = [(torch.empty((1, Ls, H_TOTAL, D), dtype=torch.bfloat16, device=device),
+                    torch.empty((1, 0, H_TOTAL, D), dtype=torch.bfloat16, device=device)) for _ in range(2)]
+        kv_calls = [0]
 
     def step(q_img, k_img, v_img, q_txt, k_txt, v_txt):
         with torch.no_grad():
             if kvs is not None:
-                return kvs(q_img, k_img, v_img, q_txt, k_txt, v_txt, win)
+                oi, ot = kv_outs[kv_calls[0] % 2]
+                kv_calls[0] += 1
+                return kvs(q_img, k_img, v_img, q_txt, k_txt, v_txt, win, out_img=oi, out_txt=ot)
             return hatt.causal_attention_with_cache_mp(
                 (q_img, q_txt), (k_img, k_txt), (v_img, v_txt), win.view(), cache_valid_len=win.valid_len,
                 update_cache=True, cache_txt=False, tokens_per_frame=T, seg_ar_attention_backend="b200",
@@ -894,7 +904,10 @@ def run_rollout(args):
     _lib.check_device_status(device)
     value = flops_total / (ms * 1e-3) / 1e12
     host_in = [t.cpu().pin_memory() for t in (*img, *txt)]
-    ems, h2d, d2h = e2e_pipelined(lambda *x: step(*x), host_in, device, args.steps, args.warmup, world)
+    if kvs is not None:
+        kv_calls[0] = 0   # step i of the loop below uses output buffer i % 2, as the loop expects
+    ems, h2d, d2h = e2e_pipelined(lambda *x: step(*x), host_in, device, args.steps, args.warmup, world,
+                                  static_outputs=kvs is not None)
     if world > 1:
         from hy_nomas_b200 import communications as comm2
         torch.cuda.synchronize(device)
