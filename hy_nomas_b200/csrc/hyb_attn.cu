@@ -806,12 +806,9 @@ __device__ __forceinline__ void merge_apply(const float (&lv)[kMergeBatch], cons
   st.m = mn;
 }
 
-// The merged row r written out (or folded into the ring accumulator).
-__device__ __forceinline__ void merge_finish(const AttnKParams& p, long long r, int lane, const MergeRow& st) {
-  const int qrow = static_cast<int>(r % p.Lq);
-  const long long bh = r / p.Lq;
-  const int h = static_cast<int>(bh % p.H);
-  const int b = static_cast<int>(bh / p.H);
+// The merged row r = (b * H + h) * Lq + qrow written out (or folded into the ring accumulator).
+__device__ __forceinline__ void merge_finish(const AttnKParams& p, long long r, int b, int h, int qrow, int lane,
+                                             const MergeRow& st) {
   const float m = st.m, wsum = st.wsum;
   const float4 acc = st.acc;
   if (p.acc_o != nullptr) {
@@ -855,26 +852,28 @@ __device__ __forceinline__ void merge_finish(const AttnKParams& p, long long r, 
   if (p.lse != nullptr && lane == 0) p.lse[r] = (wsum > 0.f && valid) ? (m + __logf(wsum)) : -INFINITY;
 }
 
+// One warp per query row: blockIdx.y = b * H + h, the block's 8 rows [8 blockIdx.x, + 8) lie
+// in one query pair (8 divides the pair's 256 rows), so a block of an unsplit pair (whose rows
+// the attention kernel wrote itself) leaves at once.  No index division per row.
 __global__ void __launch_bounds__(256, 4) merge_splits_kernel(const AttnKParams p,
                                                           const __grid_constant__ UnitMap um) {
-  const long long rows = static_cast<long long>(p.B) * p.H * p.Lq;
+  const int q_first = static_cast<int>(blockIdx.x) * 8;
+  const int ns = splits_of_pair(um, um.npairs - 1 - q_first / kPairRows);
+  if (ns <= 1) return;
+  const int qrow = q_first + (threadIdx.x >> 5);
+  if (qrow >= p.Lq) return;
   const int lane = threadIdx.x & 31;
+  const int bh = static_cast<int>(blockIdx.y);
   const long long slice = static_cast<long long>(p.B) * p.H * p.Lq;
-  for (long long r = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5; r < rows;
-       r += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
-    // key slices of the row's query pair; a row of an unsplit pair was written by the attention
-    // kernel itself
-    const int ns = splits_of_pair(um, um.npairs - 1 - static_cast<int>(r % p.Lq) / kPairRows);
-    if (ns <= 1) continue;
-    float lv[kMergeBatch];
-    float4 ov[kMergeBatch];
-    MergeRow st;
-    for (int s0 = 0; s0 < ns; s0 += kMergeBatch) {
-      merge_load(p.part_o, p.part_lse, slice, r, s0, ns, lane, lv, ov);
-      merge_apply(lv, ov, s0, ns, st);
-    }
-    merge_finish(p, r, lane, st);
+  const long long r = static_cast<long long>(bh) * p.Lq + qrow;
+  float lv[kMergeBatch];
+  float4 ov[kMergeBatch];
+  MergeRow st;
+  for (int s0 = 0; s0 < ns; s0 += kMergeBatch) {
+    merge_load(p.part_o, p.part_lse, slice, r, s0, ns, lane, lv, ov);
+    merge_apply(lv, ov, s0, ns, st);
   }
+  merge_finish(p, r, bh / p.H, bh % p.H, qrow, lane, st);
 }
 
 // Owner side of a partial scatter: one warp per (batch, head, row) of this rank's buffers, the
@@ -893,17 +892,17 @@ struct MergePartialsParams {
   float* lse_out;
 };
 
+// One warp per row: blockIdx.y = b * H + h, rows [8 blockIdx.x, + 8) of the owner's R rows.
 __global__ void __launch_bounds__(256) merge_partials_kernel(const MergePartialsParams p) {
   const int R = p.rows + p.txt;
-  const long long total = static_cast<long long>(p.B) * p.H * R;
-  const long long slice = total;  // elements between consecutive partial indices (rows)
+  const long long slice = static_cast<long long>(p.B) * p.H * R;  // elements between partial indices
   const int lane = threadIdx.x & 31;
-  for (long long r = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5; r < total;
-       r += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
-    const int lr = static_cast<int>(r % R);
-    const long long bh = r / R;
-    const int h = static_cast<int>(bh % p.H);
-    const int b = static_cast<int>(bh / p.H);
+  const int lr = static_cast<int>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (lr < R) {
+    const int bh = static_cast<int>(blockIdx.y);
+    const int h = bh % p.H;
+    const int b = bh / p.H;
+    const long long r = static_cast<long long>(bh) * R + lr;
     // four partials at a time, each LSE loaded with its row (one round trip per four)
     float lv[kMergeBatch];
     float4 ov[kMergeBatch];
@@ -986,36 +985,99 @@ __device__ __forceinline__ void load_row8(const StageSeg& s, int b, int t, int h
   }
 }
 
+// Sixteen consecutive values [16 lane8, 16 lane8 + 16) of one (batch, token, head) row as
+// fp32, by load_row8's rules (bf16 exactly; codes as code * scale, one fp32 multiply).  Codes
+// are read as two 8-byte loads: a quantised view guarantees 8-byte, not 16-byte, rows.
+__device__ __forceinline__ void load_row16(const StageSeg& s, int b, int t, int h, int lane8, float (&v)[16]) {
+  const int bb = s.bcast ? 0 : b;
+  if (s.rows != nullptr) t = __ldg(s.rows + t);
+  if (s.fmt == HYB_FMT_BF16) {
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(s.data) + bb * s.s_b +
+                                                      t * s.s_t + h * s.s_h + lane8 * 16);
+    const uint4 raw[2] = {src[0], src[1]};
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 f = __bfloat1622float2(p2[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+    return;
+  }
+  const float sc = s.scale[bb * s.c_b + t * s.c_t + h * s.c_h];
+  const uint2* src = reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(s.data) + bb * s.s_b + t * s.s_t +
+                                                    h * s.s_h + lane8 * 16);
+  const uint2 raw[2] = {src[0], src[1]};
+  const uint8_t* by = reinterpret_cast<const uint8_t*>(raw);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float a, c;
+    if (s.fmt == HYB_FMT_INT8) {
+      a = static_cast<float>(static_cast<int8_t>(by[2 * i]));
+      c = static_cast<float>(static_cast<int8_t>(by[2 * i + 1]));
+    } else {
+      const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>(by[2 * i] | (by[2 * i + 1] << 8));
+      const float2 f = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3)));
+      a = f.x;
+      c = f.y;
+    }
+    v[2 * i] = __fmul_rn(a, sc);
+    v[2 * i + 1] = __fmul_rn(c, sc);
+  }
+}
+
+// One 8-lane group per (batch, token, head) row in source order (head fastest, so the reads
+// of consecutive groups are contiguous across heads), 16 values per lane.  A group's
+// (b, t, h) is decomposed once and then advanced by the grid stride with carries, not
+// recomputed by 64-bit division per row (the division chain made the earlier 16-lane form
+// issue-bound).  Output head-major [B, H, L, 128]; the launcher checks B * L * H * 8 < 2^31.
 __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
-  const long long chunks = static_cast<long long>(p.B) * p.L * p.H * 16;
-  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < chunks;
-       c += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int sub = static_cast<int>(c & 15);
-    const long long r = c >> 4;
-    const int h = static_cast<int>(r % p.H);
-    const long long bt = r / p.H;
-    int t = static_cast<int>(bt % p.L);
-    const int b = static_cast<int>(bt / p.L);
-    const long long out_off = ((static_cast<long long>(b) * p.H + h) * p.L + t) * kHD + sub * 8;
-    int si = 0;
-    while (si < p.nseg - 1 && t >= p.seg[0][si].len) {
-      t -= p.seg[0][si].len;
+  const int Ls = p.L;
+  const int lane8 = threadIdx.x & 7;
+  const int g = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 3);
+  const int step = static_cast<int>((gridDim.x * blockDim.x) >> 3);
+  int h = g % p.H;
+  int t = (g / p.H) % Ls;
+  int b = (g / p.H) / Ls;
+  const int dh = step % p.H;
+  const int dt = (step / p.H) % Ls;
+  const int db = (step / p.H) / Ls;
+  while (b < p.B) {
+    int ts = t, si = 0;  // position within segment si
+    while (si < p.nseg - 1 && ts >= p.seg[0][si].len) {
+      ts -= p.seg[0][si].len;
       ++si;
     }
+    const long long out_off = ((static_cast<long long>(b) * p.H + h) * p.L + t) * kHD + lane8 * 16;
 #pragma unroll
     for (int o = 0; o < 2; ++o) {
       if (o < p.nout) {
-        float v[8];
-        load_row8(p.seg[o][si], b, t, h, sub, v);
-        uint4 packed;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&packed);
+        float v[16];
+        load_row16(p.seg[o][si], b, ts, h, lane8, v);
+        uint4 packed[2];
+        uint32_t* w = reinterpret_cast<uint32_t*>(packed);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 8; ++i)
           w[i] = p.out_f16[o] ? pack_f16x2(bf16_round(v[2 * i]), bf16_round(v[2 * i + 1]))
                               : pack_bf16x2(v[2 * i], v[2 * i + 1]);
-        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out[o]) + out_off) = packed;
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out[o]) + out_off);
+        dst[0] = packed[0];
+        dst[1] = packed[1];
       }
     }
+    h += dh;
+    int carry = 0;
+    if (h >= p.H) {
+      h -= p.H;
+      carry = 1;
+    }
+    t += dt + carry;
+    carry = 0;
+    if (t >= Ls) {
+      t -= Ls;
+      carry = 1;
+    }
+    b += db + carry;
   }
 }
 
@@ -1035,15 +1097,19 @@ struct GatherParams {
   __nv_bfloat16* out_v;
 };
 
+// One 8-lane group per (head, position) row, 16 values per lane, positions fastest (the
+// head-major output rows are written in order); (h, pos) advanced by the grid stride with a
+// carry instead of a 64-bit division per row.  The launcher checks H * L * 8 < 2^31.
 __global__ void __launch_bounds__(256) gather_stage_kernel(const GatherParams p) {
-  const long long chunks = static_cast<long long>(p.H) * p.L * 16;
   const long long codes = static_cast<long long>(p.Lmax) * p.H * kHD;
-  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < chunks;
-       c += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int sub = static_cast<int>(c & 15);
-    const long long r = c >> 4;
-    const int pos = static_cast<int>(r % p.L);
-    const int h = static_cast<int>(r / p.L);
+  const int lane8 = threadIdx.x & 7;
+  const int g = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 3);
+  const int step = static_cast<int>((gridDim.x * blockDim.x) >> 3);
+  int pos = g % p.L;
+  int h = g / p.L;
+  const int dpos = step % p.L;
+  const int dh = step / p.L;
+  while (h < p.H) {
     int lo = 0, hi = p.nchunks - 1;  // chunk containing pos
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
@@ -1055,7 +1121,7 @@ __global__ void __launch_bounds__(256) gather_stage_kernel(const GatherParams p)
     }
     const uint8_t* blk = p.blocks[p.owner[lo]];
     const int row = p.row0[lo] + (pos - p.bounds[lo]);
-    const long long out_off = (static_cast<long long>(h) * p.L + pos) * kHD + sub * 8;
+    const long long out_off = (static_cast<long long>(h) * p.L + pos) * kHD + lane8 * 16;
 #pragma unroll
     for (int o = 0; o < 2; ++o) {
       StageSeg sg;
@@ -1071,20 +1137,29 @@ __global__ void __launch_bounds__(256) gather_stage_kernel(const GatherParams p)
       sg.fmt = p.fmt;
       sg.len = p.Lmax;
       sg.bcast = 0;
-      float v[8];
-      load_row8(sg, 0, row, h, sub, v);
-      uint4 packed;
-      uint32_t* w = reinterpret_cast<uint32_t*>(&packed);
+      float v[16];
+      load_row16(sg, 0, row, h, lane8, v);
+      uint4 packed[2];
+      uint32_t* w = reinterpret_cast<uint32_t*>(packed);
       const bool f16 = o == 1 && p.v_f16;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 8; ++i)
         w[i] = f16 ? pack_f16x2(bf16_round(v[2 * i]), bf16_round(v[2 * i + 1])) : pack_bf16x2(v[2 * i], v[2 * i + 1]);
-      *reinterpret_cast<uint4*>((o == 0 ? p.out_k : p.out_v) + out_off) = packed;
+      uint4* dst = reinterpret_cast<uint4*>((o == 0 ? p.out_k : p.out_v) + out_off);
+      dst[0] = packed[0];
+      dst[1] = packed[1];
     }
+    pos += dpos;
+    int carry = 0;
+    if (pos >= p.L) {
+      pos -= p.L;
+      carry = 1;
+    }
+    h += dh + carry;
   }
 }
 
-// Visibility bitmap with the first Lk keys of every batch row set// Visibility bitmap with the first Lk keys of every batch row set (ring blocks: every key
+// Visibility bitmap with the first Lk keys of every batch row set (ring blocks: every key
 // of the block is valid; the block-causal rule is applied by the attention kernel).
 __global__ void __launch_bounds__(256) key_bits_kernel(int B, int Lk, int kwords, uint32_t* bits) {
   const long long n = static_cast<long long>(B) * kwords;
@@ -1203,6 +1278,36 @@ int grid_for(long long items, int threads) {
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int device_sm_count();
+
+// Blocks of 256 threads for `lanes` work lanes of a grid-striding kernel: at most one
+// resident wave (blocks per SM from the occupancy calculator, cached per kernel in *per_sm).
+template <typename K>
+long long wave_blocks(K kernel, int* per_sm, long long lanes) {
+  if (*per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 256, 0) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 4;
+    }
+    *per_sm = n;
+  }
+  long long blocks = (lanes + 255) / 256;
+  const long long wave = static_cast<long long>(device_sm_count()) * *per_sm;
+  return blocks > wave ? wave : (blocks < 1 ? 1 : blocks);
+}
+
+// stage_kernel, 8 lanes per (batch, token, head) row.
+int launch_stage(const StageParams& sp, cudaStream_t stream) {
+  const long long lanes = static_cast<long long>(sp.B) * sp.L * sp.H * 8;
+  if (lanes <= 0) return HYB_OK;
+  if (lanes >= (1LL << 31)) return fail(HYB_ERR_UNSUPPORTED, "stage: %lld rows exceed the 32-bit row index", lanes / 8);
+  static int per_sm = 0;
+  stage_kernel<<<static_cast<unsigned>(wave_blocks(stage_kernel, &per_sm, lanes)), 256, 0, stream>>>(sp);
+  HYB_CHECK_LAUNCH();
+  return HYB_OK;
+}
 
 int check_view(const hyb_tensor4& v, const char* name, bool allow_quant) {
   if (v.data == nullptr) return fail(HYB_ERR_INVALID_ARG, "%s: null data", name);
@@ -1605,8 +1710,9 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   const UnitMap um = plan_units(kp, kp.kv_splits, device_sm_count());
   int rc2 = launch_attn2(mq, mk, mv, kp, um, a->v_f16 != 0, stream);
   if (rc2 != HYB_OK || um.max_k <= 1 || kp.sc_o != nullptr) return rc2;  // owners merge scattered rows
-  const long long rows = static_cast<long long>(kp.B) * kp.H * kp.Lq;
-  merge_splits_kernel<<<grid_for(rows * 32, 256), 256, 0, stream>>>(kp, um);
+  if (BH > 65535) return fail(HYB_ERR_UNSUPPORTED, "attention: %d (batch, head) pairs in one split launch", BH);
+  merge_splits_kernel<<<dim3(static_cast<unsigned>((kp.Lq + 7) / 8), static_cast<unsigned>(BH)), 256, 0, stream>>>(
+      kp, um);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
@@ -1671,7 +1777,10 @@ extern "C" int hyb_merge_partials(int32_t count, int32_t B, int32_t H, int32_t D
   p.text_mask = text_mask;
   p.tm_sb = text_mask_sb;
   p.lse_out = lse;
-  merge_partials_kernel<<<grid_for(total * 32, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  if (static_cast<long long>(B) * H > 65535)
+    return fail(HYB_ERR_UNSUPPORTED, "merge partials: %lld (batch, head) pairs", static_cast<long long>(B) * H);
+  merge_partials_kernel<<<dim3(static_cast<unsigned>((rows + txt_rows + 7) / 8), static_cast<unsigned>(B * H)), 256, 0,
+                          static_cast<cudaStream_t>(stream)>>>(p);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
@@ -1697,10 +1806,7 @@ extern "C" int hyb_stage_head_major(int32_t B, int32_t L, int32_t H, int32_t D, 
   if (src_v != nullptr) sp.seg[1][0] = seg_of(*src_v, L, 0);
   sp.out[0] = dst_k;
   sp.out[1] = dst_v;
-  stage_kernel<<<grid_for(static_cast<long long>(B) * H * L * 16, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      sp);
-  HYB_CHECK_LAUNCH();
-  return HYB_OK;
+  return launch_stage(sp, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int hyb_ring_gather_stage(int32_t P, int32_t fmt, int32_t L, int32_t H, int32_t D, int32_t Lmax,
@@ -1736,7 +1842,11 @@ extern "C" int hyb_ring_gather_stage(int32_t P, int32_t fmt, int32_t L, int32_t 
   p.out_k = static_cast<__nv_bfloat16*>(out_k);
   p.out_v = static_cast<__nv_bfloat16*>(out_v);
   if (L == 0) return HYB_OK;
-  gather_stage_kernel<<<grid_for(static_cast<long long>(H) * L * 16, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  const long long lanes = static_cast<long long>(H) * L * 8;
+  if (lanes >= (1LL << 31)) return fail(HYB_ERR_UNSUPPORTED, "gather stage: %lld rows exceed the 32-bit row index", lanes / 8);
+  static int per_sm = 0;
+  gather_stage_kernel<<<static_cast<unsigned>(wave_blocks(gather_stage_kernel, &per_sm, lanes)), 256, 0,
+                        static_cast<cudaStream_t>(stream)>>>(p);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
@@ -1850,7 +1960,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
 
   // K / V composition (history decoded in the same pass)
   if (w.Lk > 0) {
-    StageParams sp;
+    StageParams sp{};
     sp.B = a->B;
     sp.H = a->H;
     sp.L = w.Lk;
@@ -1869,11 +1979,10 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     sp.out[1] = v_all;
     sp.out_f16[0] = 0;
     sp.out_f16[1] = 1;   // V (and so P) in fp16 for P.V
-    stage_kernel<<<grid_for(static_cast<long long>(a->B) * a->H * w.Lk * 16, 256), 256, 0, stream>>>(sp);
-    HYB_CHECK_LAUNCH();
+    if ((rc = launch_stage(sp, stream)) != HYB_OK) return rc;
   }
   if (w.Lq > 0) {
-    StageParams sp;
+    StageParams sp{};
     sp.B = a->B;
     sp.H = a->H;
     sp.L = w.Lq;
@@ -1885,8 +1994,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
     sp.out[1] = nullptr;
     sp.out_f16[0] = 0;
     sp.out_f16[1] = 0;
-    stage_kernel<<<grid_for(static_cast<long long>(a->B) * a->H * w.Lq * 16, 256), 256, 0, stream>>>(sp);
-    HYB_CHECK_LAUNCH();
+    if ((rc = launch_stage(sp, stream)) != HYB_OK) return rc;
   } else {
     return HYB_OK;
   }
