@@ -61,6 +61,8 @@ def parse():
                     help="print the dense FP8 GEMM peak of this GPU (burst and 4 s sustained) and exit")
     ap.add_argument("--no-config3", action="store_true",
                     help="config 2: skip the config-3 ring measurement reported in the same line")
+    ap.add_argument("--no-decoded-window", action="store_true",
+                    help="rollout: decode the whole window on every call instead of once per appended frame")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager calls instead of replaying one captured CUDA graph of the call")
     ap.add_argument("--sp-scheme", default="auto", choices=["auto", "ulysses", "kv"],
@@ -847,7 +849,9 @@ def run_rollout(args):
     Ls = T // world
     Tw = Ls if scheme == "kv" else T      # tokens of each frame in this rank's window
     gen = make_generator(1238 + rank, device=device)
-    win = SinkWindowKVCache(1, Hl, Tw, SINK, KEEP, device=device)
+    # each appended frame is decoded once into the window's mirror (--no-decoded-window: every
+    # call decodes the whole window, as the reference's dequantize_kv does)
+    win = SinkWindowKVCache(1, Hl, Tw, SINK, KEEP, device=device, decoded=not args.no_decoded_window)
     with torch.no_grad():
         for _ in range(PREFILL):   # rollout history (untimed): 64 frames through the ring
             win.append(seeded_kv((1, Tw, Hl, D), gen, device=device), seeded_kv((1, Tw, Hl, D), gen, device=device),
@@ -930,12 +934,15 @@ def run_rollout(args):
         "config": {"workload": "config 5: long rollout, 1-frame chunks, sink 1 + window 32 of a 64-frame history",
                    "heads": H_TOTAL, "head_dim": D, "tokens_per_frame": T, "history_tokens": Lh,
                    "visible_keys": Lh + T, "sink_frames": SINK, "window_frames": KEEP, "prefill_frames": PREFILL,
-                   "append": "quantise-on-write of each frame into its ring slot (no memmove)",
+                   "append": "quantise-on-write of each frame into its ring slot (no memmove)"
+                             + ("" if args.no_decoded_window else
+                                ", then its one-time decode into the window's bf16/fp16 mirror (history read in slot order)"),
                    "parallelism": (f"ulysses_sp{world}" if scheme == "ulysses" else f"kv_stationary_sp{world}")
                    if world > 1 else "single",
                    "l2": "inputs larger than L2 (155 MB FP8 window + 10 MB bf16 frame per step)",
                    "tflop_per_step": round(flops_total / 1e12, 4)},
-        "gpu_launches": args.steps * (8 if scheme == "kv" else 6 + (2 if world > 1 else 0)),
+        "gpu_launches": args.steps * ((8 if scheme == "kv" else 6 + (2 if world > 1 else 0))
+                                      + (0 if args.no_decoded_window else 1)),   # + the frame's decode
         "e2e": {"value": round(flops_total / (ems * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "ms_per_step": round(ems, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": None,

@@ -16,7 +16,7 @@ import torch
 PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libhyb200.so"
 
-HYB_ABI_VERSION = 4
+HYB_ABI_VERSION = 5
 
 HYB_OK = 0
 HYB_ERR_INVALID_ARG = -1
@@ -74,6 +74,7 @@ class CachedAttnArgs(ctypes.Structure):
         ("out_txt", c_ptr), ("ot_sb", c_i64), ("ot_st", c_i64), ("ot_sh", c_i64),
         ("lse", c_ptr), ("workspace", c_ptr), ("workspace_bytes", c_i64),
         ("dev_status", c_ptr), ("img_k_len", c_i32), ("scatter", c_ptr),
+        ("staged_k", c_ptr), ("staged_v", c_ptr), ("staged_pitch", c_i64),
     ]
 
 
@@ -147,6 +148,9 @@ SIGNATURES = {
     "hyb_check_finite": (c_i32, [ctypes.POINTER(Tensor4), c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "hyb_kv_dequant": (c_i32, [ctypes.POINTER(Tensor4), c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "hyb_cached_attention_workspace_bytes": (c_i64, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "hyb_cached_attention_workspace_bytes_ex": (c_i64, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "hyb_decode_rows": (c_i32, [c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(Tensor4), ctypes.POINTER(Tensor4),
+                                c_ptr, c_ptr, c_i64, c_i64, c_ptr]),
     "hyb_cached_attention_workspace_layout": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                                                        ctypes.POINTER(WorkspaceLayout)]),
     "hyb_cached_attention": (c_i32, [ctypes.POINTER(CachedAttnArgs), c_ptr]),

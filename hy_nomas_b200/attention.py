@@ -150,7 +150,22 @@ def cached_attention_local(
         (tuple(out_img.stride()[:3]) if out_img is not None else (0, 0, 0))
     if len(oi) == 3:
         oi = oi + (0, 0)
-    ws_bytes = lib.hyb_cached_attention_workspace_bytes(B, H, D, cache_valid_len, Li, Lt, int(attend_txt))
+    # a cache that keeps its history decoded (window.SinkWindowKVCache(decoded=True)): rows
+    # [0, cache_valid_len) of its head-major buffers, in slot order; this call stages its own
+    # keys after them
+    staged = kv_cache.get("staged")
+    if staged is not None:
+        sk, sv, pitch = staged
+        if tuple(sk.shape) != (B, H, pitch, D) or tuple(sv.shape) != (B, H, pitch, D) or sk.dtype != torch.bfloat16 \
+                or sv.dtype != torch.float16 or not (sk.is_contiguous() and sv.is_contiguous()):
+            raise ValueError(f"a decoded history mirror must be contiguous bf16 K / fp16 V [{B}, {H}, pitch, {D}] "
+                             "(one batch row per query batch row)")
+        _lib.require_same_device(dev, "decoded history mirror", sk, sv)
+        if cache_valid_len + Lik + (Lt if attend_txt else 0) > pitch:
+            raise ValueError(f"the decoded history mirror has {pitch} rows; this call needs "
+                             f"{cache_valid_len + Lik + (Lt if attend_txt else 0)}")
+    ws_bytes = lib.hyb_cached_attention_workspace_bytes_ex(B, H, D, cache_valid_len, Li, Lt, int(attend_txt),
+                                                           int(staged is not None))
     if ws_bytes < 0:
         raise RuntimeError("hyb200: unsupported sizes for cached attention (head_dim must be 128)")
     ws_obj = workspace if isinstance(workspace, Workspace) else None
@@ -214,9 +229,13 @@ def cached_attention_local(
     args.workspace = workspace.data_ptr()
     args.workspace_bytes = workspace.numel()
     args.dev_status = _lib.device_status(dev).data_ptr()
+    if staged is not None:
+        args.staged_k, args.staged_v, args.staged_pitch = staged[0].data_ptr(), staged[1].data_ptr(), int(staged[2])
     with torch.cuda.device(dev):
         _lib.check(lib.hyb_cached_attention(args, _lib.stream_ptr(dev)), "cached attention")
-    if ws_obj is not None and scatter is None:
+    if ws_obj is not None and staged is not None:
+        ws_obj.attn_args = None   # the kernel-only relaunch covers the staging-workspace layout only
+    if ws_obj is not None and scatter is None and staged is None:
         with torch.cuda.device(dev):
             lay = workspace_layout(B, H, cache_valid_len, Li, Lt, attend_txt, D)
         base = workspace.data_ptr()

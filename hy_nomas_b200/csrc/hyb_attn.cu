@@ -937,6 +937,8 @@ struct StageSeg {
 
 struct StageParams {
   int B, H, L, nout, nseg;
+  long long out_pitch;  // rows between consecutive (batch, head) slabs of out (0: L)
+  int out_t0;           // row t goes to row out_t0 + t of its slab
   StageSeg seg[2][3];
   void* out[2];       // [B, H, L, 128]
   int out_f16[2];     // 1: output in fp16 (the P.V operand), 0: bf16.  Either way a value is the
@@ -1048,7 +1050,7 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
       ts -= p.seg[0][si].len;
       ++si;
     }
-    const long long out_off = ((static_cast<long long>(b) * p.H + h) * p.L + t) * kHD + lane8 * 16;
+    const long long out_off = ((static_cast<long long>(b) * p.H + h) * p.out_pitch + p.out_t0 + t) * kHD + lane8 * 16;
 #pragma unroll
     for (int o = 0; o < 2; ++o) {
       if (o < p.nout) {
@@ -1254,11 +1256,13 @@ EncodeTiledFn encode_fn() {
 }
 
 // [BH, L, 128] 16-bit head-major tensor (bf16 or f16), 64 x 128 boxes with 128-byte swizzle.
-int make_map(CUtensorMap* map, const void* base, int BH, int L, bool f16 = false) {
+// [BH, L, 128] rows of 16-bit values, `pitch` rows (>= L; 0: L) between consecutive bh slabs.
+int make_map(CUtensorMap* map, const void* base, int BH, int L, bool f16 = false, long long pitch = 0) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return fail(HYB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (pitch <= 0) pitch = L;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(L), static_cast<cuuint64_t>(BH)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHD) * 2, static_cast<cuuint64_t>(L) * kHD * 2};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHD) * 2, static_cast<cuuint64_t>(pitch) * kHD * 2};
   cuuint32_t box[3] = {64, 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
@@ -1299,9 +1303,10 @@ long long wave_blocks(K kernel, int* per_sm, long long lanes) {
 }
 
 // stage_kernel, 8 lanes per (batch, token, head) row.
-int launch_stage(const StageParams& sp, cudaStream_t stream) {
+int launch_stage(StageParams sp, cudaStream_t stream) {
   const long long lanes = static_cast<long long>(sp.B) * sp.L * sp.H * 8;
   if (lanes <= 0) return HYB_OK;
+  if (sp.out_pitch == 0) sp.out_pitch = sp.L;
   if (lanes >= (1LL << 31)) return fail(HYB_ERR_UNSUPPORTED, "stage: %lld rows exceed the 32-bit row index", lanes / 8);
   static int per_sm = 0;
   stage_kernel<<<static_cast<unsigned>(wave_blocks(stage_kernel, &per_sm, lanes)), 256, 0, stream>>>(sp);
@@ -1538,7 +1543,8 @@ UnitMap plan_units(const AttnKParams& kp, int cap, int sms) {
   return um;
 }
 
-WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lik, int Lt, int attend_txt, int sms) {
+WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lik, int Lt, int attend_txt, int sms,
+                           bool staged = false) {
   WorkspaceLayout w;
   w.Lq = Li + Lt;
   w.Lk = Lh + Lik + (attend_txt ? Lt : 0);
@@ -1547,10 +1553,12 @@ WorkspaceLayout layout_for(int B, int H, int Lh, int Li, int Lik, int Lt, int at
   long long off = 0;
   w.q = off;
   off = align256(off + static_cast<long long>(B) * H * w.Lq * kHD * 2);
+  // (a call with pre-decoded history stages its keys into the caller's buffers)
+  const long long kv_rows = staged ? 0 : static_cast<long long>(B) * H * w.Lk;
   w.k = off;
-  off = align256(off + static_cast<long long>(B) * H * w.Lk * kHD * 2);
+  off = align256(off + kv_rows * kHD * 2);
   w.v = off;
-  off = align256(off + static_cast<long long>(B) * H * w.Lk * kHD * 2);
+  off = align256(off + kv_rows * kHD * 2);
   w.kbits = off;
   off = align256(off + static_cast<long long>(B) * w.kwords * 4);
   w.qbits = off;
@@ -1697,7 +1705,7 @@ int fill_params(const hyb_attn_args* a, AttnKParams& kp) {
   return HYB_OK;
 }
 
-int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
+int attn_core(const hyb_attn_args* a, cudaStream_t stream, long long kv_pitch = 0) {
   AttnKParams kp;
   int rc = fill_params(a, kp);
   if (rc != HYB_OK || a->Lq == 0) return rc;
@@ -1705,8 +1713,8 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream) {
   const int BH = a->B * a->H;
   CUtensorMap mq, mk, mv;
   if ((rc = make_map(&mq, a->q, BH, a->Lq)) != HYB_OK) return rc;
-  if ((rc = make_map(&mk, a->k, BH, a->Lk > 0 ? a->Lk : 1)) != HYB_OK) return rc;
-  if ((rc = make_map(&mv, a->v, BH, a->Lk > 0 ? a->Lk : 1, a->v_f16 != 0)) != HYB_OK) return rc;
+  if ((rc = make_map(&mk, a->k, BH, a->Lk > 0 ? a->Lk : 1, false, kv_pitch)) != HYB_OK) return rc;
+  if ((rc = make_map(&mv, a->v, BH, a->Lk > 0 ? a->Lk : 1, a->v_f16 != 0, kv_pitch)) != HYB_OK) return rc;
   const UnitMap um = plan_units(kp, kp.kv_splits, device_sm_count());
   int rc2 = launch_attn2(mq, mk, mv, kp, um, a->v_f16 != 0, stream);
   if (rc2 != HYB_OK || um.max_k <= 1 || kp.sc_o != nullptr) return rc2;  // owners merge scattered rows
@@ -1867,6 +1875,44 @@ extern "C" int64_t hyb_cached_attention_workspace_bytes(int32_t B, int32_t H, in
   return layout_for(B, H, valid_len, img_len, img_len, txt_len, attend_txt, device_sm_count()).total;
 }
 
+extern "C" int64_t hyb_cached_attention_workspace_bytes_ex(int32_t B, int32_t H, int32_t D, int32_t valid_len,
+                                                           int32_t img_len, int32_t txt_len, int32_t attend_txt,
+                                                           int32_t staged) {
+  if (D != kHD || B < 0 || H < 0 || valid_len < 0 || img_len < 0 || txt_len < 0) return -1;
+  return layout_for(B, H, valid_len, img_len, img_len, txt_len, attend_txt, device_sm_count(), staged != 0).total;
+}
+
+extern "C" int hyb_decode_rows(int32_t B, int32_t n, int32_t H, int32_t D, const hyb_tensor4* src_k,
+                               const hyb_tensor4* src_v, void* dst_k, void* dst_v, int64_t pitch, int64_t row0,
+                               void* stream) {
+  if (D != kHD) return fail(HYB_ERR_UNSUPPORTED, "decode rows: head_dim %d != 128", D);
+  if (B < 0 || n < 0 || H <= 0 || src_k == nullptr || src_v == nullptr || dst_k == nullptr || dst_v == nullptr ||
+      !al16(dst_k) || !al16(dst_v) || row0 < 0 || row0 + n > pitch || pitch > INT_MAX)
+    return fail(HYB_ERR_INVALID_ARG, "decode rows: bad arguments (rows [%lld, %lld) of pitch %lld)", (long long)row0,
+                (long long)(row0 + n), (long long)pitch);
+  int rc;
+  if ((rc = check_view(*src_k, "decode rows K", true)) != HYB_OK) return rc;
+  if ((rc = check_view(*src_v, "decode rows V", true)) != HYB_OK) return rc;
+  if ((src_k->fmt != HYB_FMT_E4M3 && src_k->fmt != HYB_FMT_INT8) || src_v->fmt != src_k->fmt)
+    return fail(HYB_ERR_UNSUPPORTED, "decode rows: K/V must both be E4M3 or INT8 codes");
+  if (B == 0 || n == 0) return HYB_OK;
+  StageParams sp{};
+  sp.B = B;
+  sp.H = H;
+  sp.L = n;
+  sp.out_pitch = pitch;
+  sp.out_t0 = static_cast<int>(row0);
+  sp.nout = 2;
+  sp.nseg = 1;
+  sp.seg[0][0] = seg_of(*src_k, n, 0);
+  sp.seg[1][0] = seg_of(*src_v, n, 0);
+  sp.out[0] = dst_k;
+  sp.out[1] = dst_v;
+  sp.out_f16[0] = 0;
+  sp.out_f16[1] = 1;
+  return launch_stage(sp, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int hyb_cached_attention_workspace_layout(int32_t B, int32_t H, int32_t D, int32_t valid_len,
                                                      int32_t img_len, int32_t txt_len, int32_t attend_txt,
                                                      hyb_workspace_layout* out) {
@@ -1906,12 +1952,17 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const int Lh = a->valid_len, Li = a->img_len, Lt = a->txt_len;
   const int Lik = a->img_k_len > 0 ? a->img_k_len : Li;
-  const WorkspaceLayout w = layout_for(a->B, a->H, Lh, Li, Lik, Lt, a->attend_txt, device_sm_count());
+  const bool staged = a->staged_k != nullptr;
+  const WorkspaceLayout w = layout_for(a->B, a->H, Lh, Li, Lik, Lt, a->attend_txt, device_sm_count(), staged);
   if (a->workspace == nullptr || a->workspace_bytes < w.total || !al16(a->workspace))
     return fail(HYB_ERR_WORKSPACE, "cached attention: workspace %lld bytes < %lld needed",
                 (long long)a->workspace_bytes, (long long)w.total);
+  if (staged && (a->staged_v == nullptr || !al16(a->staged_k) || !al16(a->staged_v) || a->staged_pitch < w.Lk))
+    return fail(HYB_ERR_INVALID_ARG,
+                "cached attention: staged history needs K and V buffers, 16-byte aligned, with a pitch of at "
+                "least %d rows (got %lld)", w.Lk, (long long)a->staged_pitch);
   int rc;
-  if (Lh > 0) {
+  if (Lh > 0 && !staged) {
     if ((rc = check_view(a->hist_k, "hist_k", true)) != HYB_OK) return rc;
     if ((rc = check_view(a->hist_v, "hist_v", true)) != HYB_OK) return rc;
     if (a->hist_k.fmt != a->hist_v.fmt) return fail(HYB_ERR_INVALID_ARG, "KV cache K/V dtype mismatch");
@@ -1947,7 +1998,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   mp.Lq = w.Lq;
   mp.qwords = w.qwords;
   mp.attend_txt = a->attend_txt;
-  mp.hist_rows = a->hist_rows;
+  mp.hist_rows = staged ? nullptr : a->hist_rows;
   mp.cache_mask = a->cache_mask;
   mp.cm_sb = a->cache_mask_sb;
   mp.cm_bcast = a->cache_batch == 1 ? 1 : 0;
@@ -1958,16 +2009,19 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   mask_kernel<<<grid_for(static_cast<long long>(a->B) * (w.kwords + w.qwords), 256), 256, 0, stream>>>(mp);
   HYB_CHECK_LAUNCH();
 
-  // K / V composition (history decoded in the same pass)
-  if (w.Lk > 0) {
+  // K / V composition (history decoded in the same pass); with a staged history only the
+  // current keys, into rows [Lh, Lk) of the caller's buffers
+  if (w.Lk > (staged ? Lh : 0)) {
     StageParams sp{};
     sp.B = a->B;
     sp.H = a->H;
-    sp.L = w.Lk;
+    sp.L = staged ? w.Lk - Lh : w.Lk;
+    sp.out_pitch = staged ? a->staged_pitch : 0;
+    sp.out_t0 = staged ? Lh : 0;
     sp.nout = 2;
     sp.nseg = 0;
     const hyb_tensor4* srcs[2][3] = {{&a->hist_k, &a->img_k, &a->txt_k}, {&a->hist_v, &a->img_v, &a->txt_v}};
-    const int lens[3] = {Lh, Lik, a->attend_txt ? Lt : 0};
+    const int lens[3] = {staged ? 0 : Lh, Lik, a->attend_txt ? Lt : 0};
     for (int si = 0; si < 3; ++si) {
       if (lens[si] == 0) continue;
       for (int o = 0; o < 2; ++o)
@@ -1975,8 +2029,8 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
                                     si == 0 ? a->hist_rows : nullptr);
       ++sp.nseg;
     }
-    sp.out[0] = k_all;
-    sp.out[1] = v_all;
+    sp.out[0] = staged ? a->staged_k : k_all;
+    sp.out[1] = staged ? a->staged_v : v_all;
     sp.out_f16[0] = 0;
     sp.out_f16[1] = 1;   // V (and so P) in fp16 for P.V
     if ((rc = launch_stage(sp, stream)) != HYB_OK) return rc;
@@ -2014,8 +2068,8 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   at.q_pos0 = a->q_pos0;
   at.k_pos0 = a->k_pos0;
   at.q = q_all;
-  at.k = k_all;
-  at.v = v_all;
+  at.k = staged ? a->staged_k : k_all;
+  at.v = staged ? a->staged_v : v_all;
   at.kbits = kbits;
   at.kwords = w.kwords;
   at.qbits = qbits;
@@ -2037,7 +2091,7 @@ extern "C" int hyb_cached_attention(const hyb_cached_attn_args* a, void* stream_
   at.part_o = reinterpret_cast<float*>(ws + w.part_o);
   at.part_lse = reinterpret_cast<float*>(ws + w.part_lse);
   at.scatter = a->scatter;
-  return attn_core(&at, stream);
+  return attn_core(&at, stream, staged ? a->staged_pitch : 0);
 }
 
 // =========================================================================================
@@ -2100,8 +2154,8 @@ extern "C" int hyb_cached_attention_noalloc(const hyb_cached_attn_args* a, void*
   if (a->D != kHD) return fail(HYB_ERR_UNSUPPORTED, "cached attention (no-alloc): head_dim %d != 128", a->D);
   if (a->B <= 0 || a->H <= 0 || a->valid_len < 0 || a->img_len < 0 || a->txt_len < 0 || a->group_tokens < 0)
     return fail(HYB_ERR_INVALID_ARG, "cached attention (no-alloc): negative sizes");
-  const int64_t need = hyb_cached_attention_workspace_bytes(a->B, a->H, a->D, a->valid_len, a->img_len,
-                                                            a->txt_len, a->attend_txt);
+  const int64_t need = hyb_cached_attention_workspace_bytes_ex(a->B, a->H, a->D, a->valid_len, a->img_len,
+                                                               a->txt_len, a->attend_txt, a->staged_k != nullptr);
   if (need < 0) return fail(HYB_ERR_INVALID_ARG, "cached attention (no-alloc): unsupported sizes");
   if (need > kNoAllocScratchBytes)
     return fail(HYB_ERR_WORKSPACE,

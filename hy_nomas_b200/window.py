@@ -15,6 +15,16 @@ row map (``history_rows``: composed history position -> cache row) that the stag
 kernel follows; the maps of every ring rotation are built once, on the device.
 The visible frames after each append are the reference's: sink frames, then the last
 ``keep`` frames (oracle/window.py restates the reference slide for the tests).
+
+With ``decoded=True`` (quantised storage) each appended frame is also decoded once into a
+head-major mirror of the slots (bf16 K, fp16 V: the values the attention's staging pass would
+produce from the codes), and the attention reads the history from the mirror in slot order
+instead of decoding the whole window on every call (the reference decodes the whole cache per
+call, nomas_cpt.py:529-531; a 1-frame rollout step then re-decodes 33 unchanged frames).  The
+slot order is not the temporal order, which the attention does not need: it is a sum over the
+set of visible keys.  Memory: the mirror holds 4 bytes per cached value next to the cache's
+~2 (e4m3 K and V + scales), plus a tail of ``tail_rows`` rows where each call stages its own
+keys.
 """
 from __future__ import annotations
 
@@ -28,7 +38,8 @@ class SinkWindowKVCache:
     sliding window of the last ``keep_frames`` frames, ``tokens_per_frame`` tokens each."""
 
     def __init__(self, batch: int, heads: int, tokens_per_frame: int, sink_frames: int, keep_frames: int, *,
-                 head_dim: int = 128, storage_format: str = "fp8_e4m3", device=None):
+                 head_dim: int = 128, storage_format: str = "fp8_e4m3", device=None, decoded: bool = False,
+                 tail_rows: int | None = None):
         if tokens_per_frame <= 0 or sink_frames < 0 or keep_frames <= 0:
             raise ValueError("window cache needs tokens_per_frame > 0, sink_frames >= 0, keep_frames > 0")
         self.B, self.H, self.D = batch, heads, head_dim
@@ -47,6 +58,14 @@ class SinkWindowKVCache:
             raise ValueError(f"unknown storage format {storage_format!r}")
         self.storage_format = storage_format
         self.frames = 0            # frames appended so far (temporal count)
+        self.mirror = None
+        if decoded:
+            if storage_format == "bf16":
+                raise ValueError("decoded=True mirrors a quantised cache (fp8_e4m3 or int8)")
+            tail = tokens_per_frame + 256 if tail_rows is None else int(tail_rows)
+            self.pitch = cap + tail  # rows per (batch, head): the slots, then the call's own keys
+            self.mirror = (torch.empty(batch, heads, self.pitch, head_dim, dtype=torch.bfloat16, device=self.device),
+                           torch.empty(batch, heads, self.pitch, head_dim, dtype=torch.float16, device=self.device))
         # Row maps, built on the device without a host sync: before the window wraps, frame f
         # sits in slot f (a prefix of the identity); once it wraps, rotation r = (frames - sink)
         # % keep puts the oldest visible window frame in slot sink + r.
@@ -89,6 +108,8 @@ class SinkWindowKVCache:
         d = dict(self.cache)
         d["history_rows"] = self.history_rows()
         d["window"] = self          # update_cache=True appends the chunk's frames here
+        if self.mirror is not None:
+            d["staged"] = (self.mirror[0], self.mirror[1], self.pitch)   # history rows in slot order
         return d
 
     # ------------------------------------------------------------------ writes
@@ -109,4 +130,19 @@ class SinkWindowKVCache:
                 self.cache["v"][:, slot * self.T:(slot + 1) * self.T] = vs
             else:
                 _kvc.quantize_kv_pair_into(self.cache, ks, vs, slot * self.T, assume_finite=assume_finite)
+                if self.mirror is not None:
+                    self._decode_slot(slot)
             self.frames += 1
+
+    def _decode_slot(self, slot: int) -> None:
+        """Decode the codes of one slot into its rows of the mirror."""
+        from . import _lib
+        lib = _lib.load()
+        code = _lib.HYB_FMT_INT8 if self.storage_format == "int8" else _lib.HYB_FMT_E4M3
+        rows = slice(slot * self.T, (slot + 1) * self.T)
+        src_k = _lib.coded_view(self.cache["k"][:, rows], self.cache["k_scale"][:, rows], code)
+        src_v = _lib.coded_view(self.cache["v"][:, rows], self.cache["v_scale"][:, rows], code)
+        with torch.cuda.device(self.device):
+            _lib.check(lib.hyb_decode_rows(self.B, self.T, self.H, self.D, src_k, src_v, self.mirror[0].data_ptr(),
+                                           self.mirror[1].data_ptr(), self.pitch, slot * self.T,
+                                           _lib.stream_ptr(self.device)), "window decode")

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define HYB_ABI_VERSION 4
+#define HYB_ABI_VERSION 5
 
 /* status codes */
 #define HYB_OK 0
@@ -133,7 +133,35 @@ typedef struct hyb_cached_attn_args {
                               schedule passes all queries of the chunk and its own keys */
   const hyb_part_scatter* scatter;  /* NULL, or: partial rows go to their owners (out_img/out_txt
                                        unused, no merge here) */
+  /* Pre-decoded history (ABI 5), or NULL: the call decodes hist_k / hist_v through hist_rows.
+     When staged_k is set, history key t (t < valid_len) is row t of staged_k / staged_v, bf16 K
+     and fp16 V [B, H, staged_pitch, D] holding the values the call's own decode would produce
+     (a cache that decodes each appended frame once, see hyb_decode_rows); hist_k, hist_v and
+     hist_rows are not read, cache_mask is indexed by t, and the current image and text keys
+     are staged into rows [valid_len, valid_len + img_k_len + txt_len) of the same buffers, so
+     staged_pitch must cover them.  The order of the history rows is free: attention is a sum
+     over the set of visible keys. */
+  void* staged_k;
+  void* staged_v;
+  int64_t staged_pitch;
 } hyb_cached_attn_args;
+
+/* Decode n rows of a quantised K/V pair (E4M3 / INT8 views [B, n, H, D] with their scales)
+ * into head-major rows [row0, row0 + n) of dst_k (bf16) and dst_v (fp16 holding the same bf16
+ * value) [B, H, pitch, D]: value for value the decode hyb_cached_attention applies to history
+ * rows (bf16(code * scale), dequantize_kv of int8_kv_cache.py:182-205).  A cache that decodes
+ * each frame once when it is appended passes these buffers as staged_k / staged_v.  No
+ * reference counterpart: the reference decodes the whole cache on every call
+ * (nomas_cpt.py:529-531). */
+int hyb_decode_rows(int32_t B, int32_t n, int32_t H, int32_t D, const hyb_tensor4* src_k,
+                    const hyb_tensor4* src_v, void* dst_k, void* dst_v, int64_t pitch, int64_t row0,
+                    void* stream);
+
+/* Workspace bytes of hyb_cached_attention; staged != 0 for a call with staged_k set (no
+ * K/V staging area: the caller's buffers hold it). */
+int64_t hyb_cached_attention_workspace_bytes_ex(int32_t B, int32_t H, int32_t D, int32_t valid_len,
+                                                int32_t img_len, int32_t txt_len, int32_t attend_txt,
+                                                int32_t staged);
 
 /* Library identity. */
 int hyb_version(void);

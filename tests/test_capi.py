@@ -47,6 +47,7 @@ int main(void) {
   F(hyb_cached_attn_args, hist_rows) F(hyb_cached_attn_args, cache_mask) F(hyb_cached_attn_args, oi_seg)
   F(hyb_cached_attn_args, out_txt) F(hyb_cached_attn_args, lse) F(hyb_cached_attn_args, workspace_bytes)
   F(hyb_cached_attn_args, dev_status) F(hyb_cached_attn_args, img_k_len) F(hyb_cached_attn_args, scatter)
+  F(hyb_cached_attn_args, staged_k) F(hyb_cached_attn_args, staged_pitch)
   F(hyb_attn_args, q) F(hyb_attn_args, kwords) F(hyb_attn_args, qbits) F(hyb_attn_args, oi_sseg)
   F(hyb_attn_args, lse) F(hyb_attn_args, dev_status) F(hyb_attn_args, kv_splits) F(hyb_attn_args, v_f16) F(hyb_attn_args, part_lse)
   F(hyb_attn_args, img_k_len) F(hyb_attn_args, k_pos1) F(hyb_attn_args, acc_o) F(hyb_attn_args, acc_mode)
@@ -142,6 +143,36 @@ def test_workspace_size_formula():
     Lk, Lq = Lh + Li + Lt, Li + Lt
     assert ws >= B * H * (Lq + 2 * Lk) * 128 * 2
     assert ws < B * H * (Lq + 2 * Lk) * 128 * 2 + 1 << 20
+
+
+def test_staged_history_workspace_and_argument_checks():
+    """A call with a pre-decoded history needs no K/V staging area, and its buffers must be
+    given together, aligned, with a pitch that covers the history and the call's own keys;
+    hyb_decode_rows rejects rows outside the pitch and bf16 sources.  Nothing runs."""
+    lib = _lib.load()
+    B, H, Lh, Li, Lt = 1, 24, 51480, 1560, 1
+    full = lib.hyb_cached_attention_workspace_bytes_ex(B, H, 128, Lh, Li, Lt, 1, 0)
+    staged = lib.hyb_cached_attention_workspace_bytes_ex(B, H, 128, Lh, Li, Lt, 1, 1)
+    assert full == lib.hyb_cached_attention_workspace_bytes(B, H, 128, Lh, Li, Lt, 1)
+    assert full - staged == 2 * B * H * (Lh + Li + Lt) * 128 * 2
+    c = _lib.CachedAttnArgs()
+    c.abi_version = _lib.HYB_ABI_VERSION
+    c.B, c.H, c.D, c.cache_batch, c.valid_len, c.img_len, c.txt_len, c.attend_txt = 1, 2, 128, 1, 256, 64, 0, 1
+    c.workspace, c.workspace_bytes = 256, 1 << 40
+    c.staged_k, c.staged_v, c.staged_pitch = 256, 512, 256 + 63   # one row short of the call's keys
+    assert lib.hyb_cached_attention(ctypes.byref(c), None) == _lib.HYB_ERR_INVALID_ARG
+    assert "pitch" in _lib.last_error()
+    c.staged_pitch, c.staged_v = 320, None
+    assert lib.hyb_cached_attention(ctypes.byref(c), None) == _lib.HYB_ERR_INVALID_ARG
+    codes = _lib.Tensor4()
+    codes.data, codes.fmt, codes.scale = 256, _lib.HYB_FMT_E4M3, 512
+    codes.s_b, codes.s_t, codes.s_h = 128 * 2 * 64, 128 * 2, 128
+    assert lib.hyb_decode_rows(1, 64, 2, 128, ctypes.byref(codes), ctypes.byref(codes), 256, 512, 100, 40,
+                               None) == _lib.HYB_ERR_INVALID_ARG
+    bf = _lib.Tensor4()
+    bf.data, bf.fmt, bf.s_b, bf.s_t, bf.s_h = 256, _lib.HYB_FMT_BF16, 128 * 2 * 64, 128 * 2, 128
+    assert lib.hyb_decode_rows(1, 64, 2, 128, ctypes.byref(bf), ctypes.byref(bf), 256, 512, 128, 0,
+                               None) == _lib.HYB_ERR_UNSUPPORTED
 
 
 def test_no_device_is_reported_not_faked():

@@ -346,17 +346,20 @@ def test_balanced_work_list_matches_oracle(cuda_lib, monkeypatch):
     assert (lse.cpu() - ref_lse).abs().max() < 1e-3
 
 
+@pytest.mark.parametrize("decoded", [False, True])
 @pytest.mark.parametrize("sink,keep,fmt,write_in_call", [(1, 3, "fp8_e4m3", True), (2, 2, "int8", False)])
-def test_window_rollout_matches_oracle(cuda_lib, sink, keep, fmt, write_in_call):
+def test_window_rollout_matches_oracle(cuda_lib, sink, keep, fmt, write_in_call, decoded):
     """Long-rollout loop: every step attends a 1-frame chunk to the sink + sliding-window ring
     through the drop-in call, then appends the frame (quantise-on-write into the recycled
-    slot).  Each step equals the oracle over the reference's slid history."""
+    slot; with ``decoded`` also its one-time decode into the window's mirror, which the
+    attention then reads in slot order).  Each step equals the oracle over the reference's slid
+    history."""
     from hy_nomas_b200.window import SinkWindowKVCache
     from oracle import window as ow
     dev = torch.device("cuda")
     T, H = 96, 2
     gen = make_generator(77 + keep)
-    win = SinkWindowKVCache(1, H, T, sink, keep, storage_format=fmt, device=dev)
+    win = SinkWindowKVCache(1, H, T, sink, keep, storage_format=fmt, device=dev, decoded=decoded)
     all_k, all_v = [], []
     for step in range(sink + keep + 4):
         q, k, v = (seeded_kv((1, T, H, 128), gen) for _ in range(3))

@@ -18,17 +18,19 @@ from parity import check_bf16
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("P,T,sink,keep,Lt,fmt,slices", [
-    (4, 256, 1, 3, 1, "fp8_e4m3", None),   # 64 rows per owner
-    (3, 300, 2, 2, 2, "int8", 2),          # 100 rows per owner: warps straddle owners
-    (2, 512, 1, 4, 1, "fp8_e4m3", 3),
+@pytest.mark.parametrize("P,T,sink,keep,Lt,fmt,slices,decoded", [
+    (4, 256, 1, 3, 1, "fp8_e4m3", None, False),   # 64 rows per owner
+    (3, 300, 2, 2, 2, "int8", 2, False),          # 100 rows per owner: warps straddle owners
+    (2, 512, 1, 4, 1, "fp8_e4m3", 3, False),
+    (4, 256, 1, 3, 1, "fp8_e4m3", None, True),    # windows keeping their history decoded
+    (3, 300, 2, 2, 2, "int8", 2, True),
 ])
-def test_kv_stationary_rollout_matches_oracle(cuda_lib, P, T, sink, keep, Lt, fmt, slices):
+def test_kv_stationary_rollout_matches_oracle(cuda_lib, P, T, sink, keep, Lt, fmt, slices, decoded):
     dev = torch.device("cuda")
     H = 2
     Ls = T // P
     gen = make_generator(4100 + P * 7 + keep)
-    wins = [SinkWindowKVCache(1, H, Ls, sink, keep, storage_format=fmt, device=dev) for _ in range(P)]
+    wins = [SinkWindowKVCache(1, H, Ls, sink, keep, storage_format=fmt, device=dev, decoded=decoded) for _ in range(P)]
     all_k, all_v = [], []
     for step in range(sink + keep + 3):
         q, k, v = (seeded_kv((1, T, H, 128), gen) for _ in range(3))
