@@ -136,21 +136,22 @@ def main():
     Hk, Ltk = 4, 1
     Lsk = 96
     Tk = Lsk * world
-    win = SinkWindowKVCache(1, Hk, Lsk, 1, 2, device=dev)
-    wins = [SinkWindowKVCache(1, Hk, Lsk, 1, 2, device=dev) for _ in range(world)]
     kvs = KVStationaryAttention(None, 1, Lsk, Hk, Ltk, 3 * Lsk, dev)
-    gk = make_generator(515)
     sl2 = slice(rank * Lsk, (rank + 1) * Lsk)
-    for step in range(4):
-        fq, fk, fv = (seeded_kv((1, Tk, Hk, D), gk).to(dev) for _ in range(3))
-        tq2, tk2, tv2 = (seeded_kv((1, Ltk, Hk, D), gk).to(dev) for _ in range(3))
-        with torch.no_grad():
-            o_img, o_txt = kvs(fq[:, sl2], fk[:, sl2], fv[:, sl2], tq2, tk2, tv2, win)
-            e_img, e_txt = kv_stationary_emulated(fq, fk, fv, tq2, tk2, tv2, wins, slices=kvs.slices)
-        if not (torch.equal(o_img, e_img[:, sl2]) and torch.equal(o_txt, e_txt)):
-            print("KV-stationary mismatch on rank", rank, "step", step,
-                  (o_img.float() - e_img[:, sl2].float()).abs().max().item())
-            ok = False
+    for decoded in (False, True):   # windows decoding per call / keeping their history decoded
+        win = SinkWindowKVCache(1, Hk, Lsk, 1, 2, device=dev, decoded=decoded)
+        wins = [SinkWindowKVCache(1, Hk, Lsk, 1, 2, device=dev, decoded=decoded) for _ in range(world)]
+        gk = make_generator(515)
+        for step in range(4):
+            fq, fk, fv = (seeded_kv((1, Tk, Hk, D), gk).to(dev) for _ in range(3))
+            tq2, tk2, tv2 = (seeded_kv((1, Ltk, Hk, D), gk).to(dev) for _ in range(3))
+            with torch.no_grad():
+                o_img, o_txt = kvs(fq[:, sl2], fk[:, sl2], fv[:, sl2], tq2, tk2, tv2, win)
+                e_img, e_txt = kv_stationary_emulated(fq, fk, fv, tq2, tk2, tv2, wins, slices=kvs.slices)
+            if not (torch.equal(o_img, e_img[:, sl2]) and torch.equal(o_txt, e_txt)):
+                print("KV-stationary mismatch on rank", rank, "step", step, "decoded", decoded,
+                      (o_img.float() - e_img[:, sl2].float()).abs().max().item())
+                ok = False
     kvs.close()
     ok_t = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
