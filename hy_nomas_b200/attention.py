@@ -403,6 +403,10 @@ def causal_attention_with_cache_mp(
         raise NotImplementedError("a ring cache without its SinkWindowKVCache cannot be written")
     if update_cache and window is not None and cache_txt and txt_k.shape[1] > 0:
         raise NotImplementedError("window caches hold whole image frames; pass cache_txt=False")
+    if swa_commit and kv_cache.get("staged") is not None:
+        raise NotImplementedError("a decoded mirror is not kept for bounded (SWA) histories: their commit "
+                                  "moves history rows")
+    mirror_rows = 0   # rows written before the attention, decoded into the cache's mirror after it
     if update_cache and window is None and not swa_commit:
         seg_k = [img_k, txt_k] if cache_txt else [img_k]
         seg_v = [img_v, txt_v] if cache_txt else [img_v]
@@ -411,8 +415,11 @@ def causal_attention_with_cache_mp(
         if new_end > cache_shape[1]:
             raise ValueError("KV pair shape, capacity, dtype, or device mismatch")
         if compressed:
+            # with a decoded mirror the attention stages this call's keys into the mirror rows
+            # this write covers, so their decode runs after the attention
+            mirror_rows = write_tokens if kv_cache.get("staged") is not None else 0
             kvc.quantize_kv_segments_into(kv_cache, [t.detach() for t in seg_k], [t.detach() for t in seg_v],
-                                          cache_valid_len, assume_finite=_assume_finite())
+                                          cache_valid_len, assume_finite=_assume_finite(), decode=mirror_rows == 0)
         else:
             off = cache_valid_len
             for tk, tv in zip(seg_k, seg_v):
@@ -465,6 +472,8 @@ def causal_attention_with_cache_mp(
             history_mask=history_mask, text_mask=cur_txt_mask, attend_txt=attend_txt,
             group_tokens=group_tokens, out_img=o_send, out_img_strides=out_img_strides, hist_rows=hist_rows)
     stats["calls"] += 1
+    if mirror_rows:
+        kvc.refresh_decoded(kv_cache, cache_valid_len, mirror_rows)
     if swa_commit:
         # the bounded history is committed after the attention has read the old rows
         write_mask = torch.ones(B, img_len + txt_len, dtype=torch.bool, device=img_q.device)

@@ -182,6 +182,8 @@ def intra_segment_attention(img_q, img_k, img_v, txt_q, txt_k, txt_v, kv_cache, 
     for b in range(B):
         sl = slice(b, b + 1)
         kv_b = _sample_cache(kv_cache, b) if kv_cache is not None and kv_cache["k"].shape[0] == B else kv_cache
+        if kv_b is not None and "staged" in kv_b:   # the text-row passes below reuse the staging workspace
+            kv_b = {name: t for name, t in kv_b.items() if name != "staged"}
         hm_b = history_mask[sl] if history_mask is not None and history_mask.shape[0] == B else history_mask
         tm_b = text_mask[sl] if text_mask is not None else None
         oi_b, ot_b = out_img[sl], out_txt[sl]

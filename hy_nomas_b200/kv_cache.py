@@ -78,17 +78,60 @@ def _make_block(batch, capacity, heads, dim, dtype, device, pin_memory):
 
 
 def make_int8_kv_block(batch: int, capacity: int, heads: int, dim: int, *,
-                       device, pin_memory: bool = False) -> dict:
-    """int8 codes [B, cap, H, D] + fp32 scales [B, cap, H, 1] (int8_kv_cache.py:92-107)."""
-    return _make_block(batch, capacity, heads, dim, torch.int8, device, pin_memory)
+                       device, pin_memory: bool = False, decoded: bool = False, tail_rows: int = 0) -> dict:
+    """int8 codes [B, cap, H, D] + fp32 scales [B, cap, H, 1] (int8_kv_cache.py:92-107);
+    ``decoded``: also keep the rows decoded (attach_decoded_mirror)."""
+    block = _make_block(batch, capacity, heads, dim, torch.int8, device, pin_memory)
+    return attach_decoded_mirror(block, tail_rows) if decoded else block
 
 
 def make_fp8_kv_block(batch: int, capacity: int, heads: int, dim: int, *,
-                      device, pin_memory: bool = False) -> dict:
-    """float8_e4m3fn codes [B, cap, H, D] + fp32 scales [B, cap, H, 1]."""
+                      device, pin_memory: bool = False, decoded: bool = False, tail_rows: int = 0) -> dict:
+    """float8_e4m3fn codes [B, cap, H, D] + fp32 scales [B, cap, H, 1]; ``decoded``: also keep
+    the rows decoded (attach_decoded_mirror)."""
     block = _make_block(batch, capacity, heads, dim, torch.float8_e4m3fn, device, pin_memory)
     block["storage_format"] = FP8_FORMAT
-    return block
+    return attach_decoded_mirror(block, tail_rows) if decoded else block
+
+
+def attach_decoded_mirror(cache: dict, tail_rows: int = 0) -> dict:
+    """Keep a quantised cache decoded as well: ``cache["staged"] = (K, V, pitch)``, head-major
+    bf16 K / fp16 V [B, H, cap + tail_rows, D] holding bf16(code * scale) of every row (the values
+    the attention's staging pass would produce).  Every write through this module decodes the
+    rows it wrote, so a call reads its history from here instead of decoding the whole cache
+    (the reference's dequantize_kv per call, nomas_cpt.py:529-531, int8_kv_cache.py:182-205).
+    A call stages its own keys into the rows after its history, so the capacity (or
+    ``tail_rows``) must cover history + current keys.  Rows written to the codes by other means
+    need refresh_decoded.  Returns the cache."""
+    _fmt_code(cache)   # quantised storage only
+    B, cap, H, D = cache["k"].shape
+    dev = cache["k"].device
+    pitch = cap + int(tail_rows)
+    cache["staged"] = (torch.empty(B, H, pitch, D, dtype=torch.bfloat16, device=dev),
+                       torch.empty(B, H, pitch, D, dtype=torch.float16, device=dev), pitch)
+    refresh_decoded(cache, 0, cap)
+    return cache
+
+
+def refresh_decoded(cache: dict, start: int, n: int) -> None:
+    """Decode rows [start, start + n) of the codes into the cache's decoded mirror (no-op
+    without one)."""
+    staged = cache.get("staged")
+    if staged is None or n <= 0:
+        return
+    lib = _lib.load()
+    fmt = _fmt_code(cache)
+    k, v, ks, vs = cache["k"], cache["v"], cache["k_scale"], cache["v_scale"]
+    if start < 0 or start + n > k.shape[1]:
+        raise ValueError("decoded rows outside the cache")
+    _lib.require_device(k)
+    rows = slice(start, start + n)
+    src_k = _lib.coded_view(k[:, rows], ks[:, rows], fmt)
+    src_v = _lib.coded_view(v[:, rows], vs[:, rows], fmt)
+    B, _, H, D = k.shape
+    with torch.cuda.device(k.device):
+        _lib.check(lib.hyb_decode_rows(B, n, H, D, src_k, src_v, staged[0].data_ptr(), staged[1].data_ptr(),
+                                       staged[2], start, _lib.stream_ptr(k.device)), "KV decode into the mirror")
 
 
 def _validate(cache: dict, key: str) -> None:
@@ -166,11 +209,13 @@ def quantize_kv_into(cache: dict, key: str, values: torch.Tensor, start: int, *,
     other = {"k": cache[key], "v": cache[key], "k_scale": cache[f"{key}_scale"],
              "v_scale": cache[f"{key}_scale"]}
     _append_pair(other, values, values, start)
+    refresh_decoded(cache, start, values.shape[1])
 
 
 def quantize_kv_pair_into(cache: dict, k: torch.Tensor, v: torch.Tensor, start: int, *,
-                          assume_finite: bool = False) -> None:
-    """Validate K and V before writing either persistent payload or scale."""
+                          assume_finite: bool = False, decode: bool = True) -> None:
+    """Validate K and V before writing either persistent payload or scale; with a decoded
+    mirror (and ``decode``) the written rows are decoded into it too."""
     if k.shape != v.shape or k.dtype != v.dtype or k.device != v.device:
         raise ValueError("K/V shapes, dtypes, and devices must match")
     for key, values in (("k", k), ("v", v)):
@@ -188,12 +233,15 @@ def quantize_kv_pair_into(cache: dict, k: torch.Tensor, v: torch.Tensor, start: 
     if not assume_finite and _any_nonfinite(k, v):
         raise ValueError("Cannot quantize non-finite KV values")
     _append_pair(cache, k, v, start)
+    if decode:
+        refresh_decoded(cache, start, k.shape[1])
 
 
 def quantize_kv_segments_into(cache: dict, segments_k, segments_v, start: int, *,
-                              assume_finite: bool = False) -> None:
+                              assume_finite: bool = False, decode: bool = True) -> None:
     """Append [seg_0 | seg_1] (e.g. image then text tokens) at ``start`` in one pass, with
-    the validation of quantize_kv_pair_into; no concatenated copy is made."""
+    the validation of quantize_kv_pair_into; no concatenated copy is made.  ``decode``: as in
+    quantize_kv_pair_into (a caller that stages keys into the mirror's rows first decodes later)."""
     segments_k = [s for s in segments_k if s.shape[1] > 0]
     segments_v = [s for s in segments_v if s.shape[1] > 0]
     if not segments_k:
@@ -219,6 +267,8 @@ def quantize_kv_segments_into(cache: dict, segments_k, segments_v, start: int, *
         _append_pair(cache, segments_k[0], segments_v[0], start)
     else:
         _append_pair(cache, segments_k[0], segments_v[0], start, segments_k[1], segments_v[1])
+    if decode:
+        refresh_decoded(cache, start, total)
 
 
 def dequantize_kv(cache: dict, key: str, valid_len: int) -> torch.Tensor:
