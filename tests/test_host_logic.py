@@ -357,3 +357,20 @@ def test_kv_stationary_slice_choice():
     assert 2 <= s <= 8
     assert choose_slices(1, 24, 1561, 300, 148) == 1
     assert choose_slices(1, 2, 256, 128 * 64, 148) >= 8
+
+
+def test_decoded_mirrors_are_for_quantised_caches_only():
+    """A decoded mirror holds the decode of codes: a bf16 cache or window has nothing to decode,
+    and asking for one is an error before any allocation or kernel."""
+    from hy_nomas_b200 import kv_cache as kvc
+    from hy_nomas_b200.window import SinkWindowKVCache
+    plain = {"k": torch.zeros(1, 8, 2, 128, dtype=torch.bfloat16), "v": torch.zeros(1, 8, 2, 128, dtype=torch.bfloat16)}
+    with pytest.raises(TypeError):
+        kvc.attach_decoded_mirror(plain)
+    assert "staged" not in plain
+    with pytest.raises(ValueError, match="quantised"):
+        SinkWindowKVCache(1, 2, 16, 1, 2, storage_format="bf16", device="cpu", decoded=True)
+    win = SinkWindowKVCache(1, 2, 16, 1, 2, storage_format="fp8_e4m3", device="cpu", decoded=True, tail_rows=8)
+    mk, mv, pitch = win.view()["staged"]
+    assert pitch == 3 * 16 + 8 and tuple(mk.shape) == (1, 2, pitch, 128)
+    assert mk.dtype == torch.bfloat16 and mv.dtype == torch.float16
