@@ -116,6 +116,11 @@ def cached_attention_local(
     with ``scatter`` (an ``_lib.PartScatter``): a rank of a KV-stationary schedule attends every
     query of the chunk to the keys it holds, and the partial rows go to their owner ranks'
     buffers (no outputs here; returns ``(None, None)``).
+
+    A cache that keeps its rows decoded (``kv_cache["staged"]``, see
+    ``kv_cache.attach_decoded_mirror`` and ``window.SinkWindowKVCache(decoded=True)``) is read
+    from its mirror: rows [0, cache_valid_len) in the mirror's order (``hist_rows`` is then not
+    used), and this call's own keys are staged into the mirror rows after them.
     """
     lib = _lib.load()
     B, Li, H, D = img_q.shape
