@@ -754,30 +754,41 @@ __global__ void __launch_bounds__(kThreads2, 1)
 // text queries), plus the final LSE when requested.  One warp per row, 4 dims per lane; a warp
 // loads a row's partials (up to four slices, each LSE with its row) before any arithmetic, so
 // a row costs one round trip to memory, not two (config 2: 86 -> 67.5 us per launch).
-constexpr int kMergeBatch = 4;  // partial rows loaded together by merge_splits_kernel
+constexpr int kMergeBatch = 4;  // partial rows loaded together by the merge kernels
+// A row's 128 columns are merged by 16 lanes, 8 columns (two float4) each, so a warp merges
+// two rows and a lane keeps twice the bytes in flight that 32 lanes of 4 columns would (the
+// merges are bound by loads in flight, not by instructions).
+constexpr int kMergeLanes = 16;
+constexpr int kMergeCols = kHD / kMergeLanes;     // 8
+constexpr int kMergeVecs = kMergeCols / 4;        // float4 per lane and slice
+constexpr int kMergeRowsPerBlock = 256 / kMergeLanes;  // 16 rows per 256-thread block
 
 struct MergeRow {
   float m = -INFINITY;  // running maximum of the slice LSEs
   float wsum = 0.f;     // sum of exp(lse - m)
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float acc[kMergeCols] = {};
 };
 
+// Slices [s0, s0 + kMergeBatch) of row r: each LSE loaded together with its row's columns
+// (one round trip per batch).  l = lane within the row's 16.
 __device__ __forceinline__ void merge_load(const float* part_o, const float* part_lse, long long slice, long long r,
-                                           int s0, int ns, int lane, float (&lv)[kMergeBatch],
-                                           float4 (&ov)[kMergeBatch]) {
+                                           int s0, int ns, int l, float (&lv)[kMergeBatch],
+                                           float4 (&ov)[kMergeBatch][kMergeVecs]) {
 #pragma unroll
   for (int u = 0; u < kMergeBatch; ++u) {
     if (s0 + u < ns) {
       lv[u] = __ldg(part_lse + (s0 + u) * slice + r);
-      ov[u] = __ldg(reinterpret_cast<const float4*>(part_o + ((s0 + u) * slice + r) * kHD) + lane);
+      const float4* row = reinterpret_cast<const float4*>(part_o + ((s0 + u) * slice + r) * kHD) + l * kMergeVecs;
+#pragma unroll
+      for (int c = 0; c < kMergeVecs; ++c) ov[u][c] = __ldg(row + c);
     }
   }
 }
 
 // Fold slices [s0, s0 + kMergeBatch) into the running merge (the sums run in slice order; with
 // at most kMergeBatch slices this is the plain LSE-weighted sum against the overall maximum).
-__device__ __forceinline__ void merge_apply(const float (&lv)[kMergeBatch], const float4 (&ov)[kMergeBatch], int s0,
-                                            int ns, MergeRow& st) {
+__device__ __forceinline__ void merge_apply(const float (&lv)[kMergeBatch], const float4 (&ov)[kMergeBatch][kMergeVecs],
+                                            int s0, int ns, MergeRow& st) {
   float mb = -INFINITY;
 #pragma unroll
   for (int u = 0; u < kMergeBatch; ++u)
@@ -787,30 +798,37 @@ __device__ __forceinline__ void merge_apply(const float (&lv)[kMergeBatch], cons
   if (st.m != -INFINITY && st.m != mn) {
     const float sc = __expf(st.m - mn);
     st.wsum *= sc;
-    st.acc.x *= sc;
-    st.acc.y *= sc;
-    st.acc.z *= sc;
-    st.acc.w *= sc;
+#pragma unroll
+    for (int i = 0; i < kMergeCols; ++i) st.acc[i] *= sc;
   }
 #pragma unroll
   for (int u = 0; u < kMergeBatch; ++u) {
     if (s0 + u < ns) {
       const float w = __expf(lv[u] - mn);
       st.wsum += w;
-      st.acc.x += w * ov[u].x;
-      st.acc.y += w * ov[u].y;
-      st.acc.z += w * ov[u].z;
-      st.acc.w += w * ov[u].w;
+#pragma unroll
+      for (int c = 0; c < kMergeVecs; ++c) {
+        st.acc[4 * c] += w * ov[u][c].x;
+        st.acc[4 * c + 1] += w * ov[u][c].y;
+        st.acc[4 * c + 2] += w * ov[u][c].z;
+        st.acc[4 * c + 3] += w * ov[u][c].w;
+      }
     }
   }
   st.m = mn;
 }
 
+// The lane's 8 columns of a merged row, scaled, as bf16 (one 16-byte store).
+__device__ __forceinline__ void merge_store_bf16(__nv_bfloat16* dst, int l, const float (&v)[kMergeCols], float sc) {
+  *reinterpret_cast<uint4*>(dst + l * kMergeCols) =
+      make_uint4(pack_bf16x2(v[0] * sc, v[1] * sc), pack_bf16x2(v[2] * sc, v[3] * sc),
+                 pack_bf16x2(v[4] * sc, v[5] * sc), pack_bf16x2(v[6] * sc, v[7] * sc));
+}
+
 // The merged row r = (b * H + h) * Lq + qrow written out (or folded into the ring accumulator).
-__device__ __forceinline__ void merge_finish(const AttnKParams& p, long long r, int b, int h, int qrow, int lane,
+__device__ __forceinline__ void merge_finish(const AttnKParams& p, long long r, int b, int h, int qrow, int l,
                                              const MergeRow& st) {
   const float m = st.m, wsum = st.wsum;
-  const float4 acc = st.acc;
   if (p.acc_o != nullptr) {
     // Ring step: the merged slices are this step's rows; fold them into the accumulator.
     const bool merge = (p.acc_mode & 1) != 0;
@@ -819,23 +837,29 @@ __device__ __forceinline__ void merge_finish(const AttnKParams& p, long long r, 
     const AccWeights aw = acc_weights(merge ? p.acc_lse[r] : -INFINITY, lse_b);
     const float cb = wsum > 0.f ? aw.wb / wsum : 0.f;
     float* arow = p.acc_o + ((static_cast<size_t>(b) * p.Lq + qrow) * p.H + h) * kHD;
-    float4 v = make_float4(acc.x * cb, acc.y * cb, acc.z * cb, acc.w * cb);
+    float v[kMergeCols];
+#pragma unroll
+    for (int i = 0; i < kMergeCols; ++i) v[i] = st.acc[i] * cb;
     if (aw.wa != 0.f) {
-      const float4 a4 = reinterpret_cast<const float4*>(arow)[lane];
-      v.x = fmaf(aw.wa, a4.x, v.x);
-      v.y = fmaf(aw.wa, a4.y, v.y);
-      v.z = fmaf(aw.wa, a4.z, v.z);
-      v.w = fmaf(aw.wa, a4.w, v.w);
+#pragma unroll
+      for (int c = 0; c < kMergeVecs; ++c) {
+        const float4 a4 = reinterpret_cast<const float4*>(arow)[l * kMergeVecs + c];
+        v[4 * c] = fmaf(aw.wa, a4.x, v[4 * c]);
+        v[4 * c + 1] = fmaf(aw.wa, a4.y, v[4 * c + 1]);
+        v[4 * c + 2] = fmaf(aw.wa, a4.z, v[4 * c + 2]);
+        v[4 * c + 3] = fmaf(aw.wa, a4.w, v[4 * c + 3]);
+      }
     }
     if (fin) {
       __nv_bfloat16* dst = p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg + (qrow % p.oi_seg) * p.oi_t +
                            h * p.oi_h;
-      *reinterpret_cast<uint2*>(dst + lane * 4) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
-      if (p.lse != nullptr && lane == 0) p.lse[r] = aw.lse;
+      merge_store_bf16(dst, l, v, 1.f);
+      if (p.lse != nullptr && l == 0) p.lse[r] = aw.lse;
     } else {
-      reinterpret_cast<float4*>(arow)[lane] = v;
-      __syncwarp();
-      if (lane == 0) p.acc_lse[r] = aw.lse;
+#pragma unroll
+      for (int c = 0; c < kMergeVecs; ++c)
+        reinterpret_cast<float4*>(arow)[l * kMergeVecs + c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      if (l == 0) p.acc_lse[r] = aw.lse;
     }
     return;
   }
@@ -847,33 +871,32 @@ __device__ __forceinline__ void merge_finish(const AttnKParams& p, long long r, 
                            ? p.out_img + b * p.oi_b + (qrow / p.oi_seg) * p.oi_sseg + (qrow % p.oi_seg) * p.oi_t +
                                  h * p.oi_h
                            : p.out_txt + b * p.ot_b + static_cast<long long>(qrow - p.Li) * p.ot_t + h * p.ot_h;
-  *reinterpret_cast<uint2*>(dst + lane * 4) =
-      make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
-  if (p.lse != nullptr && lane == 0) p.lse[r] = (wsum > 0.f && valid) ? (m + __logf(wsum)) : -INFINITY;
+  merge_store_bf16(dst, l, st.acc, inv);
+  if (p.lse != nullptr && l == 0) p.lse[r] = (wsum > 0.f && valid) ? (m + __logf(wsum)) : -INFINITY;
 }
 
-// One warp per query row: blockIdx.y = b * H + h, the block's 8 rows [8 blockIdx.x, + 8) lie
-// in one query pair (8 divides the pair's 256 rows), so a block of an unsplit pair (whose rows
+// 16 lanes per query row: blockIdx.y = b * H + h, the block's 16 rows [16 blockIdx.x, + 16) lie
+// in one query pair (16 divides the pair's 256 rows), so a block of an unsplit pair (whose rows
 // the attention kernel wrote itself) leaves at once.  No index division per row.
 __global__ void __launch_bounds__(256, 4) merge_splits_kernel(const AttnKParams p,
                                                           const __grid_constant__ UnitMap um) {
-  const int q_first = static_cast<int>(blockIdx.x) * 8;
+  const int q_first = static_cast<int>(blockIdx.x) * kMergeRowsPerBlock;
   const int ns = splits_of_pair(um, um.npairs - 1 - q_first / kPairRows);
   if (ns <= 1) return;
-  const int qrow = q_first + (threadIdx.x >> 5);
+  const int qrow = q_first + static_cast<int>(threadIdx.x) / kMergeLanes;
   if (qrow >= p.Lq) return;
-  const int lane = threadIdx.x & 31;
+  const int l = threadIdx.x & (kMergeLanes - 1);
   const int bh = static_cast<int>(blockIdx.y);
   const long long slice = static_cast<long long>(p.B) * p.H * p.Lq;
   const long long r = static_cast<long long>(bh) * p.Lq + qrow;
   float lv[kMergeBatch];
-  float4 ov[kMergeBatch];
+  float4 ov[kMergeBatch][kMergeVecs];
   MergeRow st;
   for (int s0 = 0; s0 < ns; s0 += kMergeBatch) {
-    merge_load(p.part_o, p.part_lse, slice, r, s0, ns, lane, lv, ov);
+    merge_load(p.part_o, p.part_lse, slice, r, s0, ns, l, lv, ov);
     merge_apply(lv, ov, s0, ns, st);
   }
-  merge_finish(p, r, bh / p.H, bh % p.H, qrow, lane, st);
+  merge_finish(p, r, bh / p.H, bh % p.H, qrow, l, st);
 }
 
 // Owner side of a partial scatter: one warp per (batch, head, row) of this rank's buffers, the
@@ -896,8 +919,8 @@ struct MergePartialsParams {
 __global__ void __launch_bounds__(256) merge_partials_kernel(const MergePartialsParams p) {
   const int R = p.rows + p.txt;
   const long long slice = static_cast<long long>(p.B) * p.H * R;  // elements between partial indices
-  const int lane = threadIdx.x & 31;
-  const int lr = static_cast<int>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int l = threadIdx.x & (kMergeLanes - 1);
+  const int lr = static_cast<int>(blockIdx.x) * kMergeRowsPerBlock + static_cast<int>(threadIdx.x) / kMergeLanes;
   if (lr < R) {
     const int bh = static_cast<int>(blockIdx.y);
     const int h = bh % p.H;
@@ -905,22 +928,20 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const MergePartials
     const long long r = static_cast<long long>(bh) * R + lr;
     // four partials at a time, each LSE loaded with its row (one round trip per four)
     float lv[kMergeBatch];
-    float4 ov[kMergeBatch];
+    float4 ov[kMergeBatch][kMergeVecs];
     MergeRow st;
     for (int s0 = 0; s0 < p.count; s0 += kMergeBatch) {
-      merge_load(p.o, p.lse, slice, r, s0, p.count, lane, lv, ov);
+      merge_load(p.o, p.lse, slice, r, s0, p.count, l, lv, ov);
       merge_apply(lv, ov, s0, p.count, st);
     }
     const float m = st.m, wsum = st.wsum;
-    const float4 acc = st.acc;
     const bool img = lr < p.rows;
     const bool valid = img || p.text_mask == nullptr || p.text_mask[b * p.tm_sb + (lr - p.rows)] != 0;
     const float inv = (wsum > 0.f && valid) ? 1.f / wsum : 0.f;
     __nv_bfloat16* dst = img ? p.out_img + b * p.oi_b + static_cast<long long>(lr) * p.oi_t + h * p.oi_h
                              : p.out_txt + b * p.ot_b + static_cast<long long>(lr - p.rows) * p.ot_t + h * p.ot_h;
-    *reinterpret_cast<uint2*>(dst + lane * 4) =
-        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
-    if (p.lse_out != nullptr && lane == 0) p.lse_out[r] = (wsum > 0.f && valid) ? m + __logf(wsum) : -INFINITY;
+    merge_store_bf16(dst, l, st.acc, inv);
+    if (p.lse_out != nullptr && l == 0) p.lse_out[r] = (wsum > 0.f && valid) ? m + __logf(wsum) : -INFINITY;
   }
 }
 
@@ -946,49 +967,9 @@ struct StageParams {
                       // fp16 holds every such bf16 value exactly in the range of K/V activations
 };
 
-// Eight consecutive values of one (batch, token, head) row as fp32: bf16 sources exactly,
-// quantised sources as code * scale (one fp32 multiply, as dequantize_kv does before its
-// single rounding).
-__device__ __forceinline__ void load_row8(const StageSeg& s, int b, int t, int h, int sub, float (&v)[8]) {
-  const int bb = s.bcast ? 0 : b;
-  if (s.rows != nullptr) t = __ldg(s.rows + t);
-  if (s.fmt == HYB_FMT_BF16) {
-    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(s.data) + bb * s.s_b + t * s.s_t +
-                               h * s.s_h + sub * 8;
-    const uint4 raw = *reinterpret_cast<const uint4*>(src);
-    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(p2[i]);
-      v[2 * i] = f.x;
-      v[2 * i + 1] = f.y;
-    }
-    return;
-  }
-  const float sc = s.scale[bb * s.c_b + t * s.c_t + h * s.c_h];
-  const uint8_t* src = static_cast<const uint8_t*>(s.data) + bb * s.s_b + t * s.s_t + h * s.s_h + sub * 8;
-  const uint2 raw = *reinterpret_cast<const uint2*>(src);
-  const uint8_t* by = reinterpret_cast<const uint8_t*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float a, c;
-    if (s.fmt == HYB_FMT_INT8) {
-      a = static_cast<float>(static_cast<int8_t>(by[2 * i]));
-      c = static_cast<float>(static_cast<int8_t>(by[2 * i + 1]));
-    } else {
-      const __nv_fp8x2_storage_t pair =
-          static_cast<__nv_fp8x2_storage_t>(by[2 * i] | (by[2 * i + 1] << 8));
-      const float2 f = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3)));
-      a = f.x;
-      c = f.y;
-    }
-    v[2 * i] = __fmul_rn(a, sc);
-    v[2 * i + 1] = __fmul_rn(c, sc);
-  }
-}
-
 // Sixteen consecutive values [16 lane8, 16 lane8 + 16) of one (batch, token, head) row as
-// fp32, by load_row8's rules (bf16 exactly; codes as code * scale, one fp32 multiply).  Codes
+// fp32: bf16 sources exactly, quantised sources as code * scale (one fp32 multiply, as
+// dequantize_kv does before its single rounding).  Codes
 // are read as two 8-byte loads: a quantised view guarantees 8-byte, not 16-byte, rows.
 __device__ __forceinline__ void load_row16(const StageSeg& s, int b, int t, int h, int lane8, float (&v)[16]) {
   const int bb = s.bcast ? 0 : b;
@@ -1086,7 +1067,7 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
 // Sequence-parallel K/V blocks -> one head-major bf16 K/V of the whole sequence.  Position
 // `pos` lies in chunk c ([bounds[c], bounds[c+1])), held by rank owner[c] at block row
 // row0[c] + (pos - bounds[c]).  A block is [K codes | V codes | K scales | V scales] for Lmax
-// rows of H heads (the ring message layout); decode as load_row8.
+// rows of H heads (the ring message layout); decode as load_row16.
 constexpr int kMaxGatherChunks = 128;
 struct GatherParams {
   int L, H, Lmax, fmt, nchunks;
@@ -1719,8 +1700,9 @@ int attn_core(const hyb_attn_args* a, cudaStream_t stream, long long kv_pitch = 
   int rc2 = launch_attn2(mq, mk, mv, kp, um, a->v_f16 != 0, stream);
   if (rc2 != HYB_OK || um.max_k <= 1 || kp.sc_o != nullptr) return rc2;  // owners merge scattered rows
   if (BH > 65535) return fail(HYB_ERR_UNSUPPORTED, "attention: %d (batch, head) pairs in one split launch", BH);
-  merge_splits_kernel<<<dim3(static_cast<unsigned>((kp.Lq + 7) / 8), static_cast<unsigned>(BH)), 256, 0, stream>>>(
-      kp, um);
+  merge_splits_kernel<<<dim3(static_cast<unsigned>((kp.Lq + kMergeRowsPerBlock - 1) / kMergeRowsPerBlock),
+                             static_cast<unsigned>(BH)),
+                        256, 0, stream>>>(kp, um);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
@@ -1787,8 +1769,9 @@ extern "C" int hyb_merge_partials(int32_t count, int32_t B, int32_t H, int32_t D
   p.lse_out = lse;
   if (static_cast<long long>(B) * H > 65535)
     return fail(HYB_ERR_UNSUPPORTED, "merge partials: %lld (batch, head) pairs", static_cast<long long>(B) * H);
-  merge_partials_kernel<<<dim3(static_cast<unsigned>((rows + txt_rows + 7) / 8), static_cast<unsigned>(B * H)), 256, 0,
-                          static_cast<cudaStream_t>(stream)>>>(p);
+  merge_partials_kernel<<<dim3(static_cast<unsigned>((rows + txt_rows + kMergeRowsPerBlock - 1) / kMergeRowsPerBlock),
+                               static_cast<unsigned>(B * H)),
+                          256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }
