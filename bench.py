@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--e2e-timeline", action="store_true",
                     help="after the measurement, one more pass of the end-to-end loop with CUDA events around "
                          "each upload / compute / read-back, and the host link alone; printed to stderr")
-    ap.add_argument("--ring-schedule", default="allgather", choices=["allgather", "ring"],
+    ap.add_argument("--ring-schedule", default="allgather", choices=["allgather", "allgather_overlap", "ring"],
                     help="ring workload: every block to every rank over peer memory, or neighbour passing")
     ap.add_argument("--library-comparison", action="store_true",
                     help="time this kernel and flashinfer's CUTLASS sm100a FMHA (fmha_varlen) on the same bf16 "
@@ -817,9 +817,12 @@ def ring_measurement(args, rank, world, device):
         "config": {"workload": "config 3: ring SP, 21 frames x 1560 tokens, frame-causal", "heads": H_TOTAL,
                    "head_dim": D, "seq_len": L, "tokens_per_frame": T, "layout": "zig-zag (2N chunks)",
                    "parallelism": f"ring_sp{world}" if world > 1 else "single",
-                   "schedule": (f"{sched}: " + ("every e4m3 block pushed to every rank over peer memory, one "
-                                                "attention launch" if sched == "allgather" else
-                                                "neighbour passing over NCCL send/recv, one launch per step")),
+                   "schedule": (f"{sched}: " + {
+                       "allgather": "every e4m3 block pushed to every rank over peer memory, one attention launch",
+                       "allgather_overlap": "every e4m3 block pushed to every rank over peer memory on a side "
+                                            "stream while the own-block launch runs, then the other ranks' keys "
+                                            "in up to two launches merged through the fp32 accumulator",
+                       "ring": "neighbour passing over NCCL send/recv, one launch per step"}[sched]),
                    "timed_call": "eager" if args.no_graph else "CUDA graph replay of one ring call",
                    "kv_block": "fp8_e4m3 codes + fp32 per-(token, head) scales, quantised each step",
                    "l2": "inputs larger than L2 (201 MB bf16 per tensor over the job)",

@@ -126,6 +126,8 @@ SIGNATURES = {
     "hyb_peer_alloc": (c_i32, [c_i64, ctypes.POINTER(c_ptr), c_ptr]),
     "hyb_peer_push_bytes": (c_i32, [c_i32, c_i32, c_ptr, c_i64, ctypes.POINTER(c_ptr), ctypes.POINTER(PeerSync),
                                     c_ptr]),
+    "hyb_peer_push_bytes_n": (c_i32, [c_i32, c_i32, c_ptr, c_i64, ctypes.POINTER(c_ptr), ctypes.POINTER(PeerSync),
+                                      c_i32, c_ptr]),
     "hyb_ring_gather_stage": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(c_ptr), c_i32,
                                       ctypes.POINTER(c_i32), ctypes.POINTER(c_i32), ctypes.POINTER(c_i32),
                                       c_ptr, c_ptr, c_i32, c_ptr]),

@@ -335,15 +335,33 @@ struct PushBytesParams {
 
 // The same bytes to every rank (an all-gather contribution); destinations whose pointer is the
 // source itself are skipped.
+// Eight 16-byte chunks per thread and iteration, all loaded before any store, so that a grid
+// of a few blocks (the overlapped ring schedule leaves the other SMs to an attention launch)
+// still keeps enough bytes in flight to fill the links.
+constexpr int kPushUnroll = 8;
 __global__ void __launch_bounds__(256) push_bytes_kernel(const PushBytesParams p) {
   const long long total = p.chunks16 * p.P;
-  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < total;
-       c += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int k = static_cast<int>(c / p.chunks16);
-    const long long i = c - k * p.chunks16;
-    const int d = (p.rank + 1 + k) % p.P;
-    if (p.dst[d] == p.src) continue;
-    p.dst[d][i] = p.src[i];
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long c0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c0 < total;
+       c0 += stride * kPushUnroll) {
+    uint4 v[kPushUnroll];
+#pragma unroll
+    for (int u = 0; u < kPushUnroll; ++u) {
+      const long long c = c0 + u * stride;
+      if (c < total) {
+        const int k = static_cast<int>(c / p.chunks16);
+        v[u] = p.src[c - k * p.chunks16];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kPushUnroll; ++u) {
+      const long long c = c0 + u * stride;
+      if (c < total) {
+        const int k = static_cast<int>(c / p.chunks16);
+        const int d = (p.rank + 1 + k) % p.P;
+        if (p.dst[d] != p.src) p.dst[d][c - k * p.chunks16] = v[u];
+      }
+    }
   }
   grid_signal_and_wait(p.sync);
 }
@@ -595,8 +613,16 @@ extern "C" int hyb_peer_barrier(int32_t P, int32_t rank, const hyb_peer_sync* sy
   return HYB_OK;
 }
 
+extern "C" int hyb_peer_push_bytes_n(int32_t P, int32_t rank, const void* src, int64_t bytes, void* const* dst,
+                                     const hyb_peer_sync* sync, int32_t max_blocks, void* stream);
+
 extern "C" int hyb_peer_push_bytes(int32_t P, int32_t rank, const void* src, int64_t bytes, void* const* dst,
                                    const hyb_peer_sync* sync, void* stream) {
+  return hyb_peer_push_bytes_n(P, rank, src, bytes, dst, sync, 0, stream);
+}
+
+extern "C" int hyb_peer_push_bytes_n(int32_t P, int32_t rank, const void* src, int64_t bytes, void* const* dst,
+                                     const hyb_peer_sync* sync, int32_t max_blocks, void* stream) {
   if (P <= 1 || P > kMaxRanks || rank < 0 || rank >= P || bytes < 0 || (bytes % 16) != 0 || dst == nullptr ||
       (bytes > 0 && !al16(src)))
     return fail(HYB_ERR_INVALID_ARG, "peer push: bad arguments (16-byte multiples, 2..%d ranks)", kMaxRanks);
@@ -612,7 +638,9 @@ extern "C" int hyb_peer_push_bytes(int32_t P, int32_t rank, const void* src, int
   int rc = peer_sync_of(sync, P, rank, &p.sync);
   if (rc != HYB_OK) return rc;
   const long long total = p.chunks16 * P;
-  push_bytes_kernel<<<grid_for(total > 0 ? total : 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  int blocks = grid_for(total > 0 ? total : 1, 256);
+  if (max_blocks > 0 && blocks > max_blocks) blocks = max_blocks;
+  push_bytes_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   HYB_CHECK_LAUNCH();
   return HYB_OK;
 }

@@ -311,7 +311,7 @@ class GatherAttention:
 
     def __init__(self, plan: RingPlan, rank: int, heads: int, device, *, tokens_per_frame: int,
                  causal_frames: int = 1, kv_format: str = "fp8_e4m3", softmax_scale: float | None = None,
-                 group=None, shared=None):
+                 group=None, shared=None, overlap: bool = False, push_blocks: int = 24):
         self.plan, self.rank, self.H, self.device = plan, rank, heads, torch.device(device)
         self.G = int(causal_frames) * int(tokens_per_frame)
         self.scale = float(softmax_scale) if softmax_scale else 0.0
@@ -361,6 +361,143 @@ class GatherAttention:
         self.status = _lib.device_status(dev)
         self.launches = 0
         self.event_log = None
+        self.overlap = bool(overlap) and P > 1
+        self.push_blocks = int(push_blocks)
+        if self.overlap:
+            self._setup_overlap()
+
+    # ------------------------------------------------------------ overlapped schedule
+    # The rank attends its own keys while its block crosses NVLink: the push runs on a side
+    # stream on `push_blocks` blocks, the own-block launch on the other SMs; the other ranks'
+    # keys, decoded once the push barrier has passed, follow in at most two launches (the
+    # chunks before the rank's last chunk, two position segments under zig-zag sharding, then
+    # those after it, whose keys only the rows of the same frame group see).  The launches
+    # merge through the fp32 accumulator (acc_mode); only the last writes the bf16 output.
+    def _chunk_table(self, chunks):
+        n = len(chunks)
+        starts, off = [], 0
+        for c in chunks:
+            starts.append(off)
+            off += c[1]
+        bounds = (ctypes.c_int32 * (n + 1))(*(starts + [off]))
+        owner = (ctypes.c_int32 * max(n, 1))(*[c[2] for c in chunks])
+        row0 = (ctypes.c_int32 * max(n, 1))(*[c[3] for c in chunks])
+        return n, off, bounds, owner, row0
+
+    @staticmethod
+    def _segments(chunks):
+        segs = []
+        for pos, n, _, _ in chunks:
+            if segs and segs[-1][0] + segs[-1][1] == pos:
+                segs[-1] = (segs[-1][0], segs[-1][1] + n)
+            else:
+                segs.append((pos, n))
+        return segs
+
+    def _setup_overlap(self) -> None:
+        plan, r, H, dev = self.plan, self.rank, self.H, self.device
+        mine = [c for c in plan.gather_chunks() if c[2] == r]
+        others = [c for c in plan.gather_chunks() if c[2] != r]
+        own_end = max(c[0] + c[1] for c in mine) if mine else 0
+        groups = [[c for c in others if c[0] < own_end], [c for c in others if c[0] >= own_end]]
+        self.own_tab = self._chunk_table(mine)
+        self.own_segs = self._segments(mine)
+        Ls = self.Ls
+        self.kv_own = torch.empty((2, H * max(Ls, 1) * _D), dtype=torch.bfloat16, device=dev)
+        self.parts = []   # (gather table, head-major K/V buffer, keys, position segments)
+        for g in groups:
+            n = sum(c[1] for c in g)
+            if n:
+                segs = self._segments(g)
+                if len(segs) > 2:
+                    raise RuntimeError("overlapped ring schedule: more than two key segments in one launch")
+                buf = torch.empty((2, H * n * _D), dtype=torch.bfloat16, device=dev)
+                self.parts.append((self._chunk_table(g), buf, n, segs))
+        self.acc = torch.empty((max(Ls, 1), H, _D), dtype=torch.float32, device=dev)
+        self.acc_lse = torch.empty((H, max(Ls, 1)), dtype=torch.float32, device=dev)
+        self.ov_bits, splits = {}, 1
+        with torch.cuda.device(dev):
+            stream = _lib.stream_ptr(dev)
+            for Lk in [Ls] + [n for _, _, n, _ in self.parts]:
+                kw = ((Lk + 127) // 128) * 4
+                if Lk not in self.ov_bits:
+                    t = torch.empty(max(kw, 4), dtype=torch.int32, device=dev)
+                    _lib.check(self.lib.hyb_fill_key_bits(1, Lk, kw, t.data_ptr(), stream), "key bits")
+                    self.ov_bits[Lk] = (t, kw)
+                lay = _lib.WorkspaceLayout()
+                _lib.check(self.lib.hyb_cached_attention_workspace_layout(1, H, _D, Lk - min(Lk, Ls), max(Ls, 1), 0,
+                                                                          0, ctypes.byref(lay)), "ring layout")
+                splits = max(splits, lay.kv_splits)
+        self.ov_splits = splits
+        self.ov_part_o = torch.empty((splits * H * max(Ls, 1) * _D,), dtype=torch.float32, device=dev) \
+            if splits > 1 else None
+        self.ov_part_lse = torch.empty((splits * H * max(Ls, 1),), dtype=torch.float32, device=dev) \
+            if splits > 1 else None
+        self.side = torch.cuda.Stream(device=dev)
+
+    def _gather(self, tab, dst, stream: int) -> None:
+        n, L, bounds, owner, row0 = tab
+        if L == 0:
+            return
+        _lib.check(self.lib.hyb_ring_gather_stage(self.plan.world, self.code_fmt, L, self.H, _D, self.Lmax,
+                                                  self.block_tab, n, bounds, owner, row0, dst[0].data_ptr(),
+                                                  dst[1].data_ptr(), 1, stream), "ring gather stage")
+        self.launches += 1
+
+    def _launch(self, k_ptr, v_ptr, Lk, segs, mode, out, lse, stream: int) -> None:
+        plan, H, Ls = self.plan, self.H, self.Ls
+        a = _lib.AttnArgs()
+        a.abi_version = _lib.HYB_ABI_VERSION
+        a.B, a.H, a.D, a.Lq, a.Lk = 1, H, _D, Ls, Lk
+        a.hist_len, a.img_len, a.img_k_len = 0, Ls, Lk
+        a.group_tokens = self.G
+        a.softmax_scale = self.scale
+        a.q_seg, a.q_pos0, a.q_pos1 = plan.positions(self.rank)
+        if len(segs) == 1:
+            a.k_seg, a.k_pos0, a.k_pos1 = 0, segs[0][0], 0
+        else:
+            a.k_seg, a.k_pos0, a.k_pos1 = segs[0][1], segs[0][0], segs[1][0]
+        a.q, a.k, a.v = self.qh.data_ptr(), k_ptr, v_ptr
+        bits, kw = self.ov_bits[Lk]
+        a.kbits, a.kwords = bits.data_ptr(), kw
+        a.qbits, a.qwords = None, 0
+        a.out_img = out.data_ptr()
+        a.oi_sb, a.oi_st, a.oi_sh = out.stride(0), out.stride(1), out.stride(2)
+        a.oi_seg, a.oi_sseg = Ls, 0
+        a.lse = lse.data_ptr() if lse is not None else None
+        a.dev_status = self.status.data_ptr()
+        a.kv_splits = self.ov_splits
+        a.v_f16 = 1
+        if self.ov_splits > 1:
+            a.part_o, a.part_lse = self.ov_part_o.data_ptr(), self.ov_part_lse.data_ptr()
+        a.acc_o, a.acc_lse, a.acc_mode = self.acc.data_ptr(), self.acc_lse.data_ptr(), mode
+        if self.event_log is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record(torch.cuda.current_stream(self.device))
+        _lib.check(self.lib.hyb_attn_fwd(ctypes.byref(a), stream), "ring attention (overlapped)")
+        if self.event_log is not None:
+            ev[1].record(torch.cuda.current_stream(self.device))
+            self.event_log.append(ev)   # the launches of one call add up to its attention time
+        self.launches += 2 if self.ov_splits > 1 else 1
+
+    def attend_own(self, q, out, lse, stream: int) -> None:
+        """Q staged head-major, the own block decoded, and its launch (first of the merge)."""
+        H, Ls = self.H, self.Ls
+        qv = _lib.bf16_view(q)
+        _lib.check(self.lib.hyb_stage_head_major(1, Ls, H, _D, ctypes.byref(qv), None, self.qh.data_ptr(), None,
+                                                 stream), "ring stage q")
+        self.launches += 1
+        self._gather(self.own_tab, self.kv_own, stream)
+        last = not self.parts
+        self._launch(self.kv_own[0].data_ptr(), self.kv_own[1].data_ptr(), Ls, self.own_segs, 2 if last else 0,
+                     out, lse, stream)
+
+    def attend_others(self, out, lse, stream: int) -> None:
+        """The other ranks' keys (after the push barrier): per part a decode and a launch."""
+        for i, (tab, buf, n, segs) in enumerate(self.parts):
+            self._gather(tab, buf, stream)
+            mode = 1 | (2 if i == len(self.parts) - 1 else 0)
+            self._launch(buf[0].data_ptr(), buf[1].data_ptr(), n, segs, mode, out, lse, stream)
 
     def fill_own(self, k, v) -> None:
         self.slots[self.rank].fill(k, v)
@@ -432,8 +569,30 @@ class GatherAttention:
             cs = _lib.stream_ptr(dev)
             self.fill_own(k, v)
             self.launches += 1
-            self.exchange(cs)
-            self.attend(q, out, lse, cs)
+            if not self.overlap:
+                self.exchange(cs)
+                self.attend(q, out, lse, cs)
+                return out
+            # Side stream: the entry barrier and the push, after everything this stream did
+            # before (the previous call's decodes of the peers' blocks included).
+            compute = torch.cuda.current_stream(dev)
+            filled = torch.cuda.Event()
+            filled.record(compute)
+            pushed = torch.cuda.Event()
+            with torch.cuda.stream(self.side):
+                self.side.wait_event(filled)
+                ss = self.side.cuda_stream
+                _lib.check(self.lib.hyb_peer_barrier(self.plan.world, self.rank, ctypes.byref(self.peers.sync), ss),
+                           "ring block barrier")
+                _lib.check(self.lib.hyb_peer_push_bytes_n(self.plan.world, self.rank,
+                                                          self.slots[self.rank].buf.data_ptr(), self.block_bytes,
+                                                          self._push_dst, ctypes.byref(self.peers.sync),
+                                                          self.push_blocks, ss), "ring block push")
+                pushed.record(self.side)
+            self.launches += 2
+            self.attend_own(q, out, lse, cs)
+            compute.wait_event(pushed)
+            self.attend_others(out, lse, cs)
         return out
 
     def close(self) -> None:
@@ -445,7 +604,7 @@ class GatherAttention:
 _PLANS: dict = {}
 
 
-SCHEDULES = ("allgather", "ring")
+SCHEDULES = ("allgather", "allgather_overlap", "ring")
 
 
 def ring_attention(q, k, v, group=None, *, seq_len: int, tokens_per_frame: int, causal_frames: int = 1,
@@ -479,8 +638,9 @@ def ring_plan_state(q, *, seq_len, world, rank, tokens_per_frame, causal_frames=
         plan = RingPlan(seq_len, P, layout)
         kw = dict(tokens_per_frame=tokens_per_frame, causal_frames=causal_frames, kv_format=kv_format,
                   softmax_scale=softmax_scale)
-        if schedule == "allgather":
-            ra = GatherAttention(plan, r, q.shape[2], q.device, group=group, **kw)
+        if schedule in ("allgather", "allgather_overlap"):
+            ra = GatherAttention(plan, r, q.shape[2], q.device, group=group, overlap=schedule == "allgather_overlap",
+                                 **kw)
         else:
             ra = RingAttention(plan, r, q.shape[2], q.device, **kw)
         _PLANS[key] = ra
@@ -501,9 +661,10 @@ def ring_attention_emulated(q, k, v, world: int, *, tokens_per_frame: int, causa
     """``world`` emulated ranks in one process on one GPU: q/k/v are the full sequence
     [1, L, H, 128]; the same kernels, in the same order, as ``ring_attention`` with the given
     schedule.  Returns the full output."""
-    if schedule == "allgather":
+    if schedule in ("allgather", "allgather_overlap"):
         return _gather_emulated(q, k, v, world, tokens_per_frame=tokens_per_frame, causal_frames=causal_frames,
-                                kv_format=kv_format, layout=layout, softmax_scale=softmax_scale)
+                                kv_format=kv_format, layout=layout, softmax_scale=softmax_scale,
+                                overlap=schedule == "allgather_overlap")
     plan = RingPlan(q.shape[1], world, layout)
     H, dev = q.shape[2], q.device
     rings = [RingAttention(plan, r, H, dev, tokens_per_frame=tokens_per_frame, causal_frames=causal_frames,
@@ -535,7 +696,8 @@ def ring_attention_emulated(q, k, v, world: int, *, tokens_per_frame: int, causa
     return plan.unshard(outs)
 
 
-def _gather_emulated(q, k, v, world, *, tokens_per_frame, causal_frames, kv_format, layout, softmax_scale):
+def _gather_emulated(q, k, v, world, *, tokens_per_frame, causal_frames, kv_format, layout, softmax_scale,
+                     overlap=False):
     plan = RingPlan(q.shape[1], world, layout)
     H, dev = q.shape[2], q.device
     kw = dict(tokens_per_frame=tokens_per_frame, causal_frames=causal_frames, kv_format=kv_format,
@@ -543,6 +705,10 @@ def _gather_emulated(q, k, v, world, *, tokens_per_frame, causal_frames, kv_form
     block_bytes = ((2 * (plan.max_length() * H * _D + plan.max_length() * H * 4)) + 15) // 16 * 16
     shared = torch.empty(world * block_bytes, dtype=torch.uint8, device=dev)
     states = [GatherAttention(plan, r, H, dev, shared=shared, **kw) for r in range(world)]
+    if overlap and world > 1:
+        for st in states:   # the overlapped launches over the shared buffer (no push)
+            st.overlap = True
+            st._setup_overlap()
     for r, st in enumerate(states):
         if plan.length(r):
             st.fill_own(plan.shard(k, r).contiguous(), plan.shard(v, r).contiguous())
@@ -553,6 +719,10 @@ def _gather_emulated(q, k, v, world, *, tokens_per_frame, causal_frames, kv_form
             o = torch.empty((1, plan.length(r), H, _D), dtype=torch.bfloat16, device=dev)
             if plan.length(r):
                 qs = plan.shard(q, r).contiguous()
-                st.attend(qs, o, None, cs)
+                if st.overlap:
+                    st.attend_own(qs, o, None, cs)
+                    st.attend_others(o, None, cs)
+                else:
+                    st.attend(qs, o, None, cs)
             outs.append(o)
     return plan.unshard(outs)

@@ -361,6 +361,11 @@ int hyb_peer_barrier(int32_t P, int32_t rank, const hyb_peer_sync* sync, void* s
  * dynamic_ring_attention.py:45-83). */
 int hyb_peer_push_bytes(int32_t P, int32_t rank, const void* src, int64_t bytes, void* const* dst,
                         const hyb_peer_sync* sync, void* stream);
+/* The same on at most max_blocks blocks of 256 threads (<= 0: as many as the bytes need), so
+ * that a kernel on another stream (the own-block attention of the overlapped ring schedule)
+ * runs on the other SMs while the push crosses NVLink. */
+int hyb_peer_push_bytes_n(int32_t P, int32_t rank, const void* src, int64_t bytes, void* const* dst,
+                          const hyb_peer_sync* sync, int32_t max_blocks, void* stream);
 
 /* Ulysses send-side pack (sequence -> heads): q, k, v bf16 [B, Ls, H, D] -> send buffer
  * [P, Ls_max, nsrc*B, H/P, D] (the all_to_all_qkv layout, padding rows zeroed).

@@ -111,7 +111,8 @@ def main():
     inputs = [tuple(seeded_kv((1, Lr, 4, D), make_generator(77 + 10 * c + i)).to(dev) for i in range(3))
               for c in range(2)]
     for schedule, layout in (("ring", "zigzag"), ("ring", "contiguous"), ("allgather", "zigzag"),
-                             ("allgather", "contiguous")):
+                             ("allgather", "contiguous"), ("allgather_overlap", "zigzag"),
+                             ("allgather_overlap", "contiguous")):
         plan = ring.RingPlan(Lr, world, layout)
         emus = [ring.ring_attention_emulated(*x, world, tokens_per_frame=Tr, layout=layout, schedule=schedule)
                 for x in inputs]

@@ -109,7 +109,7 @@ def test_lse_merge_kernel_matches_oracle(cuda_lib):
     torch.testing.assert_close(acc.cpu().double(), torch.from_numpy(g["out"])[0], rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("schedule", ["ring", "allgather"])
+@pytest.mark.parametrize("schedule", ["ring", "allgather", "allgather_overlap"])
 @pytest.mark.parametrize("P,frames,T,layout", [(1, 5, 64, "zigzag"), (4, 21, 48, "zigzag"),
                                                (3, 7, 100, "zigzag"), (3, 7, 100, "contiguous"),
                                                (8, 21, 39, "zigzag")])

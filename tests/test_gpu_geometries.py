@@ -43,8 +43,8 @@ def decoded(x):
     return oq.dequantize(*oq.quantize_e4m3(x.cpu()))
 
 
-@pytest.mark.parametrize("world", [1, 8])
-def test_config3_ring_geometry(cuda_lib, world):
+@pytest.mark.parametrize("world,schedule", [(1, "allgather"), (8, "allgather"), (8, "allgather_overlap")])
+def test_config3_ring_geometry(cuda_lib, world, schedule):
     dev = torch.device("cuda")
     H, L = 2, 21 * T
     gen = make_generator(3003)
@@ -52,14 +52,14 @@ def test_config3_ring_geometry(cuda_lib, world):
     if world == 1:
         out = ring.ring_attention(q, k, v, None, seq_len=L, tokens_per_frame=T)
     else:
-        out = ring.ring_attention_emulated(q, k, v, world, tokens_per_frame=T, schedule="allgather")
+        out = ring.ring_attention_emulated(q, k, v, world, tokens_per_frame=T, schedule=schedule)
     torch.cuda.synchronize()
     _lib.check_device_status(dev)
     kd, vd = decoded(k).to(dev), decoded(v).to(dev)
     frame = torch.arange(L, device=dev) // T
     for h in range(H):
         ref = exact(q[0, :, h], kd[0, :, h], vd[0, :, h], lambda r: frame[None, :] <= frame[r][:, None])
-        check_bf16(out[0, :, h], ref, f"config 3 ring, {world} rank(s), head {h}")
+        check_bf16(out[0, :, h], ref, f"config 3 ring ({schedule}), {world} rank(s), head {h}")
 
 
 def test_config4_geometry(cuda_lib):
