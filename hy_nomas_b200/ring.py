@@ -342,7 +342,10 @@ class GatherAttention:
         self.owner = (ctypes.c_int32 * self.nchunks)(*[c[2] for c in chunks])
         self.row0 = (ctypes.c_int32 * self.nchunks)(*[c[3] for c in chunks])
         self.block_tab = (ctypes.c_void_p * P)(*[base + r * self.block_bytes for r in range(P)])
-        self.kv = torch.empty((2, H * max(L, 1) * _D), dtype=torch.bfloat16, device=dev)
+        self.overlap = bool(overlap) and P > 1
+        # the single-launch schedule's head-major K/V of the whole sequence (the overlapped one
+        # decodes into per-launch buffers instead)
+        self.kv = None if self.overlap else torch.empty((2, H * max(L, 1) * _D), dtype=torch.bfloat16, device=dev)
         Ls = plan.length(rank)
         self.Ls = Ls
         self.qh = torch.empty((H * max(Ls, 1) * _D,), dtype=torch.bfloat16, device=dev)
@@ -354,14 +357,14 @@ class GatherAttention:
             _lib.check(lib.hyb_cached_attention_workspace_layout(1, H, _D, L - Ls, max(Ls, 1), 0, 0, ctypes.byref(lay)),
                        "gather layout")
         self.kv_splits = max(1, lay.kv_splits)
+        single = self.kv_splits > 1 and not self.overlap
         self.part_o = torch.empty((self.kv_splits * H * max(Ls, 1) * _D,), dtype=torch.float32, device=dev) \
-            if self.kv_splits > 1 else None
+            if single else None
         self.part_lse = torch.empty((self.kv_splits * H * max(Ls, 1),), dtype=torch.float32, device=dev) \
-            if self.kv_splits > 1 else None
+            if single else None
         self.status = _lib.device_status(dev)
         self.launches = 0
         self.event_log = None
-        self.overlap = bool(overlap) and P > 1
         self.push_blocks = int(push_blocks)
         if self.overlap:
             self._setup_overlap()
@@ -704,11 +707,8 @@ def _gather_emulated(q, k, v, world, *, tokens_per_frame, causal_frames, kv_form
               softmax_scale=softmax_scale)
     block_bytes = ((2 * (plan.max_length() * H * _D + plan.max_length() * H * 4)) + 15) // 16 * 16
     shared = torch.empty(world * block_bytes, dtype=torch.uint8, device=dev)
-    states = [GatherAttention(plan, r, H, dev, shared=shared, **kw) for r in range(world)]
-    if overlap and world > 1:
-        for st in states:   # the overlapped launches over the shared buffer (no push)
-            st.overlap = True
-            st._setup_overlap()
+    # with overlap, the overlapped launches over the shared buffer (no push)
+    states = [GatherAttention(plan, r, H, dev, shared=shared, overlap=overlap, **kw) for r in range(world)]
     for r, st in enumerate(states):
         if plan.length(r):
             st.fill_own(plan.shard(k, r).contiguous(), plan.shard(v, r).contiguous())
