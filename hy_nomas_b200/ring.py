@@ -296,6 +296,34 @@ def _u8_tensor(ptr: int, nbytes: int, device) -> torch.Tensor:
     return torch.as_tensor(_DeviceArray(ptr, (nbytes,), "|u1"), device=device)
 
 
+def position_segments(chunks):
+    """Maximal runs of consecutive positions of (position, length, owner, row) chunks given in
+    position order: the key position segments of one launch."""
+    segs = []
+    for pos, n, _, _ in chunks:
+        if segs and segs[-1][0] + segs[-1][1] == pos:
+            segs[-1] = (segs[-1][0], segs[-1][1] + n)
+        else:
+            segs.append((pos, n))
+    return segs
+
+
+def overlap_groups(plan: RingPlan, rank: int):
+    """Chunks of the overlapped all-gather schedule for ``rank``: its own chunks, and the other
+    ranks' non-empty chunk groups, one launch each: those before the end of the rank's last
+    chunk (at most two position segments under either layout: the ranges before and between
+    the rank's chunks), then those after it (one segment)."""
+    chunks = plan.gather_chunks()
+    mine = [c for c in chunks if c[2] == rank]
+    others = [c for c in chunks if c[2] != rank]
+    own_end = max(c[0] + c[1] for c in mine) if mine else 0
+    groups = [g for g in ([c for c in others if c[0] < own_end], [c for c in others if c[0] >= own_end]) if g]
+    for g in groups:
+        if len(position_segments(g)) > 2:
+            raise RuntimeError("overlapped ring schedule: more than two key segments in one launch")
+    return mine, groups
+
+
 class GatherAttention:
     """The all-gather schedule of ring attention for a switched fabric.  Every rank quantises
     its K/V into its slot of a block buffer that every rank maps (CUDA IPC), pushes the block
@@ -387,35 +415,18 @@ class GatherAttention:
         row0 = (ctypes.c_int32 * max(n, 1))(*[c[3] for c in chunks])
         return n, off, bounds, owner, row0
 
-    @staticmethod
-    def _segments(chunks):
-        segs = []
-        for pos, n, _, _ in chunks:
-            if segs and segs[-1][0] + segs[-1][1] == pos:
-                segs[-1] = (segs[-1][0], segs[-1][1] + n)
-            else:
-                segs.append((pos, n))
-        return segs
-
     def _setup_overlap(self) -> None:
-        plan, r, H, dev = self.plan, self.rank, self.H, self.device
-        mine = [c for c in plan.gather_chunks() if c[2] == r]
-        others = [c for c in plan.gather_chunks() if c[2] != r]
-        own_end = max(c[0] + c[1] for c in mine) if mine else 0
-        groups = [[c for c in others if c[0] < own_end], [c for c in others if c[0] >= own_end]]
+        H, dev = self.H, self.device
+        mine, groups = overlap_groups(self.plan, self.rank)
         self.own_tab = self._chunk_table(mine)
-        self.own_segs = self._segments(mine)
+        self.own_segs = position_segments(mine)
         Ls = self.Ls
         self.kv_own = torch.empty((2, H * max(Ls, 1) * _D), dtype=torch.bfloat16, device=dev)
         self.parts = []   # (gather table, head-major K/V buffer, keys, position segments)
         for g in groups:
             n = sum(c[1] for c in g)
-            if n:
-                segs = self._segments(g)
-                if len(segs) > 2:
-                    raise RuntimeError("overlapped ring schedule: more than two key segments in one launch")
-                buf = torch.empty((2, H * n * _D), dtype=torch.bfloat16, device=dev)
-                self.parts.append((self._chunk_table(g), buf, n, segs))
+            buf = torch.empty((2, H * n * _D), dtype=torch.bfloat16, device=dev)
+            self.parts.append((self._chunk_table(g), buf, n, position_segments(g)))
         self.acc = torch.empty((max(Ls, 1), H, _D), dtype=torch.float32, device=dev)
         self.acc_lse = torch.empty((H, max(Ls, 1)), dtype=torch.float32, device=dev)
         self.ov_bits, splits = {}, 1

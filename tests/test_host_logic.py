@@ -374,3 +374,21 @@ def test_decoded_mirrors_are_for_quantised_caches_only():
     mk, mv, pitch = win.view()["staged"]
     assert pitch == 3 * 16 + 8 and tuple(mk.shape) == (1, 2, pitch, 128)
     assert mk.dtype == torch.bfloat16 and mv.dtype == torch.float16
+
+
+@pytest.mark.parametrize("layout", ["zigzag", "contiguous"])
+@pytest.mark.parametrize("world,L", [(2, 32760), (4, 32760), (8, 32760), (3, 1000), (8, 300)])
+def test_overlapped_ring_groups_cover_every_other_chunk(layout, world, L):
+    """The overlapped ring schedule attends each rank's own chunks, then the other ranks' chunks
+    in at most two launches of at most two position segments each; together they are every
+    chunk of the sequence exactly once."""
+    from hy_nomas_b200.ring import RingPlan, overlap_groups, position_segments
+    plan = RingPlan(L, world, layout)
+    for r in range(world):
+        mine, groups = overlap_groups(plan, r)
+        assert len(groups) <= 2 and all(len(position_segments(g)) <= 2 for g in groups)
+        seen = sorted(c for g in [mine] + groups for c in g)
+        assert seen == plan.gather_chunks()
+        assert sum(c[1] for c in mine) == plan.length(r)
+        for g in groups:
+            assert g == sorted(g) and all(c[2] != r for c in g)
